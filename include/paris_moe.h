@@ -1,0 +1,112 @@
+/*
+ * paris_moe.h -- C ABI of the B200 (sm_100a) Qwen3.5-35B-A3B sparse-MoE block.
+ *
+ * Plain pointers and sizes only: bf16 tensors are `uint16_t` bit patterns in
+ * device memory, row-major; streams are `cudaStream_t` passed as `void*`.
+ * Every entry point is asynchronous on the given stream, never synchronises
+ * the host, allocates nothing, and returns a status (`PMOE_OK` = 0, negative
+ * on error; see `pmoe_status_string`).
+ *
+ * Shapes (Qwen3.5-35B-A3B: H=2048, E=256, K=8, I=512, Is=512):
+ *   x          [T, H]       hidden states
+ *   w_router   [E, H]       gate.weight
+ *   w_gate_up  [E, 2I, H]   experts.gate_up_proj (rows [0,I) gate, [I,2I) up)
+ *   w_down     [E, H, I]    experts.down_proj
+ *   w_sh_gate  [Is, H]      shared_expert.gate_proj.weight
+ *   w_sh_up    [Is, H]      shared_expert.up_proj.weight
+ *   w_sh_down  [H, Is]      shared_expert.down_proj.weight
+ *   w_sh_gvec  [1, H]       shared_expert_gate.weight
+ * These are the HF module's own tensors (transformers
+ * models/qwen3_5_moe/modeling_qwen3_5_moe.py:713-792), used in place.
+ */
+#ifndef PARIS_MOE_H_
+#define PARIS_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  PMOE_OK = 0,
+  PMOE_ERR_ARG = -1,        /* bad shape, pointer or flag */
+  PMOE_ERR_ALIGN = -2,      /* a tensor is not 16-byte aligned */
+  PMOE_ERR_WORKSPACE = -3,  /* workspace too small */
+  PMOE_ERR_CUDA = -4,       /* a CUDA runtime call failed (launch, copy) */
+  PMOE_ERR_UNSUPPORTED = -5,/* shape outside what the kernels implement */
+  PMOE_ERR_PEER_TIMEOUT = -6,/* a bounded wait on a peer GPU ran out */
+  PMOE_ERR_DEVICE = -7      /* not an sm_100 device */
+};
+
+/* Flags of pmoe_block_forward. */
+enum {
+  PMOE_F_SHARED = 1,        /* add sigmoid(x.w_sh_gvec) * shared_expert(x) */
+  PMOE_F_ROUTED = 2,        /* add the routed experts in [expert_lo, expert_hi) */
+  PMOE_F_FORCE_STREAM = 4,  /* weight-streaming kernels at any T (testing) */
+  PMOE_F_FORCE_TC = 8       /* tcgen05 grouped GEMMs at any T (testing) */
+};
+
+/* Human-readable name of a status code. */
+const char* pmoe_status_string(int status);
+
+/* Library version string ("paris_moe <semver> sm_100a"). */
+const char* pmoe_version(void);
+
+/* Bytes of device workspace pmoe_route / pmoe_block_forward need for this
+ * shape.  The workspace holds the router partials, routing, CSR dispatch,
+ * the SiLU*up intermediate and the weighted expert rows.  Replaces the
+ * per-call temporaries of engine/kernels/moe_grouped_mlp.py:115-163 and
+ * engine/kernels/moe_dispatch.py:119-137. */
+int pmoe_workspace_size(int T, int H, int E, int K, int I, int Is, size_t* bytes);
+
+/* Router + top-k + dispatch only.
+ * Replaces Qwen3_5MoeTopKRouter.forward (modeling_qwen3_5_moe.py:762-770)
+ * followed by moe_dispatch_indices (engine/kernels/moe_dispatch.py:178-209):
+ *   topk_idx    [T, K] int32  experts by descending bf16 logit, ties -> lower index
+ *   topk_w      [T, K] fp32   renormalised softmax weights
+ *   offsets     [E+1]  int32  CSR offsets of the (token, slot) pairs by expert
+ *   sorted_tok  [T*K]  int32  token of each pair, stable by pair index
+ *   sorted_slot [T*K]  int32  slot of each pair
+ *   shared_gate [T]    fp32   sigmoid(x . w_sh_gvec)
+ * Any output pointer may be NULL (not copied out). */
+int pmoe_route(const uint16_t* x, int T, int H, int E, int K,
+               const uint16_t* w_router, const uint16_t* w_sh_gvec,
+               int32_t* topk_idx, float* topk_w, int32_t* offsets,
+               int32_t* sorted_tok, int32_t* sorted_slot, float* shared_gate,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* The whole MoE block, y[T,H] (bf16) =
+ *     sum_k w_tk * down_e(SiLU(gate_e x) * up_e x)          (PMOE_F_ROUTED, e in [lo,hi))
+ *   + sigmoid(x . w_sh_gvec) * shared_expert(x)             (PMOE_F_SHARED)
+ * Replaces Qwen3_5MoeSparseMoeBlock.forward (modeling_qwen3_5_moe.py:781-792)
+ * and its patched twin fused_moe_forward (engine/kernels/moe_grouped_mlp.py:166-186).
+ * With expert_lo/hi a strict sub-range it is one rank's routed partial of
+ * ep_forward (engine/runtime/ep.py:97-143) before the all-reduce.
+ * The combine accumulates in fp32 in a fixed order (deterministic). */
+int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                       const uint16_t* w_router, const uint16_t* w_gate_up,
+                       const uint16_t* w_down, const uint16_t* w_sh_gate,
+                       const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                       const uint16_t* w_sh_gvec, int expert_lo, int expert_hi, int flags,
+                       uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* pmoe_block_forward that also records CUDA events on `stream` between its
+ * phases, for per-kernel timing by a benchmark: events[0] before routing,
+ * [1] after routing (router, top-k, dispatch), [2] after gate_up+SiLU*mul,
+ * [3] after down+weighting, [4] after the combine.  NULL entries and
+ * n_events < 5 skip the corresponding records.  No reference counterpart
+ * (instrumentation of pmoe_block_forward). */
+int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                                const uint16_t* w_router, const uint16_t* w_gate_up,
+                                const uint16_t* w_down, const uint16_t* w_sh_gate,
+                                const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                                const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                                int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
+                                void* stream, void* const* events, int n_events);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PARIS_MOE_H_ */

@@ -1,0 +1,76 @@
+"""ctypes binding of libparis_moe.so (the C ABI in include/paris_moe.h).
+
+There is no fallback: if the library is missing or fails to load, every
+operator raises.  ``load()`` never builds; ``build.py`` (or
+``__graft_entry__.build()``) does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libparis_moe.so")
+
+# Every symbol include/paris_moe.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+SIGNATURES = {
+    "pmoe_status_string": (ctypes.c_char_p, [_I]),
+    "pmoe_version": (ctypes.c_char_p, []),
+    "pmoe_workspace_size": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
+    "pmoe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "pmoe_block_forward": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
+                                _I, _I, _I, _P, _P, _SZ, _P]),
+    "pmoe_block_forward_profiled": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
+                                         _P, _I, _I, _I, _P, _P, _SZ, _P,
+                                         ctypes.POINTER(_P), _I]),
+}
+
+PMOE_F_SHARED = 1
+PMOE_F_ROUTED = 2
+PMOE_F_FORCE_STREAM = 4
+PMOE_F_FORCE_TC = 8
+
+_lock = threading.Lock()
+_lib = None
+
+
+class PmoeError(RuntimeError):
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn} failed: status {status} ({msg})")
+        self.status = status
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"{path} is missing: build it with `python {_PKG}/build.py` "
+                "(the MoE operator has no CPU or Python fallback)")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(fn_name: str, status: int) -> None:
+    if status != 0:
+        msg = load().pmoe_status_string(status).decode()
+        raise PmoeError(fn_name, status, msg)
+
+
+def workspace_size(T, H, E, K, I, Is) -> int:
+    out = ctypes.c_size_t(0)
+    check("pmoe_workspace_size", load().pmoe_workspace_size(T, H, E, K, I, Is, ctypes.byref(out)))
+    return int(out.value)

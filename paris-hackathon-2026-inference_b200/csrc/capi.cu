@@ -1,0 +1,166 @@
+// extern "C" entry points of libparis_moe (declared in include/paris_moe.h).
+#include <mutex>
+
+#include "pmoe_common.cuh"
+#include "pmoe_kernels.cuh"
+
+using namespace pmoe;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_init_mu;
+bool g_dev_ready[kMaxDevices] = {};
+int g_dev_sms[kMaxDevices] = {};
+
+// Per-device one-time set-up on the current device: checks for sm_100 and
+// sets kernel attributes.  Cheap after the first call.
+int ensure_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PMOE_ERR_CUDA;
+  if (g_dev_ready[dev]) return PMOE_OK;
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_dev_ready[dev]) return PMOE_OK;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (prop.major != 10) return PMOE_ERR_DEVICE;
+  if (route_init() != cudaSuccess) return PMOE_ERR_CUDA;
+  if (stream_init(prop.multiProcessorCount) != cudaSuccess) return PMOE_ERR_CUDA;
+  g_dev_sms[dev] = prop.multiProcessorCount;
+  g_dev_ready[dev] = true;
+  return PMOE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_shape(int T, int H, int E, int K, int I, int Is) {
+  if (T < 0 || H <= 0 || E <= 0 || K <= 0 || I <= 0 || Is <= 0) return PMOE_ERR_ARG;
+  if (K > E || K > 32) return PMOE_ERR_UNSUPPORTED;
+  if (E > 256) return PMOE_ERR_UNSUPPORTED;
+  if (H % 128 != 0 || I % 32 != 0 || Is % 32 != 0) return PMOE_ERR_UNSUPPORTED;
+  if (long(T) * K > (1L << 30)) return PMOE_ERR_UNSUPPORTED;
+  return PMOE_OK;
+}
+
+inline const __nv_bfloat16* bf(const uint16_t* p) {
+  return reinterpret_cast<const __nv_bfloat16*>(p);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pmoe_status_string(int s) {
+  switch (s) {
+    case PMOE_OK: return "ok";
+    case PMOE_ERR_ARG: return "invalid argument";
+    case PMOE_ERR_ALIGN: return "tensor not 16-byte aligned";
+    case PMOE_ERR_WORKSPACE: return "workspace too small";
+    case PMOE_ERR_CUDA: return "CUDA runtime error";
+    case PMOE_ERR_UNSUPPORTED: return "unsupported shape";
+    case PMOE_ERR_PEER_TIMEOUT: return "timed out waiting for a peer GPU";
+    case PMOE_ERR_DEVICE: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+const char* pmoe_version(void) { return "paris_moe 0.1.0 sm_100a"; }
+
+int pmoe_workspace_size(int T, int H, int E, int K, int I, int Is, size_t* bytes) {
+  if (!bytes) return PMOE_ERR_ARG;
+  int s = check_shape(T, H, E, K, I, Is);
+  if (s != PMOE_OK) return s;
+  *bytes = carve(nullptr, make_dims(T, H, E, K, I, Is)).bytes;
+  return PMOE_OK;
+}
+
+int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_router,
+               const uint16_t* w_sh_gvec, int32_t* topk_idx, float* topk_w, int32_t* offsets,
+               int32_t* sorted_tok, int32_t* sorted_slot, float* shared_gate, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  int s = check_shape(T, H, E, K, 32, 32);
+  if (s != PMOE_OK) return s;
+  if (T == 0) return PMOE_OK;
+  if (!x || !w_router || !w_sh_gvec || !workspace) return PMOE_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_router) || !aligned16(w_sh_gvec)) return PMOE_ERR_ALIGN;
+  if ((s = ensure_device()) != PMOE_OK) return s;
+  Dims d = make_dims(T, H, E, K, 32, 32);
+  Workspace ws = carve(workspace, d);
+  if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  const size_t P = size_t(T) * K;
+  auto cp = [&](void* dst, const void* src, size_t n) {
+    return dst ? cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, st) : cudaSuccess;
+  };
+  if (cp(topk_idx, ws.topk_idx, P * 4) != cudaSuccess || cp(topk_w, ws.topk_w, P * 4) != cudaSuccess ||
+      cp(offsets, ws.offsets, size_t(E + 1) * 4) != cudaSuccess ||
+      cp(sorted_tok, ws.sorted_tok, P * 4) != cudaSuccess ||
+      cp(sorted_slot, ws.sorted_slot, P * 4) != cudaSuccess ||
+      cp(shared_gate, ws.shared_gate, size_t(T) * 4) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  return PMOE_OK;
+}
+
+int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                                const uint16_t* w_router, const uint16_t* w_gate_up,
+                                const uint16_t* w_down, const uint16_t* w_sh_gate,
+                                const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                                const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                                int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
+                                void* stream, void* const* events, int n_events) {
+  int s = check_shape(T, H, E, K, I, Is);
+  if (s != PMOE_OK) return s;
+  if (expert_lo < 0 || expert_hi > E || expert_lo > expert_hi) return PMOE_ERR_ARG;
+  if (flags & ~(PMOE_F_SHARED | PMOE_F_ROUTED | PMOE_F_FORCE_STREAM | PMOE_F_FORCE_TC))
+    return PMOE_ERR_ARG;
+  if (T == 0) return PMOE_OK;
+  const void* ptrs[] = {x, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up, w_sh_down, w_sh_gvec,
+                        y, workspace};
+  for (const void* p : ptrs) {
+    if (!p) return PMOE_ERR_ARG;
+    if (!aligned16(p)) return PMOE_ERR_ALIGN;
+  }
+  if ((s = ensure_device()) != PMOE_OK) return s;
+  Dims d = make_dims(T, H, E, K, I, Is);
+  Workspace ws = carve(workspace, d);
+  if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int with_shared = (flags & PMOE_F_SHARED) ? 1 : 0;
+  const int with_routed = (flags & PMOE_F_ROUTED) ? 1 : 0;
+  auto mark = [&](int i) {
+    if (events && i < n_events && events[i])
+      return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
+    return cudaSuccess;
+  };
+  if (mark(0) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi, with_shared,
+                   with_routed, ws, st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (launch_stream_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
+                            bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr)
+      != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  if (mark(3) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (launch_combine(d, ws, expert_lo, expert_hi, with_shared, with_routed,
+                     reinterpret_cast<__nv_bfloat16*>(y), st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
+  return PMOE_OK;
+}
+
+int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                       const uint16_t* w_router, const uint16_t* w_gate_up,
+                       const uint16_t* w_down, const uint16_t* w_sh_gate,
+                       const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                       const uint16_t* w_sh_gvec, int expert_lo, int expert_hi, int flags,
+                       uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
+  return pmoe_block_forward_profiled(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down,
+                                     w_sh_gate, w_sh_up, w_sh_down, w_sh_gvec, expert_lo,
+                                     expert_hi, flags, y, workspace, workspace_bytes, stream,
+                                     nullptr, 0);
+}
+
+}  // extern "C"

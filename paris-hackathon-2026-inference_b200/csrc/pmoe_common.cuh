@@ -1,0 +1,128 @@
+// Shared device helpers for the B200 MoE-block kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/paris_moe.h"
+
+namespace pmoe {
+
+// ---- workspace layout --------------------------------------------------------
+// One flat caller-provided buffer; every region 256-byte aligned.  The same
+// function is used by the size query and by the launchers so they can never
+// disagree.
+struct Workspace {
+  int32_t* counts;      // [E]        per-expert pair counts (zeroed by the router kernel)
+  int32_t* offsets;     // [E+2]      CSR offsets; [E]..[E+1] is the shared expert's rows
+  int32_t* active;      // [E+1]      experts this rank computes (hit, in range) + shared
+  int32_t* n_active;    // [4]        [0] = entries in `active`
+  int32_t* topk_idx;    // [T*K]
+  float* topk_w;        // [T*K]
+  float* shared_gate;   // [T]        sigmoid(x . w_sh_gvec)
+  int32_t* sorted_tok;  // [T*K+T]    source token of each dispatched row
+  int32_t* sorted_slot; // [T*K]
+  int32_t* pair_dst;    // [T*K+T]    destination row in `rows` (t*K+s, or T*K+t)
+  float* pair_w;        // [T*K+T]    routing weight (or shared gate) of each row
+  float* logit_part;    // [KS][T][Rpad] router partial sums
+  __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
+  float* rows;          // [T*K+T][H] weighted expert outputs, token-major
+  size_t bytes;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Dims {
+  int T, H, E, K, I, Is;
+  int Rpad;   // router rows (E experts + shared gate) padded to 16
+  int KS;     // router split-K factor
+  int ldh;    // row stride of h
+};
+
+inline int router_split(int T, int H) {
+  // Enough independent warps to cover the GPU at small T; 1 at large T.
+  int ks = 1;
+  int ttiles = (T + 31) / 32;
+  while (ks < 16 && ttiles * ks < 32 && (H / (ks * 2)) % 128 == 0) ks *= 2;
+  return ks;
+}
+
+inline Dims make_dims(int T, int H, int E, int K, int I, int Is) {
+  Dims d{T, H, E, K, I, Is, 0, 0, 0};
+  d.Rpad = ((E + 1) + 15) / 16 * 16;
+  d.KS = router_split(T, H);
+  d.ldh = I > Is ? I : Is;
+  return d;
+}
+
+inline Workspace carve(void* base, const Dims& d) {
+  Workspace w{};
+  size_t off = 0;
+  char* b = static_cast<char*>(base);
+  auto take = [&](size_t n) { char* p = b ? b + off : nullptr; off = align256(off + n); return p; };
+  size_t P = size_t(d.T) * d.K, R = P + d.T;
+  w.counts = (int32_t*)take(sizeof(int32_t) * d.E);
+  w.offsets = (int32_t*)take(sizeof(int32_t) * (d.E + 2));
+  w.active = (int32_t*)take(sizeof(int32_t) * (d.E + 1));
+  w.n_active = (int32_t*)take(sizeof(int32_t) * 4);
+  w.topk_idx = (int32_t*)take(sizeof(int32_t) * P);
+  w.topk_w = (float*)take(sizeof(float) * P);
+  w.shared_gate = (float*)take(sizeof(float) * d.T);
+  w.sorted_tok = (int32_t*)take(sizeof(int32_t) * R);
+  w.sorted_slot = (int32_t*)take(sizeof(int32_t) * P);
+  w.pair_dst = (int32_t*)take(sizeof(int32_t) * R);
+  w.pair_w = (float*)take(sizeof(float) * R);
+  w.logit_part = (float*)take(sizeof(float) * size_t(d.KS) * d.T * d.Rpad);
+  w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
+  w.rows = (float*)take(sizeof(float) * R * d.H);
+  w.bytes = off;
+  return w;
+}
+
+// ---- device helpers ------------------------------------------------------------
+
+// 128-bit streaming load for weights: each byte is read once per call, so keep
+// it out of L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// 128-bit load for activations that several warps of a CTA re-read.
+__device__ __forceinline__ uint4 ldg_keep(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// D += A(16x16, row) * B(16x8, col), bf16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 32-wide k step of a 16-row weight tile against 8 columns.
+//
+// Lane (g = lane/4, c = lane%4) holds, from one 16-byte load each, global
+// k in [k0+8c, k0+8c+8) of weight rows g and g+8 (wa, wb) and of column g of
+// the activation tile (xv).  The two MMAs see a fixed permutation of the 32
+// k indices, identical for A and B, so the dot product is unchanged while
+// every operand comes from one coalesced 128-bit load.
+__device__ __forceinline__ void mma_k32(float (&d)[4], const uint4& wa, const uint4& wb,
+                                        const uint4& xv) {
+  mma16816(d, wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+  mma16816(d, wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+}  // namespace pmoe

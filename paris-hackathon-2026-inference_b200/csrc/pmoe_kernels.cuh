@@ -1,0 +1,23 @@
+// Host-side launchers shared between the translation units of libparis_moe.
+#pragma once
+#include "pmoe_common.cuh"
+
+namespace pmoe {
+
+cudaError_t route_init();
+cudaError_t stream_init(int num_sms);
+
+cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                         const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
+                         int with_routed, const Workspace& ws, cudaStream_t st);
+
+cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
+                                  const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
+                                  const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
+                                  const __nv_bfloat16* w_sh_down, const Workspace& ws,
+                                  cudaStream_t st, void* mid_event);
+
+cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
+                           int with_routed, __nv_bfloat16* y, cudaStream_t st);
+
+}  // namespace pmoe
