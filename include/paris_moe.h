@@ -37,7 +37,8 @@ enum {
   PMOE_ERR_CUDA = -4,       /* a CUDA runtime call failed (launch, copy) */
   PMOE_ERR_UNSUPPORTED = -5,/* shape outside what the kernels implement */
   PMOE_ERR_PEER_TIMEOUT = -6,/* a bounded wait on a peer GPU ran out */
-  PMOE_ERR_DEVICE = -7      /* not an sm_100 device */
+  PMOE_ERR_DEVICE = -7,     /* not an sm_100 device */
+  PMOE_ERR_NOALLOC_TOO_LARGE = -8 /* shape needs more scratch than the no-alloc entry has */
 };
 
 /* Flags of pmoe_block_forward. */
@@ -105,6 +106,34 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
                                 const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
                                 int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
                                 void* stream, void* const* events, int n_events);
+
+/* pmoe_block_forward for callers that cannot allocate device memory: it takes
+ * no workspace.  Meant for hosts such as a serving engine that reserves all
+ * of HBM up front (KV cache, weights) and allows no allocation on its decode
+ * path, or a program in another language calling through a bare FFI with no
+ * device allocator of its own.  No counterpart in the reference (whose torch
+ * code allocates its temporaries through PyTorch on every call).
+ *
+ * Scratch is one fixed array of pmoe_noalloc_scratch_bytes() (8 MiB) in
+ * device memory, held by every GPU that loads the library until the process
+ * exits.  Shapes whose workspace (pmoe_workspace_size) exceeds it -- at the
+ * Qwen3.5 shape, more than 64 tokens -- return PMOE_ERR_NOALLOC_TOO_LARGE
+ * without launching anything.  The first call on a device looks up the
+ * array's device address (set-up, once per device); make that first call
+ * before any stream capture.  All calls on a device share the array and it
+ * keeps the previous call's contents, so calls that may overlap on the GPU
+ * race and must be ordered by the caller.  Allocates nothing: no cudaMalloc,
+ * no cudaFree, no allocating library routine.  Same arguments, results and
+ * status codes as pmoe_block_forward otherwise. */
+int pmoe_block_forward_noalloc(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                               const uint16_t* w_router, const uint16_t* w_gate_up,
+                               const uint16_t* w_down, const uint16_t* w_sh_gate,
+                               const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                               const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                               int flags, uint16_t* y, void* stream);
+
+/* Size in bytes of the fixed scratch array of pmoe_block_forward_noalloc. */
+size_t pmoe_noalloc_scratch_bytes(void);
 
 #ifdef __cplusplus
 }

@@ -27,6 +27,9 @@ SIGNATURES = {
     "pmoe_block_forward_profiled": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
                                          _P, _I, _I, _I, _P, _P, _SZ, _P,
                                          ctypes.POINTER(_P), _I]),
+    "pmoe_block_forward_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
+                                        _P, _I, _I, _I, _P, _P]),
+    "pmoe_noalloc_scratch_bytes": (_SZ, []),
 }
 
 PMOE_F_SHARED = 1

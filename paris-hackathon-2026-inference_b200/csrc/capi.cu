@@ -60,6 +60,8 @@ const char* pmoe_status_string(int s) {
     case PMOE_ERR_UNSUPPORTED: return "unsupported shape";
     case PMOE_ERR_PEER_TIMEOUT: return "timed out waiting for a peer GPU";
     case PMOE_ERR_DEVICE: return "device is not sm_100 (B200)";
+    case PMOE_ERR_NOALLOC_TOO_LARGE:
+      return "shape needs more scratch than pmoe_block_forward_noalloc's fixed array";
     default: return "unknown status";
   }
 }
