@@ -37,7 +37,7 @@ int check_shape(int T, int H, int E, int K, int I, int Is) {
   if (T < 0 || H <= 0 || E <= 0 || K <= 0 || I <= 0 || Is <= 0) return PMOE_ERR_ARG;
   if (K > E || K > 32) return PMOE_ERR_UNSUPPORTED;
   if (E > 256) return PMOE_ERR_UNSUPPORTED;
-  if (H % 128 != 0 || I % 32 != 0 || Is % 32 != 0) return PMOE_ERR_UNSUPPORTED;
+  if (H % 256 != 0 || I % 64 != 0 || Is % 64 != 0) return PMOE_ERR_UNSUPPORTED;
   if (long(T) * K > (1L << 30)) return PMOE_ERR_UNSUPPORTED;
   return PMOE_OK;
 }
@@ -80,13 +80,13 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
                const uint16_t* w_sh_gvec, int32_t* topk_idx, float* topk_w, int32_t* offsets,
                int32_t* sorted_tok, int32_t* sorted_slot, float* shared_gate, void* workspace,
                size_t workspace_bytes, void* stream) {
-  int s = check_shape(T, H, E, K, 32, 32);
+  int s = check_shape(T, H, E, K, 64, 64);
   if (s != PMOE_OK) return s;
   if (T == 0) return PMOE_OK;
   if (!x || !w_router || !w_sh_gvec || !workspace) return PMOE_ERR_ARG;
   if (!aligned16(x) || !aligned16(w_router) || !aligned16(w_sh_gvec)) return PMOE_ERR_ALIGN;
   if ((s = ensure_device()) != PMOE_OK) return s;
-  Dims d = make_dims(T, H, E, K, 32, 32);
+  Dims d = make_dims(T, H, E, K, 64, 64);
   Workspace ws = carve(workspace, d);
   if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -24,7 +24,8 @@ struct Workspace {
   int32_t* sorted_slot; // [T*K]
   int32_t* pair_dst;    // [T*K+T]    destination row in `rows` (t*K+s, or T*K+t)
   float* pair_w;        // [T*K+T]    routing weight (or shared gate) of each row
-  float* logit_part;    // [KS][T][Rpad] router partial sums
+  float* logit_part;    // [T][Rpad]   router logits (bf16-rounded) + raw shared-gate sum
+  int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major
   size_t bytes;
@@ -35,22 +36,17 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 struct Dims {
   int T, H, E, K, I, Is;
   int Rpad;   // router rows (E experts + shared gate) padded to 16
-  int KS;     // router split-K factor
+  int KS;     // router split-K factor (1)
   int ldh;    // row stride of h
 };
 
-inline int router_split(int T, int H) {
-  // Enough independent warps to cover the GPU at small T; 1 at large T.
-  int ks = 1;
-  int ttiles = (T + 31) / 32;
-  while (ks < 16 && ttiles * ks < 32 && (H / (ks * 2)) % 128 == 0) ks *= 2;
-  return ks;
-}
+// Token counts up to this use the single-launch routing kernel.
+constexpr int kFusedRouteMaxT = 128;
 
 inline Dims make_dims(int T, int H, int E, int K, int I, int Is) {
   Dims d{T, H, E, K, I, Is, 0, 0, 0};
   d.Rpad = ((E + 1) + 15) / 16 * 16;
-  d.KS = router_split(T, H);
+  d.KS = 1;
   d.ldh = I > Is ? I : Is;
   return d;
 }
@@ -73,6 +69,7 @@ inline Workspace carve(void* base, const Dims& d) {
   w.pair_dst = (int32_t*)take(sizeof(int32_t) * R);
   w.pair_w = (float*)take(sizeof(float) * R);
   w.logit_part = (float*)take(sizeof(float) * size_t(d.KS) * d.T * d.Rpad);
+  w.status = (int32_t*)take(sizeof(int32_t) * 8);
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
   w.rows = (float*)take(sizeof(float) * R * d.H);
   w.bytes = off;

@@ -1,10 +1,17 @@
-// Weight-streaming expert kernels for the HBM-bound decode regime (small T).
+// TMA-staged weight-streaming expert kernels for the HBM-bound decode regime.
 //
-// At T <= 64 each active expert sees a handful of tokens, so the block is a
-// stream over ~1.4 GB of expert weights with arithmetic intensity of a few
-// FLOP/B.  Every weight byte is loaded exactly once with a 128-bit
-// L1-bypassing load straight into mma.sync fragments (see mma_k32); the
-// activations (tiny, re-read by the warps of a CTA) come through L1.
+// At T <= 64 each active expert sees a handful of tokens: the block is a
+// stream over ~1.4 GB of expert weights at a few FLOP/B.  Each persistent
+// CTA (one per SM) runs a warp-specialised pipeline:
+//   * warp 0, one lane: producer.  Walks this CTA's units and issues 2D TMA
+//     loads (128-byte swizzle, L2 evict-first) of 64-row x 64-column weight
+//     tiles into an mbarrier ring of 128 KiB, so ~128 KiB per SM is in
+//     flight independent of register pressure;
+//   * warps 1..4: consumers.  Each owns 16 weight rows of the tile, reads
+//     its mma.sync A fragments from the swizzled tile with 128-bit shared
+//     loads and the activations (tiny, reused by every warp) from L1, and
+//     releases the stage.
+// Every weight byte is loaded from HBM exactly once per call.
 //
 // Reference arithmetic: the per-expert body of Qwen3_5MoeExperts.forward
 // (modeling_qwen3_5_moe.py:743-749), the shared expert Qwen3_5MoeMLP
@@ -12,6 +19,7 @@
 // engine/kernels/moe_grouped_mlp.py:152-163 (done here in fp32).
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
+#include "pmoe_tma.cuh"
 
 namespace pmoe {
 
@@ -24,34 +32,101 @@ struct ExpertTables {
   const float* pair_w;
 };
 
-// Units of work per expert and their weight rows.
-// gate_up: unit = 16 intermediate columns j (gate rows j.., up rows I+j..).
-// down:    unit = 16 output rows of down_proj.
+constexpr int kConsumers = 4;
+constexpr int kStreamThreads = 32 * (kConsumers + 1);
+constexpr int kUnitRows = 16 * kConsumers;    // 64 weight rows per tile
+constexpr int kKC = 64;                       // k per tile (128-byte rows)
+constexpr int kBoxBytes = kUnitRows * kKC * 2;  // 8 KiB
+constexpr int kRingBytes = 128 * 1024;
+constexpr int kGuStages = kRingBytes / (2 * kBoxBytes);  // gate + up tile per stage
+constexpr int kDnStages = kRingBytes / kBoxBytes;
+constexpr int kStreamSmem = kRingBytes + 2 * kDnStages * 8 + 1024;
 
-__global__ void __launch_bounds__(256) gate_up_stream_kernel(
-    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate_up,
-    const __nv_bfloat16* __restrict__ w_sh_gate, const __nv_bfloat16* __restrict__ w_sh_up,
-    ExpertTables tb, int H, int E, int I, int Is, int ldh, __nv_bfloat16* __restrict__ h) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int U = (I > Is ? I : Is) / 16;
-  const long n_units = long(tb.n_active[0]) * U;
-  const long nwarps = long(gridDim.x) * (blockDim.x / 32);
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void set_status(int* status, int code) { atomicCAS(status, 0, code); }
+
+// Producer drain after an abort: wait (bounded) for every issued, not yet
+// consumed stage so no bulk copy is still writing this CTA's shared memory.
+__device__ __forceinline__ void drain(uint64_t* full, uint32_t issued, int stages) {
+  const uint32_t first = issued > uint32_t(stages) ? issued - stages : 0;
+  for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % stages], (j / stages) & 1);
+}
+
+// ---------------------------------------------------------------------------
+// gate_up + SiLU*mul.  Unit = (expert, 64 intermediate columns j): the gate
+// rows j.. and the up rows I+j.. of that expert (shared expert: its own two
+// weight matrices).  h[row, j] = bf16(silu(x.Wg_j) * (x.Wu_j)) for each of
+// the expert's dispatched rows, 32 rows per pass.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
+    const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_sg,
+    const __grid_constant__ CUtensorMap tm_su, const __nv_bfloat16* __restrict__ x,
+    ExpertTables tb, int H, int E, int I, int Is, int ldh, __nv_bfloat16* __restrict__ h,
+    int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
+  uint64_t* empty = full + kGuStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGuStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const int UJ = (I > Is ? I : Is) / kUnitRows;
+  const int n_units = tb.n_active[0] * UJ;
+  const int nkc = H / kKC;
+
+  if (warp == 0) {
+    if (lane != 0) return;
+    prefetch_tmap(&tm_gu);
+    prefetch_tmap(&tm_sg);
+    prefetch_tmap(&tm_su);
+    const uint64_t pol = l2_policy_evict_first();
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int e = tb.active[u / UJ], jb = u % UJ;
+      const bool sh = (e == E);
+      if (jb * kUnitRows >= (sh ? Is : I)) continue;
+      const int n = tb.offsets[e + 1] - tb.offsets[e];
+      const CUtensorMap* mg = sh ? &tm_sg : &tm_gu;
+      const CUtensorMap* mu = sh ? &tm_su : &tm_gu;
+      const int rg = sh ? jb * kUnitRows : e * 2 * I + jb * kUnitRows;
+      const int ru = sh ? jb * kUnitRows : e * 2 * I + I + jb * kUnitRows;
+      for (int nb = 0; nb < n; nb += 32) {
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kGuStages;
+          if (it >= uint32_t(kGuStages) && !mbar_wait(&empty[s], ((it / kGuStages) & 1) ^ 1)) {
+            set_status(status, kStatusTimeoutEmpty);
+            drain(full, it, kGuStages);
+            return;
+          }
+          mbar_arrive_expect_tx(&full[s], 2 * kBoxBytes);
+          uint8_t* dst = smem + s * 2 * kBoxBytes;
+          tma_load_2d_hint(dst, mg, kc * kKC, rg, &full[s], pol);
+          tma_load_2d_hint(dst + kBoxBytes, mu, kc * kKC, ru, &full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  // consumers
+  const int cw = warp - 1, g = lane >> 2, c = lane & 3;
+  const int r0 = cw * 16 + g, r1 = r0 + 8;
+  const uint32_t sbase = smem_u32(smem);
   const uint4 zero = make_uint4(0, 0, 0, 0);
-  for (long u = long(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); u < n_units;
-       u += nwarps) {
-    const int e = tb.active[u / U];
-    const int jg = int(u % U);
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int e = tb.active[u / UJ], jb = u % UJ;
     const bool sh = (e == E);
-    const int Ie = sh ? Is : I;
-    if (jg * 16 >= Ie) continue;
-    const __nv_bfloat16* wg =
-        sh ? w_sh_gate + size_t(jg * 16) * H : w_gate_up + (size_t(e) * 2 * I + jg * 16) * H;
-    const __nv_bfloat16* wu =
-        sh ? w_sh_up + size_t(jg * 16) * H : w_gate_up + (size_t(e) * 2 * I + I + jg * 16) * H;
-    const __nv_bfloat16* wg0 = wg + size_t(g) * H + 8 * c;
-    const __nv_bfloat16* wg1 = wg0 + size_t(8) * H;
-    const __nv_bfloat16* wu0 = wu + size_t(g) * H + 8 * c;
-    const __nv_bfloat16* wu1 = wu0 + size_t(8) * H;
+    if (jb * kUnitRows >= (sh ? Is : I)) continue;
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
     for (int nb = 0; nb < n; nb += 32) {
@@ -63,21 +138,33 @@ __global__ void __launch_bounds__(256) gate_up_stream_kernel(
       }
       const int ng = min(4, (n - nb + 7) / 8);  // warp-uniform
       float ag[4][4] = {}, au[4][4] = {};
-#pragma unroll 4
-      for (int k0 = 0; k0 < H; k0 += 32) {
-        const uint4 a0 = ldg_stream(wg0 + k0), a1 = ldg_stream(wg1 + k0);
-        const uint4 b0 = ldg_stream(wu0 + k0), b1 = ldg_stream(wu1 + k0);
+      for (int kc = 0; kc < nkc; ++kc, ++it) {
+        const int s = it % kGuStages;
+        if (!mbar_wait(&full[s], (it / kGuStages) & 1)) {
+          set_status(status, kStatusTimeoutFull);
+          return;
+        }
+        const uint32_t tg = sbase + s * 2 * kBoxBytes, tu = tg + kBoxBytes;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (q < ng) {
-            const uint4 xv = xp[q] ? ldg_keep(xp[q] + k0) : zero;
-            mma_k32(ag[q], a0, a1, xv);
-            mma_k32(au[q], b0, b1, xv);
+        for (int ks = 0; ks < 2; ++ks) {
+          const int ch = ks * 4 + c;
+          const uint4 a0 = lds128(tg + swz128(r0, ch)), a1 = lds128(tg + swz128(r1, ch));
+          const uint4 b0 = lds128(tu + swz128(r0, ch)), b1 = lds128(tu + swz128(r1, ch));
+          const int kk = kc * kKC + ks * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (q < ng) {
+              const uint4 xv = xp[q] ? ldg_keep(xp[q] + kk) : zero;
+              mma_k32(ag[q], a0, a1, xv);
+              mma_k32(au[q], b0, b1, xv);
+            }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      // Epilogue: rows j = jg*16 + g (+8), columns = dispatched rows p0+nb+q*8+2c (+1).
-      const int j0 = jg * 16 + g;
+      // rows j = jb*64 + r0 (+8), columns = dispatched rows p0+nb+q*8+2c (+1)
+      const int j0 = jb * kUnitRows + r0;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q < ng) {
@@ -96,24 +183,68 @@ __global__ void __launch_bounds__(256) gate_up_stream_kernel(
   }
 }
 
-__global__ void __launch_bounds__(256) down_stream_kernel(
-    const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w_down,
-    const __nv_bfloat16* __restrict__ w_sh_down, ExpertTables tb, int H, int E, int I, int Is,
-    int ldh, float* __restrict__ rows) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int U = H / 16;
-  const long n_units = long(tb.n_active[0]) * U;
-  const long nwarps = long(gridDim.x) * (blockDim.x / 32);
-  for (long u = long(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5); u < n_units;
-       u += nwarps) {
-    const int e = tb.active[u / U];
-    const int rg = int(u % U);
+// ---------------------------------------------------------------------------
+// down + routing weight.  Unit = (expert, 64 output rows of down_proj);
+// rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
+    const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
+    const __nv_bfloat16* __restrict__ h, ExpertTables tb, int H, int E, int I, int Is, int ldh,
+    float* __restrict__ rows, int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
+  uint64_t* empty = full + kDnStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDnStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const int UR = H / kUnitRows;
+  const int n_units = tb.n_active[0] * UR;
+
+  if (warp == 0) {
+    if (lane != 0) return;
+    prefetch_tmap(&tm_dn);
+    prefetch_tmap(&tm_sd);
+    const uint64_t pol = l2_policy_evict_first();
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int e = tb.active[u / UR], rb = u % UR;
+      const bool sh = (e == E);
+      const int nkc = (sh ? Is : I) / kKC;
+      const int n = tb.offsets[e + 1] - tb.offsets[e];
+      const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
+      const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
+      for (int nb = 0; nb < n; nb += 32) {
+        for (int kc = 0; kc < nkc; ++kc, ++it) {
+          const int s = it % kDnStages;
+          if (it >= uint32_t(kDnStages) && !mbar_wait(&empty[s], ((it / kDnStages) & 1) ^ 1)) {
+            set_status(status, kStatusTimeoutEmpty);
+            drain(full, it, kDnStages);
+            return;
+          }
+          mbar_arrive_expect_tx(&full[s], kBoxBytes);
+          tma_load_2d_hint(smem + s * kBoxBytes, m, kc * kKC, row, &full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  const int cw = warp - 1, g = lane >> 2, c = lane & 3;
+  const int r0 = cw * 16 + g, r1 = r0 + 8;
+  const uint32_t sbase = smem_u32(smem);
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  uint32_t it = 0;
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int e = tb.active[u / UR], rb = u % UR;
     const bool sh = (e == E);
-    const int Ke = sh ? Is : I;
-    const __nv_bfloat16* w =
-        sh ? w_sh_down + size_t(rg * 16) * Is : w_down + (size_t(e) * H + rg * 16) * I;
-    const __nv_bfloat16* w0 = w + size_t(g) * Ke + 8 * c;
-    const __nv_bfloat16* w1 = w0 + size_t(8) * Ke;
+    const int nkc = (sh ? Is : I) / kKC;
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
     for (int nb = 0; nb < n; nb += 32) {
@@ -125,19 +256,30 @@ __global__ void __launch_bounds__(256) down_stream_kernel(
       }
       const int ng = min(4, (n - nb + 7) / 8);
       float acc[4][4] = {};
-      const uint4 zero = make_uint4(0, 0, 0, 0);
-#pragma unroll 4
-      for (int k0 = 0; k0 < Ke; k0 += 32) {
-        const uint4 a0 = ldg_stream(w0 + k0), a1 = ldg_stream(w1 + k0);
+      for (int kc = 0; kc < nkc; ++kc, ++it) {
+        const int s = it % kDnStages;
+        if (!mbar_wait(&full[s], (it / kDnStages) & 1)) {
+          set_status(status, kStatusTimeoutFull);
+          return;
+        }
+        const uint32_t tw = sbase + s * kBoxBytes;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (q < ng) {
-            const uint4 hv = hp[q] ? ldg_keep(hp[q] + k0) : zero;
-            mma_k32(acc[q], a0, a1, hv);
+        for (int ks = 0; ks < 2; ++ks) {
+          const int ch = ks * 4 + c;
+          const uint4 a0 = lds128(tw + swz128(r0, ch)), a1 = lds128(tw + swz128(r1, ch));
+          const int kk = kc * kKC + ks * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (q < ng) {
+              const uint4 hv = hp[q] ? ldg_keep(hp[q] + kk) : zero;
+              mma_k32(acc[q], a0, a1, hv);
+            }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      const int r0 = rg * 16 + g;
+      const int orow = rb * kUnitRows + r0;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q < ng) {
@@ -147,9 +289,9 @@ __global__ void __launch_bounds__(256) down_stream_kernel(
             if (i + hh < n) {
               const int p = p0 + i + hh;
               const float wt = tb.pair_w[p];
-              float* orow = rows + size_t(tb.pair_dst[p]) * H;
-              orow[r0] = acc[q][hh] * wt;
-              orow[r0 + 8] = acc[q][2 + hh] * wt;
+              float* out = rows + size_t(tb.pair_dst[p]) * H;
+              out[orow] = acc[q][hh] * wt;
+              out[orow + 8] = acc[q][2 + hh] * wt;
             }
           }
         }
@@ -188,18 +330,15 @@ __global__ void __launch_bounds__(256) combine_kernel(
   reinterpret_cast<uint2*>(y + size_t(t) * H)[c4] = packed;
 }
 
-static int g_stream_blocks = 0;
+static int g_num_sms = 148;
 
 cudaError_t stream_init(int num_sms) {
-  int per_sm_gu = 0, per_sm_dn = 0;
-  cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_gu, gate_up_stream_kernel, 256, 0);
-  if (err != cudaSuccess) return err;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_dn, down_stream_kernel, 256, 0);
-  if (err != cudaSuccess) return err;
-  int per_sm = per_sm_gu < per_sm_dn ? per_sm_gu : per_sm_dn;
-  if (per_sm < 1) per_sm = 1;
-  g_stream_blocks = num_sms * per_sm;
-  return cudaSuccess;
+  g_num_sms = num_sms;
+  cudaError_t e = cudaFuncSetAttribute(gate_up_tma_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(down_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kStreamSmem);
 }
 
 cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
@@ -207,16 +346,23 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                                   const __nv_bfloat16* w_sh_down, const Workspace& ws,
                                   cudaStream_t st, void* mid_event) {
+  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd;
+  const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E;
+  if (!make_tmap_bf16_2d(&tm_gu, w_gate_up, H, E * 2 * I, H * 2, kKC, kUnitRows) ||
+      !make_tmap_bf16_2d(&tm_sg, w_sh_gate, H, Is, H * 2, kKC, kUnitRows) ||
+      !make_tmap_bf16_2d(&tm_su, w_sh_up, H, Is, H * 2, kKC, kUnitRows) ||
+      !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kKC, kUnitRows) ||
+      !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kKC, kUnitRows))
+    return cudaErrorInvalidValue;
   ExpertTables tb{ws.active, ws.n_active, ws.offsets, ws.sorted_tok, ws.pair_dst, ws.pair_w};
-  const int blocks = g_stream_blocks > 0 ? g_stream_blocks : 148 * 4;
-  gate_up_stream_kernel<<<blocks, 256, 0, st>>>(x, w_gate_up, w_sh_gate, w_sh_up, tb, d.H, d.E,
-                                                d.I, d.Is, d.ldh, ws.h);
+  gate_up_tma_kernel<<<g_num_sms, kStreamThreads, kStreamSmem, st>>>(
+      tm_gu, tm_sg, tm_su, x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.status + 1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (e != cudaSuccess) return e;
   }
-  down_stream_kernel<<<blocks, 256, 0, st>>>(ws.h, w_down, w_sh_down, tb, d.H, d.E, d.I, d.Is,
-                                             d.ldh, ws.rows);
+  down_tma_kernel<<<g_num_sms, kStreamThreads, kStreamSmem, st>>>(
+      tm_dn, tm_sd, ws.h, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.rows, ws.status + 1);
   return cudaGetLastError();
 }
 

@@ -93,7 +93,7 @@ def moe_route(x: torch.Tensor, w_router: torch.Tensor, w_sh_gvec: torch.Tensor,
         sg = torch.empty(T, dtype=torch.float32, device=dev)
         if T == 0:
             return idx, wts, offs, stok, sslot, sg
-        nbytes = _lib.workspace_size(T, H, E, k, 32, 32)
+        nbytes = _lib.workspace_size(T, H, E, k, 64, 64)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         st = _lib.load().pmoe_route(
             x.data_ptr(), T, H, E, k, w_router.data_ptr(), w_sh_gvec.data_ptr(), idx.data_ptr(),
