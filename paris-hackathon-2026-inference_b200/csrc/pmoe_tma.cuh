@@ -110,9 +110,11 @@ __device__ __forceinline__ uint4 lds128(uint32_t saddr) {
 // ---- host side ------------------------------------------------------------
 
 // 2D bf16 tensor map, rows of `inner` elements with a row pitch of
-// `row_stride_bytes`, box {box_inner, box_outer}, 128-byte swizzle.
+// `row_stride_bytes`, box {box_inner, box_outer}, 128-byte swizzle unless
+// `swizzle128` is false (then the box lands row-major, unswizzled).
 // Returns false if the driver entry point is unavailable or encoding fails.
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                       bool swizzle128 = true);
 
 }  // namespace pmoe

@@ -5,12 +5,12 @@
 // CTA (one per SM) runs a warp-specialised pipeline:
 //   * warp 0, one lane: producer.  Walks this CTA's units and issues 2D TMA
 //     loads (128-byte swizzle, L2 evict-first) of 64-row x 64-column weight
-//     tiles into an mbarrier ring of 128 KiB, so ~128 KiB per SM is in
-//     flight independent of register pressure;
+//     tiles, plus the matching 64-column slice of the activation rows, into
+//     an mbarrier ring of ~140 KiB, so that much is in flight per SM
+//     independent of register pressure;
 //   * warps 1..4: consumers.  Each owns 16 weight rows of the tile, reads
-//     its mma.sync A fragments from the swizzled tile with 128-bit shared
-//     loads and the activations (tiny, reused by every warp) from L1, and
-//     releases the stage.
+//     its mma.sync A and B fragments from shared memory with 128-bit loads,
+//     and releases the stage.
 // Every weight byte is loaded from HBM exactly once per call.
 //
 // Reference arithmetic: the per-expert body of Qwen3_5MoeExperts.forward
@@ -34,13 +34,18 @@ struct ExpertTables {
 
 constexpr int kConsumers = 4;
 constexpr int kStreamThreads = 32 * (kConsumers + 1);
-constexpr int kUnitRows = 16 * kConsumers;    // 64 weight rows per tile
-constexpr int kKC = 64;                       // k per tile (128-byte rows)
-constexpr int kBoxBytes = kUnitRows * kKC * 2;  // 8 KiB
-constexpr int kRingBytes = 128 * 1024;
-constexpr int kGuStages = kRingBytes / (2 * kBoxBytes);  // gate + up tile per stage
-constexpr int kDnStages = kRingBytes / kBoxBytes;
-constexpr int kStreamSmem = kRingBytes + 2 * kDnStages * 8 + 1024;
+constexpr int kUnitRows = 16 * kConsumers;      // 64 weight rows per tile
+constexpr int kKC = 64;                         // k per tile (128-byte rows)
+constexpr int kBoxBytes = kUnitRows * kKC * 2;  // 8 KiB weight tile
+constexpr int kActRows = 32;                    // dispatched rows per pass
+constexpr int kActBytes = kActRows * kKC * 2;   // 4 KiB activation tile
+constexpr int kGuStageBytes = 2 * kBoxBytes + kActBytes;  // gate + up + x
+constexpr int kDnStageBytes = kBoxBytes + kActBytes;      // down + h
+constexpr int kGuStages = 7;
+constexpr int kDnStages = 11;
+constexpr int kGuSmem = kGuStages * kGuStageBytes + 2 * kGuStages * 8 + 1024;
+constexpr int kDnSmem = kDnStages * kDnStageBytes + 2 * kDnStages * 8 + 1024;
+static_assert(kGuStageBytes % 1024 == 0 && kDnStageBytes % 1024 == 0, "stage alignment");
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -58,18 +63,21 @@ __device__ __forceinline__ void drain(uint64_t* full, uint32_t issued, int stage
 // ---------------------------------------------------------------------------
 // gate_up + SiLU*mul.  Unit = (expert, 64 intermediate columns j): the gate
 // rows j.. and the up rows I+j.. of that expert (shared expert: its own two
-// weight matrices).  h[row, j] = bf16(silu(x.Wg_j) * (x.Wu_j)) for each of
-// the expert's dispatched rows, 32 rows per pass.
+// weight matrices).  A stage holds the 64x64 gate and up tiles (swizzled)
+// and the same 64 k of the pass's (up to 32) gathered token rows of x (one
+// unswizzled 128-byte TMA row each), all landed on one mbarrier.
+// h[row, j] = bf16(silu(x.Wg_j) * (x.Wu_j)).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_sg,
-    const __grid_constant__ CUtensorMap tm_su, const __nv_bfloat16* __restrict__ x,
+    const __grid_constant__ CUtensorMap tm_su, const __grid_constant__ CUtensorMap tm_x,
     ExpertTables tb, int H, int E, int I, int Is, int ldh, __nv_bfloat16* __restrict__ h,
     int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGuStages * kGuStageBytes);
   uint64_t* empty = full + kGuStages;
+  __shared__ int s_tok[kActRows];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGuStages; ++s) {
@@ -88,18 +96,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     prefetch_tmap(&tm_gu);
     prefetch_tmap(&tm_sg);
     prefetch_tmap(&tm_su);
+    prefetch_tmap(&tm_x);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int e = tb.active[u / UJ], jb = u % UJ;
       const bool sh = (e == E);
       if (jb * kUnitRows >= (sh ? Is : I)) continue;
-      const int n = tb.offsets[e + 1] - tb.offsets[e];
+      const int p0 = tb.offsets[e];
+      const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* mg = sh ? &tm_sg : &tm_gu;
       const CUtensorMap* mu = sh ? &tm_su : &tm_gu;
       const int rg = sh ? jb * kUnitRows : e * 2 * I + jb * kUnitRows;
       const int ru = sh ? jb * kUnitRows : e * 2 * I + I + jb * kUnitRows;
-      for (int nb = 0; nb < n; nb += 32) {
+      for (int nb = 0; nb < n; nb += kActRows) {
+        const int nr = min(kActRows, n - nb);
+        for (int i = 0; i < nr; ++i) s_tok[i] = tb.sorted_tok[p0 + nb + i];
         for (int kc = 0; kc < nkc; ++kc, ++it) {
           const int s = it % kGuStages;
           if (it >= uint32_t(kGuStages) && !mbar_wait(&empty[s], ((it / kGuStages) & 1) ^ 1)) {
@@ -107,10 +119,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
             drain(full, it, kGuStages);
             return;
           }
-          mbar_arrive_expect_tx(&full[s], 2 * kBoxBytes);
-          uint8_t* dst = smem + s * 2 * kBoxBytes;
+          mbar_arrive_expect_tx(&full[s], 2 * kBoxBytes + nr * kKC * 2);
+          uint8_t* dst = smem + s * kGuStageBytes;
           tma_load_2d_hint(dst, mg, kc * kKC, rg, &full[s], pol);
           tma_load_2d_hint(dst + kBoxBytes, mu, kc * kKC, ru, &full[s], pol);
+          uint8_t* xd = dst + 2 * kBoxBytes;
+          for (int i = 0; i < nr; ++i) tma_load_2d(xd + i * kKC * 2, &tm_x, kc * kKC, s_tok[i], &full[s]);
         }
       }
     }
@@ -121,7 +135,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
   const int cw = warp - 1, g = lane >> 2, c = lane & 3;
   const int r0 = cw * 16 + g, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
-  const uint4 zero = make_uint4(0, 0, 0, 0);
   uint32_t it = 0;
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int e = tb.active[u / UJ], jb = u % UJ;
@@ -129,13 +142,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     if (jb * kUnitRows >= (sh ? Is : I)) continue;
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
-    for (int nb = 0; nb < n; nb += 32) {
-      const __nv_bfloat16* xp[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int i = nb + q * 8 + g;
-        xp[q] = i < n ? x + size_t(tb.sorted_tok[p0 + i]) * H + 8 * c : nullptr;
-      }
+    for (int nb = 0; nb < n; nb += kActRows) {
       const int ng = min(4, (n - nb + 7) / 8);  // warp-uniform
       float ag[4][4] = {}, au[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
@@ -144,17 +151,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
           set_status(status, kStatusTimeoutFull);
           return;
         }
-        const uint32_t tg = sbase + s * 2 * kBoxBytes, tu = tg + kBoxBytes;
+        const uint32_t tg = sbase + s * kGuStageBytes, tu = tg + kBoxBytes, tx = tu + kBoxBytes;
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           const int ch = ks * 4 + c;
           const uint4 a0 = lds128(tg + swz128(r0, ch)), a1 = lds128(tg + swz128(r1, ch));
           const uint4 b0 = lds128(tu + swz128(r0, ch)), b1 = lds128(tu + swz128(r1, ch));
-          const int kk = kc * kKC + ks * 32;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             if (q < ng) {
-              const uint4 xv = xp[q] ? ldg_keep(xp[q] + kk) : zero;
+              const uint4 xv = lds128(tx + uint32_t((q * 8 + g) * 128 + ch * 16));
               mma_k32(ag[q], a0, a1, xv);
               mma_k32(au[q], b0, b1, xv);
             }
@@ -184,16 +190,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// down + routing weight.  Unit = (expert, 64 output rows of down_proj);
+// down + routing weight.  Unit = (expert, 64 output rows of down_proj).  A
+// stage holds the 64x64 weight tile and the same 64 k of the pass's 32
+// dispatched rows of h (one TMA box; rows past the end read as zero).
 // rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
-    const __nv_bfloat16* __restrict__ h, ExpertTables tb, int H, int E, int I, int Is, int ldh,
+    const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
     float* __restrict__ rows, int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDnStages * kDnStageBytes);
   uint64_t* empty = full + kDnStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -211,16 +219,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     if (lane != 0) return;
     prefetch_tmap(&tm_dn);
     prefetch_tmap(&tm_sd);
+    prefetch_tmap(&tm_h);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int e = tb.active[u / UR], rb = u % UR;
       const bool sh = (e == E);
       const int nkc = (sh ? Is : I) / kKC;
-      const int n = tb.offsets[e + 1] - tb.offsets[e];
+      const int p0 = tb.offsets[e];
+      const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
       const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
-      for (int nb = 0; nb < n; nb += 32) {
+      for (int nb = 0; nb < n; nb += kActRows) {
         for (int kc = 0; kc < nkc; ++kc, ++it) {
           const int s = it % kDnStages;
           if (it >= uint32_t(kDnStages) && !mbar_wait(&empty[s], ((it / kDnStages) & 1) ^ 1)) {
@@ -228,8 +238,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
             drain(full, it, kDnStages);
             return;
           }
-          mbar_arrive_expect_tx(&full[s], kBoxBytes);
-          tma_load_2d_hint(smem + s * kBoxBytes, m, kc * kKC, row, &full[s], pol);
+          mbar_arrive_expect_tx(&full[s], kBoxBytes + kActBytes);
+          uint8_t* dst = smem + s * kDnStageBytes;
+          tma_load_2d_hint(dst, m, kc * kKC, row, &full[s], pol);
+          tma_load_2d(dst + kBoxBytes, &tm_h, kc * kKC, p0 + nb, &full[s]);
         }
       }
     }
@@ -239,7 +251,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
   const int cw = warp - 1, g = lane >> 2, c = lane & 3;
   const int r0 = cw * 16 + g, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
-  const uint4 zero = make_uint4(0, 0, 0, 0);
   uint32_t it = 0;
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int e = tb.active[u / UR], rb = u % UR;
@@ -247,13 +258,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const int nkc = (sh ? Is : I) / kKC;
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
-    for (int nb = 0; nb < n; nb += 32) {
-      const __nv_bfloat16* hp[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int i = nb + q * 8 + g;
-        hp[q] = i < n ? h + size_t(p0 + i) * ldh + 8 * c : nullptr;
-      }
+    for (int nb = 0; nb < n; nb += kActRows) {
       const int ng = min(4, (n - nb + 7) / 8);
       float acc[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
@@ -262,16 +267,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
           set_status(status, kStatusTimeoutFull);
           return;
         }
-        const uint32_t tw = sbase + s * kBoxBytes;
+        const uint32_t tw = sbase + s * kDnStageBytes, th = tw + kBoxBytes;
 #pragma unroll
         for (int ks = 0; ks < 2; ++ks) {
           const int ch = ks * 4 + c;
           const uint4 a0 = lds128(tw + swz128(r0, ch)), a1 = lds128(tw + swz128(r1, ch));
-          const int kk = kc * kKC + ks * 32;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             if (q < ng) {
-              const uint4 hv = hp[q] ? ldg_keep(hp[q] + kk) : zero;
+              const uint4 hv = lds128(th + swz128(q * 8 + g, ch));
               mma_k32(acc[q], a0, a1, hv);
             }
           }
@@ -335,10 +339,10 @@ static int g_num_sms = 148;
 cudaError_t stream_init(int num_sms) {
   g_num_sms = num_sms;
   cudaError_t e = cudaFuncSetAttribute(gate_up_tma_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kGuSmem);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(down_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kStreamSmem);
+                              kDnSmem);
 }
 
 cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
@@ -346,23 +350,26 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                                   const __nv_bfloat16* w_sh_down, const Workspace& ws,
                                   cudaStream_t st, void* mid_event) {
-  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd;
-  const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E;
+  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h;
+  const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
+  const uint64_t R = T * d.K + T, ldh = d.ldh;
   if (!make_tmap_bf16_2d(&tm_gu, w_gate_up, H, E * 2 * I, H * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_sg, w_sh_gate, H, Is, H * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_su, w_sh_up, H, Is, H * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kKC, kUnitRows) ||
-      !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kKC, kUnitRows))
+      !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kKC, kUnitRows) ||
+      !make_tmap_bf16_2d(&tm_x, x, H, T, H * 2, kKC, 1, /*swizzle128=*/false) ||
+      !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kKC, kActRows))
     return cudaErrorInvalidValue;
   ExpertTables tb{ws.active, ws.n_active, ws.offsets, ws.sorted_tok, ws.pair_dst, ws.pair_w};
-  gate_up_tma_kernel<<<g_num_sms, kStreamThreads, kStreamSmem, st>>>(
-      tm_gu, tm_sg, tm_su, x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.status + 1);
+  gate_up_tma_kernel<<<g_num_sms, kStreamThreads, kGuSmem, st>>>(
+      tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.status + 1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (e != cudaSuccess) return e;
   }
-  down_tma_kernel<<<g_num_sms, kStreamThreads, kStreamSmem, st>>>(
-      tm_dn, tm_sd, ws.h, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.rows, ws.status + 1);
+  down_tma_kernel<<<g_num_sms, kStreamThreads, kDnSmem, st>>>(
+      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, ws.rows, ws.status + 1);
   return cudaGetLastError();
 }
 

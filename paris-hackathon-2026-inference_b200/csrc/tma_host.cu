@@ -25,7 +25,8 @@ void resolve() {
 }  // namespace
 
 bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                       bool swizzle128) {
   std::call_once(g_once, resolve);
   if (!g_encode) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || row_stride_bytes % 16 != 0) return false;
@@ -35,7 +36,8 @@ bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint6
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
