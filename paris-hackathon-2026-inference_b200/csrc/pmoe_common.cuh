@@ -41,7 +41,7 @@ struct Dims {
 };
 
 // Token counts up to this use the single-launch routing kernel.
-constexpr int kFusedRouteMaxT = 128;
+constexpr int kFusedRouteMaxT = 64;
 
 inline Dims make_dims(int T, int H, int E, int K, int I, int Is) {
   Dims d{T, H, E, K, I, Is, 0, 0, 0};

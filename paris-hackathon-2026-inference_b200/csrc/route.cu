@@ -95,7 +95,7 @@ __device__ __forceinline__ void warp_topk(const float* row, bool round_logits, i
   for (int j = 0; j < 8; ++j) {
     const int e = j * 32 + lane;
     if (e < E) {
-      float v = __ldcg(row + e);
+      float v = row[e];
       if (round_logits) v = bf16_round(v);
       key[j] = (bf16_key(v) << 16) | uint32_t(0xFFFF - e);
     } else {
@@ -124,7 +124,7 @@ __device__ __forceinline__ void warp_topk(const float* row, bool round_logits, i
     topk_w[size_t(t) * K + lane] = ex / den;
     atomicAdd(&cnt[e], 1);
   }
-  if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-__ldcg(row + E)));
+  if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-row[E]));
 }
 
 // ---------------------------------------------------------------------------
@@ -208,7 +208,7 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
     for (int i = tid; i < nw * E; i += nthr) s_wcnt[i] = 0;
     __syncthreads();
     const int p = base + tid;
-    const int e = p < P ? __ldcg(topk_idx + p) : -1;
+    const int e = p < P ? topk_idx[p] : -1;
     const unsigned m = __match_any_sync(0xffffffffu, e);
     const int rank = __popc(m & lt_mask);
     if (e >= 0 && rank == 0) s_wcnt[warp * E + e] = __popc(m);
@@ -220,7 +220,7 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
       o.sorted_tok[pos] = p / K;
       o.sorted_slot[pos] = p % K;
       o.pair_dst[pos] = p;
-      o.pair_w[pos] = __ldcg(topk_w + p);
+      o.pair_w[pos] = topk_w[p];
     }
     __syncthreads();
     for (int ee = tid; ee < E; ee += nthr) {
@@ -233,16 +233,27 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
   for (int t = tid; t < T; t += nthr) {
     o.sorted_tok[P + t] = t;
     o.pair_dst[P + t] = P + t;
-    o.pair_w[P + t] = __ldcg(shared_gate + t);
+    o.pair_w[P + t] = shared_gate[t];
   }
 }
 
 // ---------------------------------------------------------------------------
 // Fused decode routing (T <= kFusedRouteMaxT), grid = (Rpad/16) * ceil(T/32)
-// CTAs of 256 threads.  `sync[0]` must be 0 on entry (the launcher clears it
-// with a memset node; the last CTA also resets it).
+// CTAs of 512 threads; the K dimension of each CTA's 16 x 32 logit tile is
+// split over its 16 warps and reduced in shared memory in a fixed order.
+// The last CTA (ticket in sync[0], which the launcher clears with a memset
+// node and the last CTA resets) stages all logits into shared memory with
+// one coherent bulk read, then runs top-k and the dispatch out of shared
+// memory, so its serial tail sees no global-memory latency.
 // ---------------------------------------------------------------------------
-constexpr int kFusedRouteThreads = 256;
+constexpr int kFusedRouteThreads = 512;
+constexpr int kFusedRouteWarps = kFusedRouteThreads / 32;
+
+size_t fused_route_smem_bytes(int T, int E, int K, int Rpad) {
+  return sizeof(float) * size_t(T) * Rpad + sizeof(int) * size_t(T) * K +
+         sizeof(float) * size_t(T) * K + sizeof(float) * T +
+         sizeof(int) * size_t(kFusedRouteWarps) * E;
+}
 
 __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_router,
@@ -250,13 +261,18 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     int hi, int with_shared, int with_routed, float* __restrict__ logits,
     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
     DispatchOut o, int32_t* __restrict__ sync) {
-  __shared__ float s_part[8][32][17];
+  __shared__ float s_part[kFusedRouteWarps][32][17];
   __shared__ int s_cnt[256], s_off[256], s_cur[256], s_wsum[32], s_tot[2], s_last;
-  __shared__ int s_wcnt[8 * 256];
+  extern __shared__ float s_dyn[];
+  float* s_lg = s_dyn;                                       // [T][Rpad]
+  int* s_idx = reinterpret_cast<int*>(s_lg + size_t(T) * Rpad);  // [T*K]
+  float* s_w = reinterpret_cast<float*>(s_idx + T * K);      // [T*K]
+  float* s_sg = s_w + T * K;                                  // [T]
+  int* s_wcnt = reinterpret_cast<int*>(s_sg + T);             // [warps][E]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int RG = Rpad / 16;
   const int rg = blockIdx.x % RG, tt = blockIdx.x / RG;
-  const int slice = H / 8;
+  const int slice = H / kFusedRouteWarps;
   float acc[4][4];
   router_tile(x, w_router, w_gvec, T, H, E, rg, tt, warp * slice, slice, acc);
 #pragma unroll
@@ -273,7 +289,7 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     if (t < T && r <= E) {
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += s_part[w][tl][rl];
+      for (int w = 0; w < kFusedRouteWarps; ++w) s += s_part[w][tl][rl];
       logits[size_t(t) * Rpad + r] = r < E ? bf16_round(s) : s;
     }
   }
@@ -283,14 +299,22 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // Rpad is a multiple of 16, so the [T][Rpad] block is a whole number of float4.
+  const float4* src = reinterpret_cast<const float4*>(logits);
+  float4* dst = reinterpret_cast<float4*>(s_lg);
+  for (int i = tid; i < T * Rpad / 4; i += kFusedRouteThreads) dst[i] = __ldcg(src + i);
   for (int e = tid; e < E; e += kFusedRouteThreads) s_cnt[e] = 0;
   __syncthreads();
-  for (int t = warp; t < T; t += kFusedRouteThreads / 32)
-    warp_topk(logits + size_t(t) * Rpad, false, t, E, K, topk_idx, topk_w, shared_gate, s_cnt);
-  __threadfence_block();
+  for (int t = warp; t < T; t += kFusedRouteWarps)
+    warp_topk(s_lg + size_t(t) * Rpad, false, t, E, K, s_idx, s_w, s_sg, s_cnt);
   __syncthreads();
-  block_dispatch(s_cnt, topk_idx, topk_w, shared_gate, T, E, K, lo, hi, with_shared, with_routed,
-                 o, s_off, s_cur, s_wsum, s_tot, s_wcnt);
+  block_dispatch(s_cnt, s_idx, s_w, s_sg, T, E, K, lo, hi, with_shared, with_routed, o, s_off,
+                 s_cur, s_wsum, s_tot, s_wcnt);
+  for (int i = tid; i < T * K; i += kFusedRouteThreads) {
+    topk_idx[i] = s_idx[i];
+    topk_w[i] = s_w[i];
+  }
+  for (int t = tid; t < T; t += kFusedRouteThreads) shared_gate[t] = s_sg[t];
   if (tid == 0) sync[0] = 0;
 }
 
@@ -364,7 +388,8 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
   cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
   if (d.T <= kFusedRouteMaxT) {
-    route_fused_kernel<<<RG * TT, kFusedRouteThreads, 0, st>>>(
+    route_fused_kernel<<<RG * TT, kFusedRouteThreads,
+                         fused_route_smem_bytes(d.T, d.E, d.K, d.Rpad), st>>>(
         x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, lo, hi, with_shared, with_routed,
         ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status);
     return cudaGetLastError();
@@ -381,8 +406,11 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
 }
 
 cudaError_t route_init() {
-  return cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(dispatch_smem_bytes(256)));
+  cudaError_t e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(dispatch_smem_bytes(256)));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(fused_route_smem_bytes(kFusedRouteMaxT, 256, 32, 272)));
 }
 
 }  // namespace pmoe

@@ -3,11 +3,13 @@
 // At T <= 64 each active expert sees a handful of tokens: the block is a
 // stream over ~1.4 GB of expert weights at a few FLOP/B.  Each persistent
 // CTA (one per SM) runs a warp-specialised pipeline:
-//   * warp 0, one lane: producer.  Walks this CTA's units and issues 2D TMA
-//     loads (128-byte swizzle, L2 evict-first) of 64-row x 64-column weight
-//     tiles, plus the matching 64-column slice of the activation rows, into
-//     an mbarrier ring of ~140 KiB, so that much is in flight per SM
-//     independent of register pressure;
+//   * warp 0, one lane: producer.  Takes work units from a global atomic
+//     queue (heaviest first: the shared expert sees every token), publishes
+//     each to the consumers through a small mbarrier ring, and issues 2D TMA
+//     loads (128-byte swizzle, L2 evict-first) of the unit's weight tiles --
+//     KCH k-chunks of 64 columns per stage, so each weight row contributes
+//     KCH*128 contiguous bytes per stage -- plus the matching slice of the
+//     activation rows, into a ~200 KiB mbarrier ring;
 //   * warps 1..4: consumers.  Each owns 16 weight rows of the tile, reads
 //     its mma.sync A and B fragments from shared memory with 128-bit loads,
 //     and releases the stage.
@@ -17,6 +19,8 @@
 // (modeling_qwen3_5_moe.py:743-749), the shared expert Qwen3_5MoeMLP
 // (:709-711) with its sigmoid gate (:788), and the routed combine of
 // engine/kernels/moe_grouped_mlp.py:152-163 (done here in fp32).
+#include <cstdlib>
+
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tma.cuh"
@@ -35,17 +39,25 @@ struct ExpertTables {
 constexpr int kConsumers = 4;
 constexpr int kStreamThreads = 32 * (kConsumers + 1);
 constexpr int kUnitRows = 16 * kConsumers;      // 64 weight rows per tile
-constexpr int kKC = 64;                         // k per tile (128-byte rows)
-constexpr int kBoxBytes = kUnitRows * kKC * 2;  // 8 KiB weight tile
+constexpr int kKC = 64;                         // k per tile chunk (128-byte rows)
+constexpr int kBoxBytes = kUnitRows * kKC * 2;  // 8 KiB weight tile chunk
 constexpr int kActRows = 32;                    // dispatched rows per pass
-constexpr int kActBytes = kActRows * kKC * 2;   // 4 KiB activation tile
-constexpr int kGuStageBytes = 2 * kBoxBytes + kActBytes;  // gate + up + x
-constexpr int kDnStageBytes = kBoxBytes + kActBytes;      // down + h
-constexpr int kGuStages = 7;
-constexpr int kDnStages = 11;
-constexpr int kGuSmem = kGuStages * kGuStageBytes + 2 * kGuStages * 8 + 1024;
-constexpr int kDnSmem = kDnStages * kDnStageBytes + 2 * kDnStages * 8 + 1024;
-static_assert(kGuStageBytes % 1024 == 0 && kDnStageBytes % 1024 == 0, "stage alignment");
+constexpr int kActChunkBytes = kActRows * kKC * 2;  // 4 KiB activation chunk
+constexpr int kRingBudget = 200 * 1024;
+constexpr int kUnitSlots = 4;
+
+template <int KCH>
+struct GuCfg {
+  static constexpr int kStageBytes = KCH * (2 * kBoxBytes + kActChunkBytes);
+  static constexpr int kStages = kRingBudget / kStageBytes > 16 ? 16 : kRingBudget / kStageBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 2 * kStages * 8 + 1024;
+};
+template <int KCH>
+struct DnCfg {
+  static constexpr int kStageBytes = KCH * (kBoxBytes + kActChunkBytes);
+  static constexpr int kStages = kRingBudget / kStageBytes > 16 ? 16 : kRingBudget / kStageBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 2 * kStages * 8 + 1024;
+};
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -60,36 +72,78 @@ __device__ __forceinline__ void drain(uint64_t* full, uint32_t issued, int stage
   for (uint32_t j = first; j < issued; ++j) mbar_wait(&full[j % stages], (j / stages) & 1);
 }
 
+// Work-unit hand-off from the producer lane to the consumer warps.
+struct UnitRing {
+  uint64_t full[kUnitSlots];
+  uint64_t empty[kUnitSlots];
+  int unit[kUnitSlots];
+
+  __device__ void init() {
+    for (int i = 0; i < kUnitSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumers);
+    }
+  }
+  // Producer: next unit from the global queue, heaviest (last) first; -1 = done.
+  __device__ bool publish(uint32_t ui, int* queue, int n_units, int* out_unit) {
+    const int slot = ui % kUnitSlots;
+    if (ui >= uint32_t(kUnitSlots) && !mbar_wait(&empty[slot], ((ui / kUnitSlots) & 1) ^ 1))
+      return false;
+    const int q = atomicAdd(queue, 1);
+    const int u = q < n_units ? n_units - 1 - q : -1;
+    unit[slot] = u;
+    mbar_arrive(&full[slot]);
+    *out_unit = u;
+    return true;
+  }
+  // Consumer warp: unit published in hand-off `ui`.
+  __device__ bool take(uint32_t ui, int lane, int* out_unit) {
+    const int slot = ui % kUnitSlots;
+    if (!mbar_wait(&full[slot], (ui / kUnitSlots) & 1)) return false;
+    const int u = unit[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    *out_unit = u;
+    return true;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // gate_up + SiLU*mul.  Unit = (expert, 64 intermediate columns j): the gate
 // rows j.. and the up rows I+j.. of that expert (shared expert: its own two
-// weight matrices).  A stage holds the 64x64 gate and up tiles (swizzled)
-// and the same 64 k of the pass's (up to 32) gathered token rows of x (one
-// unswizzled 128-byte TMA row each), all landed on one mbarrier.
+// weight matrices).  A stage holds KCH 64x64 gate and up tile chunks
+// (swizzled) and the same KCH*64 k of the pass's (up to 32) gathered token
+// rows of x (one unswizzled TMA row each), all landed on one mbarrier.
 // h[row, j] = bf16(silu(x.Wg_j) * (x.Wu_j)).
 // ---------------------------------------------------------------------------
+template <int KCH>
 __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_sg,
     const __grid_constant__ CUtensorMap tm_su, const __grid_constant__ CUtensorMap tm_x,
     ExpertTables tb, int H, int E, int I, int Is, int ldh, __nv_bfloat16* __restrict__ h,
-    int* __restrict__ status) {
+    int* __restrict__ status, int* __restrict__ queue) {
+  using C = GuCfg<KCH>;
+  constexpr int kStages = C::kStages;
+  constexpr int kXRow = KCH * kKC * 2;  // bytes of one staged x row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGuStages * kGuStageBytes);
-  uint64_t* empty = full + kGuStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint64_t* empty = full + kStages;
   __shared__ int s_tok[kActRows];
+  __shared__ UnitRing ur;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGuStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
+    ur.init();
     mbar_fence_init();
   }
   __syncthreads();
   const int UJ = (I > Is ? I : Is) / kUnitRows;
   const int n_units = tb.n_active[0] * UJ;
-  const int nkc = H / kKC;
+  const int nkc = H / (kKC * KCH);
 
   if (warp == 0) {
     if (lane != 0) return;
@@ -99,7 +153,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     prefetch_tmap(&tm_x);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (uint32_t ui = 0;; ++ui) {
+      int u;
+      if (!ur.publish(ui, queue, n_units, &u)) {
+        set_status(status, kStatusTimeoutEmpty);
+        drain(full, it, kStages);
+        return;
+      }
+      if (u < 0) break;
       const int e = tb.active[u / UJ], jb = u % UJ;
       const bool sh = (e == E);
       if (jb * kUnitRows >= (sh ? Is : I)) continue;
@@ -113,18 +174,23 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
         const int nr = min(kActRows, n - nb);
         for (int i = 0; i < nr; ++i) s_tok[i] = tb.sorted_tok[p0 + nb + i];
         for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int s = it % kGuStages;
-          if (it >= uint32_t(kGuStages) && !mbar_wait(&empty[s], ((it / kGuStages) & 1) ^ 1)) {
+          const int s = it % kStages;
+          if (it >= uint32_t(kStages) && !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1)) {
             set_status(status, kStatusTimeoutEmpty);
-            drain(full, it, kGuStages);
+            drain(full, it, kStages);
             return;
           }
-          mbar_arrive_expect_tx(&full[s], 2 * kBoxBytes + nr * kKC * 2);
-          uint8_t* dst = smem + s * kGuStageBytes;
-          tma_load_2d_hint(dst, mg, kc * kKC, rg, &full[s], pol);
-          tma_load_2d_hint(dst + kBoxBytes, mu, kc * kKC, ru, &full[s], pol);
-          uint8_t* xd = dst + 2 * kBoxBytes;
-          for (int i = 0; i < nr; ++i) tma_load_2d(xd + i * kKC * 2, &tm_x, kc * kKC, s_tok[i], &full[s]);
+          mbar_arrive_expect_tx(&full[s], KCH * 2 * kBoxBytes + nr * kXRow);
+          uint8_t* dst = smem + s * C::kStageBytes;
+#pragma unroll
+          for (int j = 0; j < KCH; ++j) {
+            const int k = (kc * KCH + j) * kKC;
+            tma_load_2d_hint(dst + j * kBoxBytes, mg, k, rg, &full[s], pol);
+            tma_load_2d_hint(dst + (KCH + j) * kBoxBytes, mu, k, ru, &full[s], pol);
+          }
+          uint8_t* xd = dst + 2 * KCH * kBoxBytes;
+          for (int i = 0; i < nr; ++i)
+            tma_load_2d(xd + i * kXRow, &tm_x, kc * KCH * kKC, s_tok[i], &full[s]);
         }
       }
     }
@@ -136,7 +202,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
   const int r0 = cw * 16 + g, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
   uint32_t it = 0;
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+  for (uint32_t ui = 0;; ++ui) {
+    int u;
+    if (!ur.take(ui, lane, &u)) {
+      set_status(status, kStatusTimeoutFull);
+      return;
+    }
+    if (u < 0) break;
     const int e = tb.active[u / UJ], jb = u % UJ;
     const bool sh = (e == E);
     if (jb * kUnitRows >= (sh ? Is : I)) continue;
@@ -146,23 +218,28 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
       const int ng = min(4, (n - nb + 7) / 8);  // warp-uniform
       float ag[4][4] = {}, au[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
-        const int s = it % kGuStages;
-        if (!mbar_wait(&full[s], (it / kGuStages) & 1)) {
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1)) {
           set_status(status, kStatusTimeoutFull);
           return;
         }
-        const uint32_t tg = sbase + s * kGuStageBytes, tu = tg + kBoxBytes, tx = tu + kBoxBytes;
+        const uint32_t st0 = sbase + s * C::kStageBytes;
+        const uint32_t tx = st0 + 2 * KCH * kBoxBytes;
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const int ch = ks * 4 + c;
-          const uint4 a0 = lds128(tg + swz128(r0, ch)), a1 = lds128(tg + swz128(r1, ch));
-          const uint4 b0 = lds128(tu + swz128(r0, ch)), b1 = lds128(tu + swz128(r1, ch));
+        for (int j = 0; j < KCH; ++j) {
+          const uint32_t tg = st0 + j * kBoxBytes, tu = st0 + (KCH + j) * kBoxBytes;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (q < ng) {
-              const uint4 xv = lds128(tx + uint32_t((q * 8 + g) * 128 + ch * 16));
-              mma_k32(ag[q], a0, a1, xv);
-              mma_k32(au[q], b0, b1, xv);
+          for (int ks = 0; ks < 2; ++ks) {
+            const int ch = ks * 4 + c;
+            const uint4 a0 = lds128(tg + swz128(r0, ch)), a1 = lds128(tg + swz128(r1, ch));
+            const uint4 b0 = lds128(tu + swz128(r0, ch)), b1 = lds128(tu + swz128(r1, ch));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (q < ng) {
+                const uint4 xv = lds128(tx + uint32_t((q * 8 + g) * kXRow + j * 128 + ch * 16));
+                mma_k32(ag[q], a0, a1, xv);
+                mma_k32(au[q], b0, b1, xv);
+              }
             }
           }
         }
@@ -191,24 +268,29 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
 
 // ---------------------------------------------------------------------------
 // down + routing weight.  Unit = (expert, 64 output rows of down_proj).  A
-// stage holds the 64x64 weight tile and the same 64 k of the pass's 32
-// dispatched rows of h (one TMA box; rows past the end read as zero).
-// rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
+// stage holds KCH 64x64 weight tile chunks and the same k of the pass's 32
+// dispatched rows of h (one swizzled box per chunk; rows past the end of h
+// read as zero).  rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
 // ---------------------------------------------------------------------------
+template <int KCH>
 __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
     const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
-    float* __restrict__ rows, int* __restrict__ status) {
+    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue) {
+  using C = DnCfg<KCH>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDnStages * kDnStageBytes);
-  uint64_t* empty = full + kDnStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint64_t* empty = full + kStages;
+  __shared__ UnitRing ur;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDnStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
+    ur.init();
     mbar_fence_init();
   }
   __syncthreads();
@@ -222,26 +304,37 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     prefetch_tmap(&tm_h);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (uint32_t ui = 0;; ++ui) {
+      int u;
+      if (!ur.publish(ui, queue, n_units, &u)) {
+        set_status(status, kStatusTimeoutEmpty);
+        drain(full, it, kStages);
+        return;
+      }
+      if (u < 0) break;
       const int e = tb.active[u / UR], rb = u % UR;
       const bool sh = (e == E);
-      const int nkc = (sh ? Is : I) / kKC;
+      const int nkc = (sh ? Is : I) / (kKC * KCH);
       const int p0 = tb.offsets[e];
       const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
       const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
       for (int nb = 0; nb < n; nb += kActRows) {
         for (int kc = 0; kc < nkc; ++kc, ++it) {
-          const int s = it % kDnStages;
-          if (it >= uint32_t(kDnStages) && !mbar_wait(&empty[s], ((it / kDnStages) & 1) ^ 1)) {
+          const int s = it % kStages;
+          if (it >= uint32_t(kStages) && !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1)) {
             set_status(status, kStatusTimeoutEmpty);
-            drain(full, it, kDnStages);
+            drain(full, it, kStages);
             return;
           }
-          mbar_arrive_expect_tx(&full[s], kBoxBytes + kActBytes);
-          uint8_t* dst = smem + s * kDnStageBytes;
-          tma_load_2d_hint(dst, m, kc * kKC, row, &full[s], pol);
-          tma_load_2d(dst + kBoxBytes, &tm_h, kc * kKC, p0 + nb, &full[s]);
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          uint8_t* dst = smem + s * C::kStageBytes;
+#pragma unroll
+          for (int j = 0; j < KCH; ++j) {
+            const int k = (kc * KCH + j) * kKC;
+            tma_load_2d_hint(dst + j * kBoxBytes, m, k, row, &full[s], pol);
+            tma_load_2d(dst + KCH * kBoxBytes + j * kActChunkBytes, &tm_h, k, p0 + nb, &full[s]);
+          }
         }
       }
     }
@@ -252,31 +345,42 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
   const int r0 = cw * 16 + g, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
   uint32_t it = 0;
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+  for (uint32_t ui = 0;; ++ui) {
+    int u;
+    if (!ur.take(ui, lane, &u)) {
+      set_status(status, kStatusTimeoutFull);
+      return;
+    }
+    if (u < 0) break;
     const int e = tb.active[u / UR], rb = u % UR;
     const bool sh = (e == E);
-    const int nkc = (sh ? Is : I) / kKC;
+    const int nkc = (sh ? Is : I) / (kKC * KCH);
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
     for (int nb = 0; nb < n; nb += kActRows) {
       const int ng = min(4, (n - nb + 7) / 8);
       float acc[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
-        const int s = it % kDnStages;
-        if (!mbar_wait(&full[s], (it / kDnStages) & 1)) {
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1)) {
           set_status(status, kStatusTimeoutFull);
           return;
         }
-        const uint32_t tw = sbase + s * kDnStageBytes, th = tw + kBoxBytes;
+        const uint32_t st0 = sbase + s * C::kStageBytes;
 #pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          const int ch = ks * 4 + c;
-          const uint4 a0 = lds128(tw + swz128(r0, ch)), a1 = lds128(tw + swz128(r1, ch));
+        for (int j = 0; j < KCH; ++j) {
+          const uint32_t tw = st0 + j * kBoxBytes;
+          const uint32_t th = st0 + KCH * kBoxBytes + j * kActChunkBytes;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (q < ng) {
-              const uint4 hv = lds128(th + swz128(q * 8 + g, ch));
-              mma_k32(acc[q], a0, a1, hv);
+          for (int ks = 0; ks < 2; ++ks) {
+            const int ch = ks * 4 + c;
+            const uint4 a0 = lds128(tw + swz128(r0, ch)), a1 = lds128(tw + swz128(r1, ch));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (q < ng) {
+                const uint4 hv = lds128(th + swz128(q * 8 + g, ch));
+                mma_k32(acc[q], a0, a1, hv);
+              }
             }
           }
         }
@@ -334,15 +438,44 @@ __global__ void __launch_bounds__(256) combine_kernel(
   reinterpret_cast<uint2*>(y + size_t(t) * H)[c4] = packed;
 }
 
-static int g_num_sms = 148;
+namespace {
+int g_num_sms = 148;
+int g_kch_gu = 2;  // k-chunks per gate_up stage
+int g_kch_dn = 2;  // k-chunks per down stage
+
+template <int KCH>
+cudaError_t set_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(gate_up_tma_kernel<KCH>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GuCfg<KCH>::kSmem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(down_tma_kernel<KCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              DnCfg<KCH>::kSmem);
+}
+
+int env_kch(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  if (!v) return dflt;
+  const int k = std::atoi(v);
+  return (k == 1 || k == 2 || k == 4) ? k : dflt;
+}
+
+// Largest supported chunk count <= want that divides every k extent.
+int fit_kch(int want, int k1, int k2) {
+  for (int k = want; k > 1; k >>= 1)
+    if (k1 % (kKC * k) == 0 && k2 % (kKC * k) == 0) return k;
+  return 1;
+}
+}  // namespace
 
 cudaError_t stream_init(int num_sms) {
   g_num_sms = num_sms;
-  cudaError_t e = cudaFuncSetAttribute(gate_up_tma_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kGuSmem);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(down_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kDnSmem);
+  g_kch_gu = env_kch("PMOE_STREAM_KCH_GU", g_kch_gu);
+  g_kch_dn = env_kch("PMOE_STREAM_KCH_DN", g_kch_dn);
+  cudaError_t e = set_attrs<1>();
+  if (e == cudaSuccess) e = set_attrs<2>();
+  if (e == cudaSuccess) e = set_attrs<4>();
+  return e;
 }
 
 cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
@@ -350,6 +483,8 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                                   const __nv_bfloat16* w_sh_down, const Workspace& ws,
                                   cudaStream_t st, void* mid_event) {
+  const int kg = fit_kch(g_kch_gu, d.H, d.H);
+  const int kd = fit_kch(g_kch_dn, d.I, d.Is);
   CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h;
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t R = T * d.K + T, ldh = d.ldh;
@@ -358,18 +493,25 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       !make_tmap_bf16_2d(&tm_su, w_sh_up, H, Is, H * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kKC, kUnitRows) ||
-      !make_tmap_bf16_2d(&tm_x, x, H, T, H * 2, kKC, 1, /*swizzle128=*/false) ||
+      !make_tmap_bf16_2d(&tm_x, x, H, T, H * 2, kKC * kg, 1, /*swizzle128=*/false) ||
       !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kKC, kActRows))
     return cudaErrorInvalidValue;
   ExpertTables tb{ws.active, ws.n_active, ws.offsets, ws.sorted_tok, ws.pair_dst, ws.pair_w};
-  gate_up_tma_kernel<<<g_num_sms, kStreamThreads, kGuSmem, st>>>(
-      tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.status + 1);
+  int* status = ws.status + 1;
+#define PMOE_GU(KCH)                                                                  \
+  gate_up_tma_kernel<KCH><<<g_num_sms, kStreamThreads, GuCfg<KCH>::kSmem, st>>>(      \
+      tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
+#define PMOE_DN(KCH)                                                                  \
+  down_tma_kernel<KCH><<<g_num_sms, kStreamThreads, DnCfg<KCH>::kSmem, st>>>(         \
+      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, ws.rows, status, ws.status + 3)
+  if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (e != cudaSuccess) return e;
   }
-  down_tma_kernel<<<g_num_sms, kStreamThreads, kDnSmem, st>>>(
-      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, ws.rows, ws.status + 1);
+  if (kd == 4) PMOE_DN(4); else if (kd == 2) PMOE_DN(2); else PMOE_DN(1);
+#undef PMOE_GU
+#undef PMOE_DN
   return cudaGetLastError();
 }
 
