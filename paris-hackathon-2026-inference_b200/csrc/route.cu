@@ -272,9 +272,12 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int RG = Rpad / 16;
   const int rg = blockIdx.x % RG, tt = blockIdx.x / RG;
-  const int slice = H / kFusedRouteWarps;
+  // K slices are whole 32-column steps; with small H the trailing warps get
+  // an empty slice and contribute zeros.
+  const int slice = (H / kFusedRouteWarps + 31) / 32 * 32;
+  const int k_begin = min(H, warp * slice);
   float acc[4][4];
-  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, warp * slice, slice, acc);
+  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, k_begin, min(slice, H - k_begin), acc);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     s_part[warp][q * 8 + 2 * c][g] = acc[q][0];

@@ -440,8 +440,8 @@ __global__ void __launch_bounds__(256) combine_kernel(
 
 namespace {
 int g_num_sms = 148;
-int g_kch_gu = 2;  // k-chunks per gate_up stage
-int g_kch_dn = 2;  // k-chunks per down stage
+int g_kch_gu = 4;  // k-chunks per gate_up stage (512 B per weight row)
+int g_kch_dn = 4;  // k-chunks per down stage
 
 template <int KCH>
 cudaError_t set_attrs() {
