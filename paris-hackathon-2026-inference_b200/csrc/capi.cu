@@ -26,6 +26,7 @@ int ensure_device() {
   if (prop.major != 10) return PMOE_ERR_DEVICE;
   if (route_init() != cudaSuccess) return PMOE_ERR_CUDA;
   if (stream_init(prop.multiProcessorCount) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (tc_init(prop.multiProcessorCount) != cudaSuccess) return PMOE_ERR_CUDA;
   g_dev_sms[dev] = prop.multiProcessorCount;
   g_dev_ready[dev] = true;
   return PMOE_OK;
@@ -131,6 +132,12 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int with_shared = (flags & PMOE_F_SHARED) ? 1 : 0;
   const int with_routed = (flags & PMOE_F_ROUTED) ? 1 : 0;
+  if ((flags & PMOE_F_FORCE_TC) && (flags & PMOE_F_FORCE_STREAM)) return PMOE_ERR_ARG;
+  if ((flags & PMOE_F_FORCE_TC) && !tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
+  // Weight streaming while the layer is HBM-bound (decode), tcgen05 grouped
+  // GEMMs beyond.
+  const bool use_tc = (flags & PMOE_F_FORCE_TC) ||
+                      (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d));
   auto mark = [&](int i) {
     if (events && i < n_events && events[i])
       return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -141,6 +148,14 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
                    with_routed, ws, st) != cudaSuccess)
     return PMOE_ERR_CUDA;
   if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (use_tc) {
+    if (launch_tc_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
+                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), st,
+                          events && n_events > 2 ? events[2] : nullptr) != cudaSuccess)
+      return PMOE_ERR_CUDA;
+    if (mark(3) != cudaSuccess || mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
+    return PMOE_OK;
+  }
   if (launch_stream_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                             bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr)
       != cudaSuccess)

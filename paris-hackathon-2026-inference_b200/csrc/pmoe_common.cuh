@@ -27,7 +27,11 @@ struct Workspace {
   float* logit_part;    // [T][Rpad]   router logits (bf16-rounded) + raw shared-gate sum
   int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
-  float* rows;          // [T*K+T][H] weighted expert outputs, token-major
+  float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
+  int4* gu_tiles;       // tensor-core path tile lists: (expert, row0, nrows, n_block)
+  int4* dn_tiles;
+  int32_t* tile_counts; // [2]
+  float* y_acc;         // [T][H]     fp32 output accumulator (tensor-core path)
   size_t bytes;
 };
 
@@ -72,6 +76,12 @@ inline Workspace carve(void* base, const Dims& d) {
   w.status = (int32_t*)take(sizeof(int32_t) * 8);
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
   w.rows = (float*)take(sizeof(float) * R * d.H);
+  const size_t mt_max = R / 128 + d.E + 2;  // M tiles over all experts, partial ones included
+  const int imax = d.I > d.Is ? d.I : d.Is;
+  w.gu_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(imax / 128 + 1));
+  w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 256 + 1));
+  w.tile_counts = (int32_t*)take(sizeof(int32_t) * 4);
+  w.y_acc = (float*)take(sizeof(float) * size_t(d.T) * d.H);
   w.bytes = off;
   return w;
 }

@@ -119,3 +119,58 @@ def test_block_prefill_zipf_streaming(full):
     rows.sort()
     assert_close(y.float().cpu().numpy()[rows], oracle_y(x, wts, route=route, rows=rows),
                  "T=8192 sample")
+
+
+# ---- tcgen05 grouped-GEMM path (prefill) -----------------------------------
+
+TC_SHAPE = dict(H=256, E=16, K=4, I=128, Is=128)
+
+
+@pytest.mark.parametrize("T", [1, 5, 64, 200, 777])
+def test_block_tc_small_shape(T):
+    """Forced tensor-core path on a small shape: ragged M tiles, empty experts."""
+    from paris_moe_b200 import workload as W
+    sh = W.MoEShape(**TC_SHAPE)
+    wts = W.make_weights(sh, seed=21)
+    x = W.make_hidden(T, sh, seed=21)
+    g = wts.to("cuda")
+    xg = x.cuda()
+    y = block(xg, g, flags=F_SH | F_RT | F_TC)
+    route = route_of(xg, g)
+    assert_close(y, oracle_y(x, wts, route=route), f"tc T={T}")
+
+
+def test_block_tc_partials(full):
+    """Forced tensor-core path, EP partial + shared-only at the full shape."""
+    wts, g, x = full
+    xg = x[:48].cuda()
+    route = route_of(xg, g)
+    p0 = block(xg, g, 0, 100, F_RT | F_TC)
+    assert_close(p0, oracle_y(x[:48], wts, route=route, expert_range=(0, 100),
+                              with_shared=False), "tc rank partial")
+    sh = block(xg, g, 0, 0, F_SH | F_TC)
+    assert_close(sh, oracle_y(x[:48], wts, route=route, expert_range=(0, 0)), "tc shared")
+
+
+def test_block_tc_matches_stream(full):
+    """Both expert paths agree at the full shape (T=64 decode batch)."""
+    wts, g, x = full
+    xg = x.cuda()
+    a = block(xg, g, flags=F_SH | F_RT | F_TC).float().cpu().numpy()
+    b = block(xg, g, flags=F_SH | F_RT | F_STREAM).float().cpu().numpy()
+    assert O.rel_l2(a, b) < 3e-3
+
+
+def test_block_prefill_zipf_tc():
+    """Default path at T=8192 (tensor cores), skewed routing; 256 sampled rows."""
+    from paris_moe_b200 import workload as W
+    wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=1.1)
+    g = wts.to("cuda")
+    x = W.make_hidden(8192, W.MoEShape(), seed=0, zipf=True)
+    xg = x.cuda()
+    y = block(xg, g)
+    route = route_of(xg, g)
+    rows = np.random.default_rng(1).choice(8192, 256, replace=False)
+    rows.sort()
+    assert_close(y.float().cpu().numpy()[rows], oracle_y(x, wts, route=route, rows=rows),
+                 "tc T=8192 sample")
