@@ -170,6 +170,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--T", type=int, default=64)
+    ap.add_argument("--zipf", type=float, default=None,
+                    help="Zipf(s) prior on the router logits (skewed prefill routing)")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
@@ -184,9 +186,11 @@ def main():
     PM = load_package()
     from paris_moe_b200 import workload as W
 
-    metric = f"MoE layer tokens/s (decode T={a.T})"
-    config = {"workload": f"Qwen3.5-35B-A3B MoE block, decode T={a.T}, near-uniform routing "
-                          "(BASELINE configs[1])",
+    regime = "decode" if a.T <= 64 else "prefill"
+    metric = f"MoE layer tokens/s ({regime} T={a.T})"
+    routing = (f"Zipf(s={a.zipf}) skewed routing (BASELINE configs[2])" if a.zipf
+               else "near-uniform routing (BASELINE configs[1])")
+    config = {"workload": f"Qwen3.5-35B-A3B MoE block, {regime} T={a.T}, {routing}",
               "T": a.T, "hidden": 2048, "experts": 256, "top_k": 8, "moe_ffn": 512,
               "shared_ffn": 512, "parallelism": f"ep{world}" if world > 1 else "single",
               "l2": "weights (1.5 GB) > L2 (126 MB): streamed from HBM every step"}
@@ -194,8 +198,8 @@ def main():
     if a.impl == "reference":
         if rank != 0:
             return
-        wts = W.make_weights(W.MoEShape(), seed=0)
-        x = W.make_hidden(a.T, W.MoEShape(), seed=0)
+        wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=a.zipf)
+        x = W.make_hidden(a.T, W.MoEShape(), seed=0, zipf=a.zipf is not None)
         ref = cpu_reference(wts, x, budget_s=1e9, max_steps=a.steps + 0)
         line = {"metric": metric, "value": ref["value"], "unit": "tokens/s", "n_gpus": a.gpus,
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": ref["ms_per_call"],
@@ -216,8 +220,8 @@ def main():
     lib = _lib.load()
 
     shape = W.MoEShape()
-    wts = W.make_weights(shape, seed=0, device=dev)
-    x = W.make_hidden(a.T, shape, seed=0, device=dev)
+    wts = W.make_weights(shape, seed=0, device=dev, zipf_s=a.zipf)
+    x = W.make_hidden(a.T, shape, seed=0, device=dev, zipf=a.zipf is not None)
     E = shape.E
     lo, hi = rank * E // world, (rank + 1) * E // world
     flags = _lib.PMOE_F_ROUTED | (_lib.PMOE_F_SHARED if rank == 0 else 0)

@@ -27,6 +27,7 @@ int ensure_device() {
   if (route_init() != cudaSuccess) return PMOE_ERR_CUDA;
   if (stream_init(prop.multiProcessorCount) != cudaSuccess) return PMOE_ERR_CUDA;
   if (tc_init(prop.multiProcessorCount) != cudaSuccess) return PMOE_ERR_CUDA;
+  if (route_tc_init() != cudaSuccess) return PMOE_ERR_CUDA;
   g_dev_sms[dev] = prop.multiProcessorCount;
   g_dev_ready[dev] = true;
   return PMOE_OK;
@@ -91,8 +92,11 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
   Workspace ws = carve(workspace, d);
   if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st) != cudaSuccess)
-    return PMOE_ERR_CUDA;
+  const bool route_tc = T > kFusedRouteMaxT && route_tc_supported(d);
+  const cudaError_t rerr =
+      route_tc ? launch_route_tc(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st)
+               : launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st);
+  if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   const size_t P = size_t(T) * K;
   auto cp = [&](void* dst, const void* src, size_t n) {
     return dst ? cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, st) : cudaSuccess;
@@ -144,13 +148,19 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
     return cudaSuccess;
   };
   if (mark(0) != cudaSuccess) return PMOE_ERR_CUDA;
-  if (launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi, with_shared,
-                   with_routed, ws, st) != cudaSuccess)
-    return PMOE_ERR_CUDA;
+  // Prefill-sized batches route on the tensor cores (that path also zeroes
+  // the fp32 accumulator of the expert GEMMs).
+  const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
+  const cudaError_t rerr =
+      route_tc ? launch_route_tc(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+                                 with_shared, with_routed, ws, st)
+               : launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+                              with_shared, with_routed, ws, st);
+  if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     if (launch_tc_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
-                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), st,
+                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), !route_tc, st,
                           events && n_events > 2 ? events[2] : nullptr) != cudaSuccess)
       return PMOE_ERR_CUDA;
     if (mark(3) != cudaSuccess || mark(4) != cudaSuccess) return PMOE_ERR_CUDA;

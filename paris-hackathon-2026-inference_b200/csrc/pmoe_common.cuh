@@ -32,6 +32,8 @@ struct Workspace {
   int4* dn_tiles;
   int32_t* tile_counts; // [2]
   float* y_acc;         // [T][H]     fp32 output accumulator (tensor-core path)
+  int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
+  int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
 };
 
@@ -82,6 +84,9 @@ inline Workspace carve(void* base, const Dims& d) {
   w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 256 + 1));
   w.tile_counts = (int32_t*)take(sizeof(int32_t) * 4);
   w.y_acc = (float*)take(sizeof(float) * size_t(d.T) * d.H);
+  const size_t ntile = (size_t(d.T) + 127) / 128;
+  w.hist = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
+  w.hist_base = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
   w.bytes = off;
   return w;
 }

@@ -23,7 +23,16 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, cudaStream_t st, void* mid_event);
+                              __nv_bfloat16* y, bool zero_acc, cudaStream_t st,
+                              void* mid_event);
+
+// Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
+// stable dispatch); also zeroes the fp32 output accumulator.
+cudaError_t route_tc_init();
+bool route_tc_supported(const Dims& d);
+cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                            const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
+                            int with_routed, const Workspace& ws, cudaStream_t st);
 
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
                            int with_routed, __nv_bfloat16* y, cudaStream_t st);

@@ -1,0 +1,354 @@
+// Prefill routing (large T): tcgen05 router GEMM with top-k in the epilogue,
+// then a parallel stable CSR dispatch.
+//
+//   router_tc_kernel   one CTA per 128-token tile: logits = x . W_r^T on the
+//                      tensor cores (M=128 tokens, N=256 experts) plus the
+//                      shared-expert gate as a second N=16 MMA whose B tile
+//                      is w_sh_gvec with TMA zero-filling rows 1..15.  The
+//                      epilogue (one token per thread) rounds each logit to
+//                      bf16, keeps the top K keys in registers (ties -> lower
+//                      expert), renormalises, and writes the tile's
+//                      per-expert histogram.
+//   route_scan_kernel  one CTA: per-expert counts, CSR offsets, active list
+//                      and, per (tile, expert), the first output slot.
+//   route_scatter_kernel  one CTA per tile: stable ranks of the tile's pairs
+//                      within their expert (pair order kept, as the stable
+//                      torch.sort of engine/kernels/moe_dispatch.py:129), the
+//                      permuted rows, the shared-expert rows, and zeroes the
+//                      tile's rows of the fp32 output accumulator.
+// Reference: Qwen3_5MoeTopKRouter.forward (modeling_qwen3_5_moe.py:762-770).
+#include "pmoe_common.cuh"
+#include "pmoe_kernels.cuh"
+#include "pmoe_tc.cuh"
+
+namespace pmoe {
+
+constexpr int kRtM = 128, kRtN = 256, kRtN2 = 16, kRtK = 64;
+constexpr int kRtStages = 4;
+constexpr int kRtA = kRtM * kRtK * 2;     // 16 KiB
+constexpr int kRtB = kRtN * kRtK * 2;     // 32 KiB
+constexpr int kRtB2 = kRtN2 * kRtK * 2;   // 2 KiB
+constexpr int kRtStageBytes = kRtA + kRtB + kRtB2;
+constexpr int kRtSmem = kRtStages * kRtStageBytes + 1024 + 256;
+constexpr int kRtThreads = 6 * 32;
+constexpr int kRtMaxK = 8;
+static_assert(kRtStageBytes % 1024 == 0, "stage alignment");
+
+__device__ __forceinline__ uint32_t rt_key(float v, int e) {
+  uint32_t b = __float_as_uint(v) >> 16;  // v is bf16-exact
+  if (b == 0x8000u) b = 0;
+  b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (b << 16) | uint32_t(0xFFFF - e);
+}
+__device__ __forceinline__ float rt_value(uint32_t key) {
+  const uint32_t s = key >> 16;
+  const uint32_t b = (s & 0x8000u) ? (s & 0x7FFFu) : (~s & 0xFFFFu);
+  return __uint_as_float(b << 16);
+}
+
+__global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+    const __grid_constant__ CUtensorMap tm_g, int T, int H, int E, int K,
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
+    int32_t* __restrict__ hist, int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRtStages * kRtStageBytes);
+  uint64_t* empty = full + kRtStages;
+  uint64_t* tfull = empty + kRtStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  __shared__ int s_hist[256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kRtM;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_fence_init();
+  }
+  for (int i = threadIdx.x; i < 256; i += kRtThreads) s_hist[i] = 0;
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nk = H / kRtK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc % kRtStages;
+        if (kc >= kRtStages && !mbar_wait(&empty[s], ((kc / kRtStages) & 1) ^ 1)) {
+          atomicCAS(status, 0, kStatusTimeoutEmpty);
+          break;
+        }
+        uint8_t* sa = smem + s * kRtStageBytes;
+        mbar_arrive_expect_tx(&full[s], kRtStageBytes);
+        tma_load_2d(sa, &tm_x, kc * kRtK, t0, &full[s]);
+        tma_load_2d(sa + kRtA, &tm_w, kc * kRtK, 0, &full[s]);
+        tma_load_2d(sa + kRtA + kRtB, &tm_g, kc * kRtK, 0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id1 = idesc_bf16_f32(kRtM, kRtN), id2 = idesc_bf16_f32(kRtM, kRtN2);
+      const uint32_t sb0 = smem_u32(smem);
+      bool ok = true;
+      for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc % kRtStages;
+        if (!mbar_wait(&full[s], (kc / kRtStages) & 1)) {
+          atomicCAS(status, 0, kStatusTimeoutFull);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = sb0 + s * kRtStageBytes;
+        const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + kRtA),
+                       gd = sdesc_k_sw128(sa + kRtA + kRtB);
+#pragma unroll
+        for (int kk = 0; kk < kRtK / 16; ++kk) {
+          const uint32_t acc = (kc | kk) != 0 ? 1u : 0u;
+          umma_bf16(tmem_base, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), id1, acc);
+          umma_bf16(tmem_base + kRtN, ad + uint64_t(kk * 2), gd + uint64_t(kk * 2), id2, acc);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(tfull);
+    }
+  } else {
+    // epilogue: warps 2..5, one token row per thread
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int t = t0 + r;
+    if (mbar_wait(tfull, 0)) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16);
+      uint32_t top[kRtMaxK];
+#pragma unroll
+      for (int k = 0; k < kRtMaxK; ++k) top[k] = 0u;
+#pragma unroll 1
+      for (int cc = 0; cc < kRtN / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(taddr + cc * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int e = cc * 32 + i;
+          if (e < E) {
+            const uint32_t key = rt_key(bf16_round(__uint_as_float(v[i])), e);
+            if (key > top[kRtMaxK - 1]) {
+              top[kRtMaxK - 1] = key;
+#pragma unroll
+              for (int k = kRtMaxK - 1; k > 0; --k) {
+                if (top[k] > top[k - 1]) {
+                  const uint32_t tmp = top[k];
+                  top[k] = top[k - 1];
+                  top[k - 1] = tmp;
+                }
+              }
+            }
+          }
+        }
+      }
+      uint32_t gv[32];
+      tmem_ld32(taddr + kRtN, gv);
+      tmem_ld_wait();
+      if (t < T) {
+        const float l0 = rt_value(top[0]);
+        float ex[kRtMaxK], den = 0.f;
+#pragma unroll
+        for (int k = 0; k < kRtMaxK; ++k) {
+          ex[k] = k < K ? __expf(rt_value(top[k]) - l0) : 0.f;
+          den += ex[k];
+        }
+        const float inv = 1.0f / den;
+#pragma unroll
+        for (int k = 0; k < kRtMaxK; ++k) {
+          if (k < K) {
+            const int e = 0xFFFF - int(top[k] & 0xFFFFu);
+            topk_idx[size_t(t) * K + k] = e;
+            topk_w[size_t(t) * K + k] = ex[k] * inv;
+            atomicAdd(&s_hist[e], 1);
+          }
+        }
+        shared_gate[t] = 1.0f / (1.0f + __expf(-__uint_as_float(gv[0])));
+      }
+    } else {
+      atomicCAS(status, 0, kStatusTimeoutTmem);
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kRtThreads) hist[size_t(blockIdx.x) * E + e] = s_hist[e];
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA of 1024 threads.  Thread (e, part) sums its quarter of the tile
+// histograms; counts -> CSR offsets and active list (as block_dispatch), and
+// base[b][e] = offsets[e] + sum_{b' < b} hist[b'][e].
+// ---------------------------------------------------------------------------
+constexpr int kScanThreads = 1024;
+
+__device__ int scan_block_excl(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int s = warp_sums[lane];
+    int si = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, si, o);
+      if (lane >= o) si += n;
+    }
+    warp_sums[lane] = si - s;
+    if (lane == 31) *total = si;
+  }
+  __syncthreads();
+  const int r = warp_sums[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
+    const int32_t* __restrict__ hist, int nb, int T, int E, int K, int lo, int hi,
+    int with_shared, int with_routed, int32_t* __restrict__ base, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ active, int32_t* __restrict__ n_active) {
+  __shared__ int s_part[4][256];
+  __shared__ int s_cnt[256], s_off[256], s_wsum[32], s_tot;
+  const int tid = threadIdx.x;
+  const int e = tid & 255, part = tid >> 8;  // 4 parts of the tile range
+  const int b0 = part * nb / 4, b1 = (part + 1) * nb / 4;
+  int sum = 0;
+  if (e < E)
+    for (int b = b0; b < b1; ++b) sum += hist[size_t(b) * E + e];
+  s_part[part][e] = sum;
+  __syncthreads();
+  if (tid < 256)
+    s_cnt[tid] = tid < E ? s_part[0][tid] + s_part[1][tid] + s_part[2][tid] + s_part[3][tid] : 0;
+  __syncthreads();
+  const int cnt = tid < E ? s_cnt[tid] : 0;
+  const int ex = scan_block_excl(cnt, s_wsum, &s_tot);
+  if (tid < E) {
+    s_off[tid] = ex;
+    offsets[tid] = ex;
+  }
+  if (tid == 0) {
+    offsets[E] = T * K;
+    offsets[E + 1] = T * K + T;
+  }
+  const int act = (with_routed && tid < E && tid >= lo && tid < hi && cnt > 0) ? 1 : 0;
+  const int apos = scan_block_excl(act, s_wsum, &s_tot);
+  if (act) active[apos] = tid;
+  if (tid == 0) {
+    int na = s_tot;
+    if (with_shared) active[na++] = E;
+    n_active[0] = na;
+  }
+  __syncthreads();
+  if (e < E) {
+    int run = s_off[e];
+    for (int p = 0; p < part; ++p) run += s_part[p][e];
+    for (int b = b0; b < b1; ++b) {
+      base[size_t(b) * E + e] = run;
+      run += hist[size_t(b) * E + e];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA per 128-token tile, 128*K threads (one pair each).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) route_scatter_kernel(
+    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
+    const float* __restrict__ shared_gate, const int32_t* __restrict__ base, int T, int H, int E,
+    int K, int32_t* __restrict__ sorted_tok, int32_t* __restrict__ sorted_slot,
+    int32_t* __restrict__ pair_dst, float* __restrict__ pair_w, float* __restrict__ y_acc) {
+  __shared__ int s_wcnt[32 * 256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int P = T * K;
+  for (int i = tid; i < nw * E; i += blockDim.x) s_wcnt[i] = 0;
+  __syncthreads();
+  const int p = blockIdx.x * kRtM * K + tid;
+  const int e = p < P ? topk_idx[p] : -1;
+  const unsigned m = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(m & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) s_wcnt[warp * E + e] = __popc(m);
+  __syncthreads();
+  if (e >= 0) {
+    int pre = 0;
+    for (int w = 0; w < warp; ++w) pre += s_wcnt[w * E + e];
+    const int pos = base[size_t(blockIdx.x) * E + e] + pre + rank;
+    sorted_tok[pos] = p / K;
+    sorted_slot[pos] = p % K;
+    pair_dst[pos] = p;
+    pair_w[pos] = topk_w[p];
+  }
+  const int tb = blockIdx.x * kRtM;
+  for (int i = tid; i < kRtM; i += blockDim.x) {
+    const int t = tb + i;
+    if (t < T) {
+      sorted_tok[P + t] = t;
+      pair_dst[P + t] = P + t;
+      pair_w[P + t] = shared_gate[t];
+    }
+  }
+  // zero this tile's rows of the fp32 output accumulator
+  const int rows = min(kRtM, T - tb);
+  float4* acc = reinterpret_cast<float4*>(y_acc + size_t(tb) * H);
+  const int n4 = rows * H / 4;
+  for (int i = tid; i < n4; i += blockDim.x) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+cudaError_t route_tc_init() {
+  return cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kRtSmem);
+}
+
+bool route_tc_supported(const Dims& d) {
+  return d.E <= kRtN && d.K <= kRtMaxK && d.H % kRtK == 0;
+}
+
+cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                            const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
+                            int with_routed, const Workspace& ws, cudaStream_t st) {
+  CUtensorMap tm_x, tm_w, tm_g;
+  const uint64_t H = d.H;
+  if (!make_tmap_bf16_2d(&tm_x, x, H, d.T, H * 2, kRtK, kRtM) ||
+      !make_tmap_bf16_2d(&tm_w, w_router, H, d.E, H * 2, kRtK, kRtN) ||
+      !make_tmap_bf16_2d(&tm_g, w_gvec, H, 1, H * 2, kRtK, kRtN2))
+    return cudaErrorInvalidValue;
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  if (err != cudaSuccess) return err;
+  const int nb = (d.T + kRtM - 1) / kRtM;
+  router_tc_kernel<<<nb, kRtThreads, kRtSmem, st>>>(tm_x, tm_w, tm_g, d.T, d.H, d.E, d.K,
+                                                    ws.topk_idx, ws.topk_w, ws.shared_gate,
+                                                    ws.hist, ws.status + 1);
+  route_scan_kernel<<<1, kScanThreads, 0, st>>>(ws.hist, nb, d.T, d.E, d.K, lo, hi, with_shared,
+                                                with_routed, ws.hist_base, ws.offsets, ws.active,
+                                                ws.n_active);
+  route_scatter_kernel<<<nb, kRtM * d.K, 0, st>>>(ws.topk_idx, ws.topk_w, ws.shared_gate,
+                                                  ws.hist_base, d.T, d.H, d.E, d.K,
+                                                  ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
+                                                  ws.pair_w, ws.y_acc);
+  return cudaGetLastError();
+}
+
+}  // namespace pmoe

@@ -391,7 +391,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, cudaStream_t st, void* mid_event) {
+                              __nv_bfloat16* y, bool zero_acc, cudaStream_t st,
+                              void* mid_event) {
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t R = T * d.K + T, ldh = d.ldh;
   CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h;
@@ -405,8 +406,11 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   plan_tiles_kernel<<<1, kPlanThreads, 0, st>>>(ws.offsets, ws.active, ws.n_active, d.E, d.H,
                                                 d.I, d.Is, ws.gu_tiles, ws.dn_tiles,
                                                 ws.tile_counts);
-  cudaError_t err = cudaMemsetAsync(ws.y_acc, 0, sizeof(float) * size_t(T) * H, st);
-  if (err != cudaSuccess) return err;
+  cudaError_t err = cudaSuccess;
+  if (zero_acc) {
+    err = cudaMemsetAsync(ws.y_acc, 0, sizeof(float) * size_t(T) * H, st);
+    if (err != cudaSuccess) return err;
+  }
   int* status = ws.status + 1;
   TileTables gu{ws.gu_tiles, ws.tile_counts, ws.sorted_tok, ws.pair_w};
   TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.sorted_tok, ws.pair_w};
