@@ -108,6 +108,12 @@ __device__ __forceinline__ void cp_async16(uint32_t sdst, const void* gsrc, uint
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
+// Arrive on `bar` when all of this thread's earlier cp.async copies have
+// completed (counts as one of the barrier's expected arrivals).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");

@@ -31,8 +31,8 @@ constexpr int kTcStages = 4;
 constexpr int kABytes = kBM * kBK * 2;   // 16 KiB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KiB
 constexpr int kTcStageBytes = kABytes + kBBytes;
-constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256;
-constexpr int kGatherLag = 2;            // cp.async groups kept in flight per gather thread
+constexpr int kEpiStage = 4 * 32 * 33 * 4;  // down epilogue: one 32x33 fp32 tile per warp
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256 + kEpiStage;
 constexpr uint32_t kTmemCols = 512;      // two 256-column fp32 accumulators
 constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN);
 
@@ -228,18 +228,31 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
           w = tt.pair_w[row0 + r];
         }
         float* dst = y_acc + size_t(tok) * H + n0;
+        // Per-warp 32x32 staging tile: each reduction instruction then covers
+        // 4 rows x 128 contiguous bytes instead of 32 scattered 16-byte pieces.
+        float* stg = reinterpret_cast<float*>(smem + kTcStages * kTcStageBytes + 256) +
+                     (warp - 2) * 32 * 33;
 #pragma unroll 1
         for (int cc = 0; cc < kBN / 32; ++cc) {
           uint32_t v[32];
           tmem_ld32(taddr + cc * 32, v);
           tmem_ld_wait();
-          if (valid) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              red_add_v4(dst + cc * 32 + 4 * i, w * __uint_as_float(v[4 * i]),
-                         w * __uint_as_float(v[4 * i + 1]), w * __uint_as_float(v[4 * i + 2]),
-                         w * __uint_as_float(v[4 * i + 3]));
+          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = w * __uint_as_float(v[i]);
+          __syncwarp();
+          const int c4 = (lane & 7) * 4;
+#pragma unroll
+          for (int pass = 0; pass < 8; ++pass) {
+            const int rr = pass * 4 + (lane >> 3);
+            float* rdst = reinterpret_cast<float*>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), rr));
+            const int rvalid = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr);
+            if (rvalid) {
+              const float* sp = stg + rr * 33 + c4;
+              red_add_v4(rdst + cc * 32 + c4, sp[0], sp[1], sp[2], sp[3]);
+            }
           }
+          __syncwarp();
         }
       }
       (void)e;
@@ -270,20 +283,12 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           cp_async16(sa + (uint32_t((c ^ (r & 7))) << 4), src + kc * kBK + c * 8, nbytes);
-        cp_async_commit();
-        if (it >= uint32_t(kGatherLag)) {
-          cp_async_wait<kGatherLag>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full[(it - kGatherLag) % kTcStages]);
-        }
+        // Arrives on full[s] once these copies land; the MMA thread fences the
+        // generic -> async proxy before issuing on the stage.
+        cp_async_mbar_arrive_noinc(&full[s]);
       }
     }
     cp_async_wait<0>();
-    fence_proxy_async_smem();
-    if (ok) {
-      const uint32_t first = it > uint32_t(kGatherLag) ? it - kGatherLag : 0;
-      for (uint32_t j = first; j < it; ++j) mbar_arrive(&full[j % kTcStages]);
-    }
   }
 
   __syncwarp();  // reconverge warps whose work ran on one elected lane
