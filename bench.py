@@ -1,28 +1,34 @@
 """Benchmark of the B200 MoE block (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--T 64] [--prefill]
+                    [--T 64] [--prefill-T 8192] [--zipf 1.1] [--no-prefill]
 
-A step is one call of the Qwen3.5-35B-A3B MoE layer on T tokens (default
-T=64, the decode configuration of BASELINE.json configs[1]).  Weights are
-random-init bf16 of the real shape (1.5 GB, larger than the 126 MB L2, so
-every step streams them from HBM; no L2 flush is needed) and hidden states
-are synthetic N(0,1).
+A step is one call of the Qwen3.5-35B-A3B MoE layer.  The headline
+(``metric``/``value``) is the decode configuration of BASELINE.json
+configs[1] at its largest batch, T=64 tokens; the same run also measures the
+prefill configuration (configs[2]: T=8192, Zipf(s=1.1)-skewed routing) and
+reports it under ``"prefill"``.  Weights are random-init bf16 of the real
+shape (1.5 GB, larger than the 126 MB L2, so every decode step streams them
+from HBM; no L2 flush is needed) and hidden states are synthetic N(0,1).
 
 * ``value``: tokens/s with inputs resident in HBM, device-timed with CUDA
   events over exactly K steps between barriers; for N>1 the max over ranks.
 * ``e2e``: the same metric through the public op with pinned host buffers:
   every step copies x host->device and y device->host inside the timed region.
-* ``roofline``: the dominant kernel (gate_up + SiLU*mul weight stream),
-  algorithmic bytes per launch / its event-timed average duration, against
-  the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+* ``roofline``: the dominant kernel (decode: the gate_up + SiLU*mul weight
+  stream, HBM-bound; prefill: the gate_up grouped GEMM, tensor-bound),
+  algorithmic bytes or FLOPs per launch / its event-timed average duration,
+  against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the reference's own path -- HF transformers
   ``Qwen3_5MoeSparseMoeBlock`` (the module the reference serves with) on the
   host cores, on a bounded sample of the same workload.
 
 ``--impl reference`` times that CPU path alone, on rank 0 (other ranks exit).
-Multi-GPU (N>1): expert parallel, experts split in contiguous ranges by
-rank (engine/runtime/ep.py:78-86); strong scaling over the same T tokens.
+Multi-GPU (N>1, one process per GPU under torch.distributed.run): expert
+parallel, experts split in contiguous ranges by rank (engine/runtime/ep.py:78-86),
+strong scaling over the same tokens.  Decode exchanges the weighted expert
+rows over NVLink from the down-projection epilogue (no collective kernel);
+prefill sums per-rank partials with NCCL all_reduce.
 """
 from __future__ import annotations
 
@@ -30,6 +36,7 @@ import argparse
 import importlib.util
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -55,9 +62,18 @@ def load_package():
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return d, "measured"
+        return json.load(open(p)), "measured"
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch of a kernel from its committed ncu summary
+    (a line `traffic_bytes_per_launch: N` in profiles/<name>.md), or None."""
+    p = os.path.join(ROOT, "profiles", f"{name}.md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(p).read())
+    return int(m.group(1)) if m else None
 
 
 # ------------------------------------------------------------------ clocks --
@@ -161,7 +177,140 @@ def cpu_reference(weights_cpu, x_cpu, budget_s: float, max_steps: int | None = N
             "ms_per_call": med * 1e3, "calls": len(times)}
 
 
-# ------------------------------------------------------------------- main ---
+# ----------------------------------------------------------- GPU measuring --
+
+class Runner:
+    """One configuration (T tokens, router weights) on this rank."""
+
+    def __init__(self, ctx, T, w_router, x):
+        import torch
+        self.ctx, self.T, self.x = ctx, T, x
+        S = ctx.S
+        self.tensors = [w_router] + ctx.wts.tensors()[1:]
+        self.y = torch.empty((T, S.H), dtype=torch.bfloat16, device=ctx.dev)
+        self.nbytes = ctx.lib_.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+        self.ws = torch.empty(self.nbytes, dtype=torch.uint8, device=ctx.dev)
+        self.wp = [t.data_ptr() for t in self.tensors]
+
+    def step(self, profiled=False):
+        c = self.ctx
+        if c.world > 1:
+            c.group.forward(self.x, self.tensors, out=self.y, workspace=self.ws)
+            return
+        S = c.S
+        args = (self.x.data_ptr(), self.T, S.H, S.E, S.K, S.I, S.Is, *self.wp, 0, S.E, 3,
+                self.y.data_ptr(), self.ws.data_ptr(), self.nbytes, c.st.cuda_stream)
+        if profiled:
+            s = c.lib.pmoe_block_forward_profiled(*args, c.ev_arr, 5)
+        else:
+            s = c.lib.pmoe_block_forward(*args)
+        c.lib_.check("pmoe_block_forward", s)
+
+    def timed(self, steps, warmup):
+        """(ms per step max over ranks, clock summary)."""
+        import torch
+        c = self.ctx
+        for _ in range(warmup):
+            self.step()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(c.local) as clk:
+            t0.record(c.st)
+            for _ in range(steps):
+                self.step()
+            t1.record(c.st)
+            torch.cuda.synchronize()
+        c.barrier()
+        return c.max_over_ranks(t0.elapsed_time(t1)) / steps, clk.summary()
+
+    def phases(self, n):
+        """Average per-phase ms (route, expert GEMM 1, expert GEMM 2 + tail,
+        combine) from events around the kernels of a synchronised call."""
+        import torch
+        c = self.ctx
+        if c.world > 1:
+            return None
+        acc = [0.0] * 4
+        for _ in range(n):
+            self.step(profiled=True)
+            torch.cuda.synchronize()
+            for i in range(4):
+                acc[i] += c.ev[i].elapsed_time(c.ev[i + 1])
+        return [v / n for v in acc]
+
+    def e2e(self, steps):
+        """Public op with pinned host buffers, copies inside the timed region."""
+        import torch
+        c = self.ctx
+        x_host = self.x.cpu().pin_memory()
+        y_host = torch.empty((self.T, c.S.H), dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(self.x)
+        from paris_moe_b200 import ops
+
+        def one():
+            xd.copy_(x_host, non_blocking=True)
+            if c.world > 1:
+                out = c.group.forward(xd, self.tensors)
+            else:
+                out = ops.moe_block(xd, *self.tensors, c.S.K, 0, c.S.E, 3)
+            y_host.copy_(out, non_blocking=True)
+
+        for _ in range(3):
+            one()
+        torch.cuda.synchronize()
+        c.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(c.st)
+        for _ in range(steps):
+            one()
+        e1.record(c.st)
+        torch.cuda.synchronize()
+        ms = c.max_over_ranks(e0.elapsed_time(e1)) / steps
+        return {"value": self.T / (ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": self.T * c.S.H * 2,
+                "d2h_bytes_per_step": self.T * c.S.H * 2, "ms_per_step": ms}
+
+
+class Ctx:
+    def __init__(self, world, rank, local):
+        import torch
+        import torch.distributed as dist
+        from paris_moe_b200 import _lib, workload as W
+        self.world, self.rank, self.local = world, rank, local
+        self.dist = dist
+        if world > 1:
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        self.dev = torch.device("cuda", local)
+        torch.cuda.set_device(self.dev)
+        self.lib_ = _lib
+        self.lib = _lib.load()
+        self.S = W.MoEShape()
+        self.wts = W.make_weights(self.S, seed=0, device=self.dev)
+        self.st = torch.cuda.current_stream(self.dev)
+        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        for e in self.ev:      # torch creates the CUDA event lazily, on first record
+            e.record(self.st)
+        self.ev_arr = (_lib._P * 5)(*[e.cuda_event for e in self.ev])
+        self.group = None
+        if world > 1:
+            from paris_moe_b200 import ep
+            self.group = ep.EPGroup(self.S.E, self.S.H, self.S.K, mode="fused")
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
+            return v
+        import torch
+        t = torch.tensor([v], device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -170,37 +319,36 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--T", type=int, default=64)
-    ap.add_argument("--zipf", type=float, default=None,
-                    help="Zipf(s) prior on the router logits (skewed prefill routing)")
+    ap.add_argument("--prefill-T", type=int, default=8192)
+    ap.add_argument("--zipf", type=float, default=1.1)
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
     import torch
-    import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    PM = load_package()
+    load_package()
     from paris_moe_b200 import workload as W
 
-    regime = "decode" if a.T <= 64 else "prefill"
-    metric = f"MoE layer tokens/s ({regime} T={a.T})"
-    routing = (f"Zipf(s={a.zipf}) skewed routing (BASELINE configs[2])" if a.zipf
-               else "near-uniform routing (BASELINE configs[1])")
-    config = {"workload": f"Qwen3.5-35B-A3B MoE block, {regime} T={a.T}, {routing}",
+    metric = f"MoE layer tokens/s (decode T={a.T})"
+    config = {"workload": f"Qwen3.5-35B-A3B MoE block, decode T={a.T}, near-uniform routing "
+                          "(BASELINE configs[1]); prefill T=8192 Zipf routing (configs[2]) "
+                          "reported under 'prefill'",
               "T": a.T, "hidden": 2048, "experts": 256, "top_k": 8, "moe_ffn": 512,
               "shared_ffn": 512, "parallelism": f"ep{world}" if world > 1 else "single",
-              "l2": "weights (1.5 GB) > L2 (126 MB): streamed from HBM every step"}
+              "l2": "weights (1.5 GB) > L2 (126 MB): streamed from HBM every step, no flush"}
 
     if a.impl == "reference":
         if rank != 0:
             return
-        wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=a.zipf)
-        x = W.make_hidden(a.T, W.MoEShape(), seed=0, zipf=a.zipf is not None)
-        ref = cpu_reference(wts, x, budget_s=1e9, max_steps=a.steps + 0)
+        wts = W.make_weights(W.MoEShape(), seed=0)
+        x = W.make_hidden(a.T, W.MoEShape(), seed=0)
+        ref = cpu_reference(wts, x, budget_s=1e9, max_steps=a.steps)
         line = {"metric": metric, "value": ref["value"], "unit": "tokens/s", "n_gpus": a.gpus,
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": ref["ms_per_call"],
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -211,153 +359,99 @@ def main():
         print(json.dumps(line))
         return
 
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    from paris_moe_b200 import _lib, ops
-    lib = _lib.load()
-
-    shape = W.MoEShape()
-    wts = W.make_weights(shape, seed=0, device=dev, zipf_s=a.zipf)
-    x = W.make_hidden(a.T, shape, seed=0, device=dev, zipf=a.zipf is not None)
-    E = shape.E
-    lo, hi = rank * E // world, (rank + 1) * E // world
-    flags = _lib.PMOE_F_ROUTED | (_lib.PMOE_F_SHARED if rank == 0 else 0)
-    st = torch.cuda.current_stream(dev)
-
-    nbytes = _lib.workspace_size(a.T, shape.H, E, shape.K, shape.I, shape.Is)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    y = torch.empty((a.T, shape.H), dtype=torch.bfloat16, device=dev)
-    wptrs = [t.data_ptr() for t in wts.tensors()]
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-    for e in ev:          # torch creates the CUDA event lazily, on first record
-        e.record(st)
-    ev_arr = (_lib._P * 5)(*[e.cuda_event for e in ev])
-    phase_ms = [0.0] * 4
-
-    def step(profiled=False):
-        args = (x.data_ptr(), a.T, shape.H, E, shape.K, shape.I, shape.Is, *wptrs, lo, hi,
-                flags, y.data_ptr(), ws.data_ptr(), nbytes, st.cuda_stream)
-        if profiled:
-            s = lib.pmoe_block_forward_profiled(*args, ev_arr, 5)
-        else:
-            s = lib.pmoe_block_forward(*args)
-        _lib.check("pmoe_block_forward", s)
-        if world > 1:
-            dist.all_reduce(y)
-
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize()
-
-    # routing statistics of this input (experts hit), for the roofline bytes
-    idx = ops.moe_route(x, wts.w_router, wts.w_sh_gvec, shape.K)[0]
-    hit = int(torch.unique(idx).numel())
-    torch.cuda.synchronize()
-
-    # ---- timed region: exactly K steps, device-timed, max over ranks ----
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t0.record(st)
-        for _ in range(a.steps):
-            step()
-        t1.record(st)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    elapsed_ms = t0.elapsed_time(t1)
-    # Per-phase (per-kernel-group) times: a separate pass with phase events,
-    # each step synchronised so every event pair can be read.
-    n_prof = min(a.steps, 50)
-    acc = [0.0] * 4
-    for _ in range(n_prof):
-        step(profiled=True)
-        torch.cuda.synchronize()
-        for i in range(4):
-            acc[i] += ev[i].elapsed_time(ev[i + 1])
-    phase_ms = [v / n_prof for v in acc]
-    if world > 1:
-        tt = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(tt.item())
-    ms_per_step = elapsed_ms / a.steps
-    value = a.T * a.steps / (elapsed_ms / 1e3)
-
-    # ---- e2e: public op, pinned host buffers, copies inside the region ----
-    x_host = x.cpu().pin_memory()
-    y_host = torch.empty((a.T, shape.H), dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
-    tensors = wts.tensors()
-
-    def e2e_step():
-        xd.copy_(x_host, non_blocking=True)
-        out = ops.moe_block(xd, *tensors, shape.K, lo, hi, flags)
-        if world > 1:
-            dist.all_reduce(out)
-        y_host.copy_(out, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(a.steps):
-        e2e_step()
-    e1.record(st)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
-    e2e_value = a.T * a.steps / (e2e_ms / 1e3)
-
+    c = Ctx(world, rank, local)
+    S = c.S
     peaks, peak_kind = measured_peaks()
-    # dominant kernel: gate_up + SiLU*mul weight stream (phase 1)
-    S = shape
-    local_hit = int(((torch.unique(idx) >= lo) & (torch.unique(idx) < hi)).sum().item())
-    gu_bytes = (local_hit * 2 * S.I * S.H + (2 * S.Is * S.H if rank == 0 else 0)) * 2 \
-        + a.T * S.H * 2 + (a.T * S.K + a.T) * S.I * 2
-    gu_ms = phase_ms[1]
-    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
-    layer_bytes = W.decode_bytes(S, a.T, hit)
 
+    # ------------------------------------------------------------ decode --
+    x = W.make_hidden(a.T, S, seed=0, device=c.dev)
+    dec = Runner(c, a.T, c.wts.w_router, x)
+    ms, clocks = dec.timed(a.steps, a.warmup)
+    phase = dec.phases(min(a.steps, 50))
+    e2e = dec.e2e(a.steps)
+    from paris_moe_b200 import ops
+    idx = ops.moe_route(x, c.wts.w_router, c.wts.w_sh_gvec, S.K)[0]
+    hit_set = torch.unique(idx)
+    hit = int(hit_set.numel())
+    lo, hi = rank * S.E // world, (rank + 1) * S.E // world
+    local_hit = int(((hit_set >= lo) & (hit_set < hi)).sum().item())
+    # dominant kernel: gate_up + SiLU*mul weight stream -- algorithmic bytes:
+    # gate/up rows of every hit expert of this rank, its share of the shared
+    # expert's gate/up rows, the activations read once and h written once.
+    sh_rows = 2 * S.Is * S.H
+    gu_bytes = (local_hit * 2 * S.I * S.H) * 2 + sh_rows * 2 + a.T * S.H * 2 \
+        + (a.T * S.K + a.T) * S.I * 2
     line = {
-        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_per_step,
+        "metric": metric, "value": a.T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init bf16 weights N(0,0.02), hidden N(0,1), seed 0)",
-        "config": config,
-        "e2e": {"value": e2e_value, "unit": "tokens/s",
-                "h2d_bytes_per_step": a.T * S.H * 2, "d2h_bytes_per_step": a.T * S.H * 2},
-        "gpu_launches": 6 * a.steps,
-        "roofline": {"kernel": "gate_up_stream_kernel", "bound": "hbm",
-                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
-                     "peak_source": peak_kind, "algorithmic_bytes": gu_bytes,
-                     "avg_launch_ms": gu_ms},
-        "layer_roofline": {"bound": "hbm", "algorithmic_bytes": layer_bytes,
-                           "experts_hit": hit,
-                           "achieved_gbs": layer_bytes / (ms_per_step * 1e-3) / 1e9,
-                           "frac": layer_bytes / (ms_per_step * 1e-3) / 1e9 / peaks["hbm_gbs"]},
-        "phase_ms": {"route": phase_ms[0], "gate_up": phase_ms[1], "down": phase_ms[2],
-                     "combine": phase_ms[3]},
-        "clocks": clk.summary(),
+        "config": config, "e2e": e2e,
+        # route (1) + gate_up (1) + down (1) + combine (1) per step
+        "gpu_launches": 4 * a.steps,
+        "clocks": clocks,
     }
+    layer_bytes = W.decode_bytes(S, a.T, hit)
+    line["layer_roofline"] = {"bound": "hbm", "algorithmic_bytes": layer_bytes,
+                              "experts_hit": hit, "unit": "GB/s",
+                              "achieved": layer_bytes / (ms * 1e-3) / 1e9,
+                              "frac": layer_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+    if phase is not None:
+        line["phase_ms"] = dict(zip(("route", "gate_up", "down", "combine"), phase))
+        ach = gu_bytes / (phase[1] * 1e-3) / 1e9
+        line["roofline"] = {"kernel": "gate_up_tma_kernel", "bound": "hbm", "achieved": ach,
+                            "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                            "frac": ach / peaks["hbm_gbs"],
+                            "traffic": profiled_traffic("gate_up_tma_decode_T64"),
+                            "algorithmic_bytes": gu_bytes, "avg_launch_ms": phase[1],
+                            "peak_source": f"{peak_kind} (hbm_gbs)"}
+    else:
+        lb = W.decode_bytes(S, a.T, local_hit) / world
+        line["roofline"] = {"kernel": "whole layer per rank", "bound": "hbm",
+                            "achieved": lb / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                            "unit": "GB/s", "frac": lb / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                            "traffic": None, "peak_source": f"{peak_kind} (hbm_gbs)"}
+
+    # ----------------------------------------------------------- prefill --
+    if not a.no_prefill:
+        wr = c.wts.w_router.clone()
+        wr[:, 0] = W.zipf_log_prior(S.E, a.zipf, 0).to(c.dev).to(torch.bfloat16)
+        xp = W.make_hidden(a.prefill_T, S, seed=0, device=c.dev, zipf=True)
+        pre = Runner(c, a.prefill_T, wr, xp)
+        psteps = max(5, min(a.steps, 100))
+        pms, pclk = pre.timed(psteps, a.warmup)
+        pphase = pre.phases(10)
+        flops = W.block_flops(S, a.prefill_T)
+        pl = {"metric": f"MoE layer tokens/s (prefill T={a.prefill_T}, Zipf s={a.zipf})",
+              "value": a.prefill_T / (pms * 1e-3), "unit": "tokens/s", "steps": psteps,
+              "ms_per_step": pms, "algorithmic_flops": flops,
+              "layer_tflops": flops / (pms * 1e-3) / 1e12,
+              "layer_frac": flops / (pms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+              # router_tc, scan, scatter, plan, gate_up, down, finalize per step
+              "gpu_launches": 7 * psteps, "clocks": pclk,
+              "e2e": pre.e2e(max(5, min(a.steps, 50)))}
+        if pphase is not None:
+            pl["phase_ms"] = dict(zip(("route", "gate_up", "down_finalize", "tail"), pphase))
+            P = a.prefill_T * S.K
+            gu_flops = 2 * (P + a.prefill_T) * S.H * 2 * S.I
+            ach = gu_flops / (pphase[1] * 1e-3) / 1e12
+            pl["roofline"] = {"kernel": "tc_grouped_kernel<gate_up>", "bound": "tensor",
+                              "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                              "frac": ach / peaks["bf16_tflops"], "traffic": profiled_traffic(
+                                  "tc_gate_up_prefill_T8192"),
+                              "algorithmic_flops": gu_flops, "avg_launch_ms": pphase[1],
+                              "peak_source": f"{peak_kind} (bf16_tflops, burst)"}
+        line["prefill"] = pl
+
     if world == 1 and rank == 0 and not a.no_cpu_baseline:
-        ref = cpu_reference(wts.to("cpu"), x.cpu(), budget_s=a.cpu_budget)
+        ref = cpu_reference(c.wts.to("cpu"), x.cpu(), budget_s=a.cpu_budget)
         line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line))
+    if c.group is not None:
+        c.group.close()
     if world > 1:
-        dist.destroy_process_group()
+        c.dist.destroy_process_group()
 
 
 if __name__ == "__main__":

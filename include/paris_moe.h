@@ -107,6 +107,55 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
                                 int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
                                 void* stream, void* const* events, int n_events);
 
+/* ---- expert parallelism over NVLink ------------------------------------------
+ * One process per GPU; every rank calls with the same x (replicated tokens)
+ * and the same weights, as ep_forward does (engine/runtime/ep.py:97-143).
+ *
+ * Size of each rank's exchange buffer for batches of up to T_max tokens:
+ * flags + two parity copies of the weighted expert rows. */
+int pmoe_ep_buffer_bytes(int T_max, int H, int K, size_t* bytes);
+
+/* The block on one rank of an expert-parallel group.
+ *   expert_lo/hi      routed experts this rank computes (engine/runtime/ep.py:78-86
+ *                     contiguous ranges, replacing its per-expert loop :124-136)
+ *   shared_lo/hi      tokens whose shared-expert rows this rank computes
+ *   peer_bufs         NULL: y is this rank's partial (routed range + shared token
+ *                     range), to be summed across ranks by the caller (the NCCL
+ *                     all_reduce of ep.py:140).  Otherwise `world` pointers to
+ *                     every rank's exchange buffer (IPC-mapped, this rank's own at
+ *                     [rank]): each computed row is stored straight into every
+ *                     rank's buffer over NVLink from the down-projection epilogue,
+ *                     completion flags are raised with release stores, and the
+ *                     combine waits (bounded; PMOE status kStatusTimeoutPeer via
+ *                     pmoe_read_status) and sums -- y is the full block output on
+ *                     every rank, no separate collective.  Streaming path only
+ *                     (T <= 64 unless PMOE_F_FORCE_STREAM).
+ *   epoch             > 0, increasing by one per call on every rank. */
+int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                          const uint16_t* w_router, const uint16_t* w_gate_up,
+                          const uint16_t* w_down, const uint16_t* w_sh_gate,
+                          const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                          const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                          int shared_lo, int shared_hi, int flags, void* const* peer_bufs,
+                          size_t peer_buf_bytes, int rank, int world, int epoch, uint16_t* y,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronously read the kernel status word of the last call that used this
+ * workspace (0 ok, 1/2/3 a bounded pipeline wait ran out, 4 a peer's flag never
+ * arrived).  Diagnostic; synchronises the device.  No reference counterpart. */
+int pmoe_read_status(const void* workspace, int T, int H, int E, int K, int I, int Is,
+                     int* status);
+
+/* Exchange-buffer plumbing (one-time set-up, not on the hot path):
+ * allocate/zero a device buffer, export it as a 64-byte CUDA IPC handle, map a
+ * peer's handle into this process, unmap it.  No reference counterpart (the
+ * reference only uses NCCL collectives). */
+int pmoe_ipc_alloc(size_t bytes, void** ptr);
+int pmoe_ipc_free(void* ptr);
+int pmoe_ipc_handle(void* ptr, void* handle);
+int pmoe_ipc_open(const void* handle, void** ptr);
+int pmoe_ipc_close(void* ptr);
+
 /* pmoe_block_forward for callers that cannot allocate device memory: it takes
  * no workspace.  Meant for hosts such as a serving engine that reserves all
  * of HBM up front (KV cache, weights) and allows no allocation on its decode

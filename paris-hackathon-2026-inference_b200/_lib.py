@@ -30,6 +30,16 @@ SIGNATURES = {
     "pmoe_block_forward_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
                                         _P, _I, _I, _I, _P, _P]),
     "pmoe_noalloc_scratch_bytes": (_SZ, []),
+    "pmoe_ep_buffer_bytes": (_I, [_I, _I, _I, ctypes.POINTER(_SZ)]),
+    "pmoe_block_forward_ep": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
+                                   _I, _I, _I, _I, _I, ctypes.POINTER(_P), _SZ, _I, _I, _I,
+                                   _P, _P, _SZ, _P]),
+    "pmoe_read_status": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "pmoe_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
+    "pmoe_ipc_free": (_I, [_P]),
+    "pmoe_ipc_handle": (_I, [_P, ctypes.c_char_p]),
+    "pmoe_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "pmoe_ipc_close": (_I, [_P]),
 }
 
 PMOE_F_SHARED = 1

@@ -1,4 +1,5 @@
 // extern "C" entry points of libparis_moe (declared in include/paris_moe.h).
+#include <cstring>
 #include <mutex>
 
 #include "pmoe_common.cuh"
@@ -110,16 +111,21 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
   return PMOE_OK;
 }
 
-int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
-                                const uint16_t* w_router, const uint16_t* w_gate_up,
-                                const uint16_t* w_down, const uint16_t* w_sh_gate,
-                                const uint16_t* w_sh_up, const uint16_t* w_sh_down,
-                                const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
-                                int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
-                                void* stream, void* const* events, int n_events) {
+// Shared implementation of the forward entry points.  `ep` (world > 0)
+// selects the expert-parallel NVLink exchange; sh_lo/sh_hi is the token range
+// whose shared-expert rows this call computes.
+static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                        const uint16_t* w_router, const uint16_t* w_gate_up,
+                        const uint16_t* w_down, const uint16_t* w_sh_gate,
+                        const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                        const uint16_t* w_sh_gvec, int expert_lo, int expert_hi, int sh_lo,
+                        int sh_hi, int flags, uint16_t* y, void* workspace,
+                        size_t workspace_bytes, void* stream, void* const* events, int n_events,
+                        const EpPeers& ep) {
   int s = check_shape(T, H, E, K, I, Is);
   if (s != PMOE_OK) return s;
   if (expert_lo < 0 || expert_hi > E || expert_lo > expert_hi) return PMOE_ERR_ARG;
+  if (sh_lo < 0 || sh_hi > T || sh_lo > sh_hi) return PMOE_ERR_ARG;
   if (flags & ~(PMOE_F_SHARED | PMOE_F_ROUTED | PMOE_F_FORCE_STREAM | PMOE_F_FORCE_TC))
     return PMOE_ERR_ARG;
   if (T == 0) return PMOE_OK;
@@ -131,6 +137,8 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
   }
   if ((s = ensure_device()) != PMOE_OK) return s;
   Dims d = make_dims(T, H, E, K, I, Is);
+  d.sh_lo = sh_lo;
+  d.sh_hi = sh_hi;
   Workspace ws = carve(workspace, d);
   if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -139,9 +147,11 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
   if ((flags & PMOE_F_FORCE_TC) && (flags & PMOE_F_FORCE_STREAM)) return PMOE_ERR_ARG;
   if ((flags & PMOE_F_FORCE_TC) && !tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
   // Weight streaming while the layer is HBM-bound (decode), tcgen05 grouped
-  // GEMMs beyond.
-  const bool use_tc = (flags & PMOE_F_FORCE_TC) ||
-                      (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d));
+  // GEMMs beyond.  The NVLink exchange rides on the streaming kernels.
+  const bool use_tc = ep.world == 0 &&
+                      ((flags & PMOE_F_FORCE_TC) ||
+                       (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d)));
+  if (ep.world > 0 && (flags & PMOE_F_FORCE_TC)) return PMOE_ERR_UNSUPPORTED;
   auto mark = [&](int i) {
     if (events && i < n_events && events[i])
       return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -167,15 +177,35 @@ int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, i
     return PMOE_OK;
   }
   if (launch_stream_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
-                            bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr)
-      != cudaSuccess)
+                            bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr,
+                            ep) != cudaSuccess)
     return PMOE_ERR_CUDA;
   if (mark(3) != cudaSuccess) return PMOE_ERR_CUDA;
-  if (launch_combine(d, ws, expert_lo, expert_hi, with_shared, with_routed,
-                     reinterpret_cast<__nv_bfloat16*>(y), st) != cudaSuccess)
+  // After the exchange every rank holds all routed rows and all shared rows.
+  Dims dc = d;
+  if (ep.world > 0) {
+    dc.sh_lo = 0;
+    dc.sh_hi = T;
+  }
+  if (launch_combine(dc, ws, ep.world > 0 ? 0 : expert_lo, ep.world > 0 ? E : expert_hi,
+                     ep.world > 0 ? 1 : with_shared, ep.world > 0 ? 1 : with_routed,
+                     reinterpret_cast<__nv_bfloat16*>(y), st, ep) != cudaSuccess)
     return PMOE_ERR_CUDA;
   if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
   return PMOE_OK;
+}
+
+int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                                const uint16_t* w_router, const uint16_t* w_gate_up,
+                                const uint16_t* w_down, const uint16_t* w_sh_gate,
+                                const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                                const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                                int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
+                                void* stream, void* const* events, int n_events) {
+  const EpPeers none{};
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, expert_lo, expert_hi, 0, T, flags, y, workspace,
+                      workspace_bytes, stream, events, n_events, none);
 }
 
 int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
@@ -188,6 +218,89 @@ int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int
                                      w_sh_gate, w_sh_up, w_sh_down, w_sh_gvec, expert_lo,
                                      expert_hi, flags, y, workspace, workspace_bytes, stream,
                                      nullptr, 0);
+}
+
+// ---- expert parallelism ------------------------------------------------------
+
+static const size_t kEpHeader = 512;  // flags [0,256), ticket at 256
+
+int pmoe_ep_buffer_bytes(int T_max, int H, int K, size_t* bytes) {
+  if (!bytes || T_max <= 0 || H <= 0 || K <= 0) return PMOE_ERR_ARG;
+  const size_t rows = (size_t(T_max) * K + T_max) * H * sizeof(float);
+  *bytes = kEpHeader + 2 * ((rows + 255) / 256 * 256);
+  return PMOE_OK;
+}
+
+int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                          const uint16_t* w_router, const uint16_t* w_gate_up,
+                          const uint16_t* w_down, const uint16_t* w_sh_gate,
+                          const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                          const uint16_t* w_sh_gvec, int expert_lo, int expert_hi,
+                          int shared_lo, int shared_hi, int flags, void* const* peer_bufs,
+                          size_t peer_buf_bytes, int rank, int world, int epoch, uint16_t* y,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  EpPeers ep{};
+  if (peer_bufs) {
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch <= 0)
+      return PMOE_ERR_ARG;
+    if (T > kFusedRouteMaxT && !(flags & PMOE_F_FORCE_STREAM)) return PMOE_ERR_UNSUPPORTED;
+    const size_t half = (peer_buf_bytes - kEpHeader) / 2;
+    const size_t need = (size_t(T) * K + T) * H * sizeof(float);
+    if (peer_buf_bytes < kEpHeader || need > half) return PMOE_ERR_WORKSPACE;
+    for (int r = 0; r < world; ++r) {
+      if (!peer_bufs[r] || !aligned16(peer_bufs[r])) return PMOE_ERR_ARG;
+      char* b = static_cast<char*>(peer_bufs[r]);
+      ep.rows[r] = reinterpret_cast<float*>(b + kEpHeader + size_t(epoch & 1) * (half / 256 * 256));
+      ep.flags[r] = reinterpret_cast<int*>(b);
+    }
+    ep.ticket = reinterpret_cast<int*>(static_cast<char*>(peer_bufs[rank]) + 256);
+    ep.world = world;
+    ep.rank = rank;
+    ep.epoch = epoch;
+  }
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, expert_lo, expert_hi, shared_lo, shared_hi, flags, y,
+                      workspace, workspace_bytes, stream, nullptr, 0, ep);
+}
+
+int pmoe_read_status(const void* workspace, int T, int H, int E, int K, int I, int Is,
+                     int* status) {
+  if (!workspace || !status) return PMOE_ERR_ARG;
+  int s = check_shape(T, H, E, K, I, Is);
+  if (s != PMOE_OK) return s;
+  Workspace ws = carve(const_cast<void*>(workspace), make_dims(T, H, E, K, I, Is));
+  return cudaMemcpy(status, ws.status + 1, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
+int pmoe_ipc_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return PMOE_ERR_ARG;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return PMOE_ERR_CUDA;
+  return cudaMemset(*ptr, 0, bytes) == cudaSuccess ? PMOE_OK : PMOE_ERR_CUDA;
+}
+
+int pmoe_ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? PMOE_OK : PMOE_ERR_CUDA; }
+
+int pmoe_ipc_handle(void* ptr, void* handle) {
+  if (!ptr || !handle) return PMOE_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return PMOE_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return PMOE_OK;
+}
+
+int pmoe_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return PMOE_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
+int pmoe_ipc_close(void* ptr) {
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? PMOE_OK : PMOE_ERR_CUDA;
 }
 
 }  // extern "C"

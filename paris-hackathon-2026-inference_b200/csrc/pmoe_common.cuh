@@ -44,13 +44,39 @@ struct Dims {
   int Rpad;   // router rows (E experts + shared gate) padded to 16
   int KS;     // router split-K factor (1)
   int ldh;    // row stride of h
+  int sh_lo, sh_hi;  // token range this call computes the shared expert for
 };
+
+// Expert-parallel exchange of the weighted expert rows over NVLink (decode).
+// Every rank routes all tokens identically; rank r computes the experts in
+// its range and writes each weighted row into EVERY rank's `rows` buffer
+// (peer stores), then the last of its CTAs to finish raises flags[q][r] =
+// epoch on every rank q.  The combine on rank q waits (bounded) for
+// flags[q][0..world) >= epoch and sums locally: no separate collective.
+constexpr int kMaxRanks = 8;
+struct EpPeers {
+  float* rows[kMaxRanks];  // each rank's rows buffer for this call (peer-mapped)
+  int* flags[kMaxRanks];   // each rank's flag array, indexed by the writing rank
+  int* ticket;             // this rank's CTA-completion counter (starts and ends at 0)
+  int world;               // 0: no exchange
+  int rank;
+  int epoch;               // strictly increasing per call, > 0
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Token counts up to this use the single-launch routing kernel.
 constexpr int kFusedRouteMaxT = 64;
 
 inline Dims make_dims(int T, int H, int E, int K, int I, int Is) {
-  Dims d{T, H, E, K, I, Is, 0, 0, 0};
+  Dims d{T, H, E, K, I, Is, 0, 0, 0, 0, T};
   d.Rpad = ((E + 1) + 15) / 16 * 16;
   d.KS = 1;
   d.ldh = I > Is ? I : Is;

@@ -15,7 +15,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                                   const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                                   const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                                  cudaStream_t st, void* mid_event);
+                                  cudaStream_t st, void* mid_event, const EpPeers& ep);
 
 cudaError_t tc_init(int num_sms);
 bool tc_supported(const Dims& d);
@@ -35,6 +35,7 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
                             int with_routed, const Workspace& ws, cudaStream_t st);
 
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
-                           int with_routed, __nv_bfloat16* y, cudaStream_t st);
+                           int with_routed, __nv_bfloat16* y, cudaStream_t st,
+                           const EpPeers& ep);
 
 }  // namespace pmoe

@@ -12,7 +12,13 @@ namespace pmoe {
 // ~1 s at 1.9 GHz: far beyond any legitimate wait inside one kernel.
 constexpr long long kWaitBudgetCycles = 2000000000LL;
 
-enum : int { kStatusOk = 0, kStatusTimeoutFull = 1, kStatusTimeoutEmpty = 2, kStatusTimeoutTmem = 3 };
+enum : int {
+  kStatusOk = 0,
+  kStatusTimeoutFull = 1,
+  kStatusTimeoutEmpty = 2,
+  kStatusTimeoutTmem = 3,
+  kStatusTimeoutPeer = 4  // a peer GPU's completion flag never arrived
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

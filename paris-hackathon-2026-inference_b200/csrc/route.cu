@@ -173,6 +173,7 @@ struct DispatchOut {
   int32_t* sorted_slot;
   int32_t* pair_dst;
   float* pair_w;
+  int sh_lo, sh_hi;  // shared-expert rows P+sh_lo .. P+sh_hi are computed
 };
 
 __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ topk_idx,
@@ -190,15 +191,15 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
     o.offsets[tid] = ex;
   }
   if (tid == 0) {
-    o.offsets[E] = P;
-    o.offsets[E + 1] = P + T;
+    o.offsets[E] = P + o.sh_lo;
+    o.offsets[E + 1] = P + o.sh_hi;
   }
   const int act = (with_routed && tid < E && tid >= lo && tid < hi && cnt > 0) ? 1 : 0;
   const int apos = block_exclusive_scan(act, s_wsum, s_tot);
   if (act) o.active[apos] = tid;
   if (tid == 0) {
     int na = *s_tot;
-    if (with_shared) o.active[na++] = E;
+    if (with_shared && o.sh_hi > o.sh_lo) o.active[na++] = E;
     o.n_active[0] = na;
   }
   __syncthreads();
@@ -386,7 +387,7 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
                          const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                          int with_routed, const Workspace& ws, cudaStream_t st) {
   DispatchOut o{ws.offsets, ws.active, ws.n_active, ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
-                ws.pair_w};
+                ws.pair_w, d.sh_lo, d.sh_hi};
   const int RG = d.Rpad / 16, TT = (d.T + 31) / 32;
   cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;

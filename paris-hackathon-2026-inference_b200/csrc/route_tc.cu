@@ -229,7 +229,8 @@ __device__ int scan_block_excl(int v, int* warp_sums, int* total) {
 
 __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
     const int32_t* __restrict__ hist, int nb, int T, int E, int K, int lo, int hi,
-    int with_shared, int with_routed, int32_t* __restrict__ base, int32_t* __restrict__ offsets,
+    int with_shared, int with_routed, int sh_lo, int sh_hi, int32_t* __restrict__ base,
+    int32_t* __restrict__ offsets,
     int32_t* __restrict__ active, int32_t* __restrict__ n_active) {
   __shared__ int s_part[4][256];
   __shared__ int s_cnt[256], s_off[256], s_wsum[32], s_tot;
@@ -251,15 +252,15 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
     offsets[tid] = ex;
   }
   if (tid == 0) {
-    offsets[E] = T * K;
-    offsets[E + 1] = T * K + T;
+    offsets[E] = T * K + sh_lo;
+    offsets[E + 1] = T * K + sh_hi;
   }
   const int act = (with_routed && tid < E && tid >= lo && tid < hi && cnt > 0) ? 1 : 0;
   const int apos = scan_block_excl(act, s_wsum, &s_tot);
   if (act) active[apos] = tid;
   if (tid == 0) {
     int na = s_tot;
-    if (with_shared) active[na++] = E;
+    if (with_shared && sh_hi > sh_lo) active[na++] = E;
     n_active[0] = na;
   }
   __syncthreads();
@@ -342,7 +343,8 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
                                                     ws.topk_idx, ws.topk_w, ws.shared_gate,
                                                     ws.hist, ws.status + 1);
   route_scan_kernel<<<1, kScanThreads, 0, st>>>(ws.hist, nb, d.T, d.E, d.K, lo, hi, with_shared,
-                                                with_routed, ws.hist_base, ws.offsets, ws.active,
+                                                with_routed, d.sh_lo, d.sh_hi, ws.hist_base,
+                                                ws.offsets, ws.active,
                                                 ws.n_active);
   route_scatter_kernel<<<nb, kRtM * d.K, 0, st>>>(ws.topk_idx, ws.topk_w, ws.shared_gate,
                                                   ws.hist_base, d.T, d.H, d.E, d.K,

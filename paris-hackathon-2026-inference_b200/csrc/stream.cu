@@ -276,7 +276,7 @@ template <int KCH>
 __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
     const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
-    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue) {
+    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep) {
   using C = DnCfg<KCH>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -397,22 +397,71 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
             if (i + hh < n) {
               const int p = p0 + i + hh;
               const float wt = tb.pair_w[p];
-              float* out = rows + size_t(tb.pair_dst[p]) * H;
-              out[orow] = acc[q][hh] * wt;
-              out[orow + 8] = acc[q][2 + hh] * wt;
+              const size_t off = size_t(tb.pair_dst[p]) * H;
+              const float v0 = acc[q][hh] * wt, v1 = acc[q][2 + hh] * wt;
+              if (ep.world > 0) {
+                // every computed row goes to every rank (peer stores over NVLink)
+                for (int rr = 0; rr < ep.world; ++rr) {
+                  float* out = ep.rows[rr] + off;
+                  out[orow] = v0;
+                  out[orow + 8] = v1;
+                }
+              } else {
+                float* out = rows + off;
+                out[orow] = v0;
+                out[orow + 8] = v1;
+              }
             }
           }
         }
       }
     }
   }
+  if (ep.world > 0) {
+    // All of this warp's peer stores are made visible system-wide before it
+    // takes a ticket; the last consumer warp of the grid releases the flags.
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+      const int prev = atomicAdd(ep.ticket, 1);
+      if (prev == int(gridDim.x) * kConsumers - 1) {
+        __threadfence_system();
+        *ep.ticket = 0;
+        for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, ep.epoch);
+      }
+    }
+  }
 }
 
 // y[t, :] = bf16( sum_{s<K, expert in [lo,hi)} rows[t*K+s, :] + rows[T*K+t, :] )
-// fp32, fixed summation order.  One thread per 4 columns.
+// fp32, fixed summation order.  One thread per 4 columns.  The shared row is
+// added for tokens in [sh_lo, sh_hi).  With an expert-parallel exchange
+// (world > 0) every block first waits, bounded, until all ranks' completion
+// flags for this epoch are up.
 __global__ void __launch_bounds__(256) combine_kernel(
     const float* __restrict__ rows, const int32_t* __restrict__ topk_idx, int T, int H, int K,
-    int lo, int hi, int with_shared, int with_routed, __nv_bfloat16* __restrict__ y) {
+    int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    const int* __restrict__ wait_flags, int world, int epoch, int* __restrict__ status,
+    __nv_bfloat16* __restrict__ y) {
+  if (world > 0) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      const long long t0 = clock64();
+      for (int r = 0; r < world && ok; ++r) {
+        while (ld_acquire_sys(wait_flags + r) < epoch) {
+          if (clock64() - t0 > kWaitBudgetCycles) {
+            ok = 0;
+            atomicCAS(status, 0, kStatusTimeoutPeer);
+            break;
+          }
+        }
+      }
+      s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+  }
   const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int cols4 = H / 4;
   if (i >= long(T) * cols4) return;
@@ -426,7 +475,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
       s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
     }
   }
-  if (with_shared) {
+  if (with_shared && t >= sh_lo && t < sh_hi) {
     const float4 v = reinterpret_cast<const float4*>(rows + (size_t(T) * K + t) * H)[c4];
     s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
   }
@@ -482,7 +531,8 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                                   const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                                   const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                                  cudaStream_t st, void* mid_event) {
+                                  cudaStream_t st, void* mid_event, const EpPeers& ep) {
+  float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
   const int kg = fit_kch(g_kch_gu, d.H, d.H);
   const int kd = fit_kch(g_kch_dn, d.I, d.Is);
   CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h;
@@ -503,7 +553,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
 #define PMOE_DN(KCH)                                                                  \
   down_tma_kernel<KCH><<<g_num_sms, kStreamThreads, DnCfg<KCH>::kSmem, st>>>(         \
-      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, ws.rows, status, ws.status + 3)
+      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep)
   if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
@@ -516,11 +566,15 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
 }
 
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
-                           int with_routed, __nv_bfloat16* y, cudaStream_t st) {
+                           int with_routed, __nv_bfloat16* y, cudaStream_t st,
+                           const EpPeers& ep) {
   const long n = long(d.T) * (d.H / 4);
   if (n == 0) return cudaSuccess;
-  combine_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(ws.rows, ws.topk_idx, d.T, d.H, d.K,
-                                                           lo, hi, with_shared, with_routed, y);
+  const float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
+  const int* flags = ep.world > 0 ? ep.flags[ep.rank] : nullptr;
+  combine_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(
+      rows, ws.topk_idx, d.T, d.H, d.K, lo, hi, with_shared, with_routed, d.sh_lo, d.sh_hi, flags,
+      ep.world, ep.epoch, ws.status + 1, y);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,177 @@
+"""Expert parallelism for the MoE block, one process per GPU.
+
+Mirrors the reference's EP module (engine/runtime/ep.py):
+
+* ``init_ep(world_size, rank, local_rank)`` -- NCCL process group
+  (ep.py:43-75), MASTER_ADDR defaulting to 127.0.0.1;
+* ``expert_range(num_experts, rank, world_size)`` -- the same contiguous
+  ``rank * n // world_size`` split (ep.py:78-86);
+* ``patch_moe_for_ep(model, rank, world_size)`` -- installs the EP forward on
+  every ``Qwen3_5MoeSparseMoeBlock`` of a model (ep.py:148-178; the reference
+  looks for ``Qwen3NextSparseMoeBlock``, which the Qwen3.5 block does not
+  subclass, so its patch never applied).
+
+Semantics follow ``ep_forward`` (ep.py:97-143): tokens are replicated, every
+rank routes all of them, computes only its experts, and the partial outputs
+are summed.  Two ways to sum:
+
+* ``fused`` (decode batches, T <= 64): the down-projection epilogue stores
+  each weighted expert row straight into every rank's exchange buffer over
+  NVLink (CUDA IPC-mapped), raises per-rank completion flags, and the
+  combine waits on them (bounded) and sums locally -- every rank ends with the
+  full output and no collective kernel runs;
+* ``nccl`` (the comparator, and prefill): each rank returns its partial
+  (its experts plus its share of the shared expert's tokens) and
+  ``torch.distributed.all_reduce`` sums them, as ep.py:140 does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+_BF16 = torch.bfloat16
+FUSED_MAX_T = 64
+
+
+def init_ep(world_size: int, rank: int, local_rank: int | None = None):
+    """NCCL process group for EP (idempotent); returns (rank, world_size)."""
+    if world_size <= 1:
+        return 0, 1
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29500")
+    if local_rank is None:
+        local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local_rank)
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", world_size=world_size, rank=rank)
+    return rank, world_size
+
+
+def expert_range(num_experts: int, rank: int, world_size: int):
+    """Contiguous experts [lo, hi) owned by ``rank`` (ep.py:78-86)."""
+    return rank * num_experts // world_size, (rank + 1) * num_experts // world_size
+
+
+def token_range(num_tokens: int, rank: int, world_size: int):
+    """Tokens [lo, hi) whose shared-expert rows ``rank`` computes."""
+    return rank * num_tokens // world_size, (rank + 1) * num_tokens // world_size
+
+
+def exchange_handles(local: bytes, group=None) -> list[bytes]:
+    """All ranks' 64-byte IPC handles, indexed by rank (host collective)."""
+    out: list = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, local, group=group)
+    return out
+
+
+class EPGroup:
+    """One rank's state for expert-parallel MoE calls.
+
+    ``mode`` is "fused" (NVLink exchange for T <= 64, NCCL partials beyond)
+    or "nccl" (always partials + all_reduce: the comparator)."""
+
+    def __init__(self, num_experts: int, hidden: int, top_k: int, mode: str = "fused",
+                 t_max: int = FUSED_MAX_T, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.E, self.H, self.K = num_experts, hidden, top_k
+        self.lo, self.hi = expert_range(num_experts, self.rank, self.world)
+        self.mode = mode
+        self.epoch = 0
+        self.lib = _lib.load()
+        self.local_buf = None
+        self.peer_ptrs = None
+        if mode == "fused" and self.world > 1:
+            nbytes = ctypes.c_size_t(0)
+            _lib.check("pmoe_ep_buffer_bytes",
+                       self.lib.pmoe_ep_buffer_bytes(t_max, hidden, top_k, ctypes.byref(nbytes)))
+            self.buf_bytes = int(nbytes.value)
+            ptr = ctypes.c_void_p()
+            _lib.check("pmoe_ipc_alloc", self.lib.pmoe_ipc_alloc(self.buf_bytes, ctypes.byref(ptr)))
+            self.local_buf = ptr.value
+            h = ctypes.create_string_buffer(64)
+            _lib.check("pmoe_ipc_handle", self.lib.pmoe_ipc_handle(self.local_buf, h))
+            handles = exchange_handles(h.raw, group)
+            ptrs = []
+            for r, hr in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.local_buf)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check("pmoe_ipc_open", self.lib.pmoe_ipc_open(hr, ctypes.byref(p)))
+                ptrs.append(p.value)
+            self.peer_ptrs = ptrs
+            self.peer_arr = (ctypes.c_void_p * self.world)(*ptrs)
+            self.t_max = t_max
+            torch.cuda.synchronize()
+            dist.barrier(group)
+
+    def uses_exchange(self, T: int) -> bool:
+        return self.peer_ptrs is not None and T <= min(self.t_max, FUSED_MAX_T)
+
+    def forward(self, x: torch.Tensor, weights, flags: int = 3,
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
+        """y[T,H] (full output on every rank) for replicated x[T,H]."""
+        T, H = x.shape
+        w = list(weights)
+        I, Is = w[1].shape[1] // 2, w[4].shape[0]
+        y = out if out is not None else torch.empty((T, H), dtype=_BF16, device=x.device)
+        if T == 0:
+            return y
+        nbytes = _lib.workspace_size(T, H, self.E, self.K, I, Is)
+        ws = workspace if workspace is not None else torch.empty(nbytes, dtype=torch.uint8,
+                                                                 device=x.device)
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        wp = [t.data_ptr() for t in w]
+        if self.uses_exchange(T):
+            self.epoch += 1
+            s = self.lib.pmoe_block_forward_ep(
+                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, 0, T, flags,
+                self.peer_arr, self.buf_bytes, self.rank, self.world, self.epoch, y.data_ptr(),
+                ws.data_ptr(), nbytes, st)
+            _lib.check("pmoe_block_forward_ep", s)
+            return y
+        slo, shi = token_range(T, self.rank, self.world)
+        s = self.lib.pmoe_block_forward_ep(
+            x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
+            None, 0, self.rank, self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)
+        _lib.check("pmoe_block_forward_ep", s)
+        if self.world > 1:
+            dist.all_reduce(y, group=self.group)
+        return y
+
+    def close(self):
+        if self.peer_ptrs is not None:
+            torch.cuda.synchronize()
+            for r, p in enumerate(self.peer_ptrs):
+                if r != self.rank:
+                    self.lib.pmoe_ipc_close(p)
+            self.lib.pmoe_ipc_free(self.local_buf)
+            self.peer_ptrs = None
+
+
+def patch_moe_for_ep(model, rank: int, world_size: int, mode: str = "fused") -> int:
+    """Install the EP forward on every Qwen3_5MoeSparseMoeBlock of ``model``
+    (after ``moe.patch_qwen3_5_moe()``).  Returns the number of blocks."""
+    if world_size <= 1:
+        return 0
+    from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeSparseMoeBlock
+    from .moe import block_weights
+    count = 0
+    group = None
+    for m in model.modules():
+        if isinstance(m, Qwen3_5MoeSparseMoeBlock):
+            if group is None:
+                group = EPGroup(m.gate.weight.shape[0], m.gate.weight.shape[1],
+                                int(m.gate.top_k), mode=mode)
+            m._pmoe_expert_range = (group.lo, group.hi)
+            m._pmoe_post = (lambda blk, x, g=group: g.forward(x, block_weights(blk)))
+            count += 1
+    return count

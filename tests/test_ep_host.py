@@ -1,0 +1,36 @@
+"""Host-side EP logic on CPU: the expert / token partitions and the IPC
+handle exchange over a 2-rank gloo group."""
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PM
+
+
+def test_expert_range_partitions():
+    from paris_moe_b200.ep import expert_range, token_range
+    for n, w in [(256, 1), (256, 2), (256, 8), (257, 3), (10, 4)]:
+        ranges = [expert_range(n, r, w) for r in range(w)]
+        assert ranges[0][0] == 0 and ranges[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        assert max(h - l for l, h in ranges) - min(h - l for l, h in ranges) <= 1
+        assert token_range(n, 1, w) == expert_range(n, 1, w) if w > 1 else True
+    assert expert_range(256, 3, 8) == (96, 128)      # ep.py:78-86 formula
+
+
+def _worker(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from paris_moe_b200.ep import exchange_handles
+    got = exchange_handles(bytes([rank]) * 64)
+    assert [g[0] for g in got] == list(range(world))
+    assert all(len(g) == 64 for g in got)
+    dist.destroy_process_group()
+
+
+def test_handle_exchange_gloo():
+    mp.spawn(_worker, args=(2, 29611), nprocs=2, join=True)

@@ -1,0 +1,65 @@
+"""Expert parallelism on the GPU: multi-GPU parity (when the box has two or
+more GPUs) and the bounded peer wait, which a single GPU can exercise."""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import sys
+import time
+
+import pytest
+import torch
+
+from conftest import PM, ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_ep_two_gpus_matches_single_gpu():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", "29531",
+           os.path.join(ROOT, "tests", "ep_worker.py")]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    print(p.stdout[-4000:], p.stderr[-2000:])
+    assert p.returncode == 0
+    assert p.stdout.count("EP_OK") == 2
+
+
+def test_missing_peer_times_out_without_hanging():
+    """A 2-rank exchange where rank 1 never runs: rank 0's combine gives up on
+    the absent flag after its bounded wait and reports status 4 (peer
+    timeout); the GPU context stays usable."""
+    from paris_moe_b200 import _lib, workload as W
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=64, Is=64)
+    wts = W.make_weights(S, seed=1, device="cuda")
+    x = W.make_hidden(8, S, seed=1, device="cuda")
+    T = x.shape[0]
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_ep_buffer_bytes(T, S.H, S.K, ctypes.byref(nb)) == 0
+    bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    arr = (ctypes.c_void_p * 2)(*[b.data_ptr() for b in bufs])
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    y = torch.empty_like(x)
+    t0 = time.time()
+    st = lib.pmoe_block_forward_ep(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is,
+                                   *[t.data_ptr() for t in wts.tensors()], 0, S.E // 2, 0, T, 3,
+                                   arr, nb.value, 0, 2, 1, y.data_ptr(), ws.data_ptr(), n,
+                                   torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    status = ctypes.c_int(-1)
+    assert lib.pmoe_read_status(ws.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is,
+                                ctypes.byref(status)) == 0
+    assert status.value == 4
+    assert time.time() - t0 < 60
+    # the context still works
+    from paris_moe_b200 import ops
+    z = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
+    torch.cuda.synchronize()
+    assert torch.isfinite(z.float()).all()
