@@ -332,6 +332,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("NCCL_DEBUG", "WARN")   # keep stdout to the one JSON line
     load_package()
     from paris_moe_b200 import workload as W
 
@@ -406,7 +407,7 @@ def main():
                             "algorithmic_bytes": gu_bytes, "avg_launch_ms": phase[1],
                             "peak_source": f"{peak_kind} (hbm_gbs)"}
     else:
-        lb = W.decode_bytes(S, a.T, local_hit) / world
+        lb = W.decode_bytes(S, a.T, local_hit)
         line["roofline"] = {"kernel": "whole layer per rank", "bound": "hbm",
                             "achieved": lb / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
                             "unit": "GB/s", "frac": lb / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],

@@ -191,8 +191,8 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
     o.offsets[tid] = ex;
   }
   if (tid == 0) {
-    o.offsets[E] = P + o.sh_lo;
-    o.offsets[E + 1] = P + o.sh_hi;
+    o.offsets[E] = P;  // routed rows end here; the shared block is compacted
+    o.offsets[E + 1] = P + (o.sh_hi - o.sh_lo);
   }
   const int act = (with_routed && tid < E && tid >= lo && tid < hi && cnt > 0) ? 1 : 0;
   const int apos = block_exclusive_scan(act, s_wsum, s_tot);
@@ -231,10 +231,12 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
     }
     __syncthreads();
   }
-  for (int t = tid; t < T; t += nthr) {
-    o.sorted_tok[P + t] = t;
-    o.pair_dst[P + t] = P + t;
-    o.pair_w[P + t] = shared_gate[t];
+  // shared-expert rows: dispatched row P+i is token sh_lo+i (output row P+t)
+  for (int i = tid; i < o.sh_hi - o.sh_lo; i += nthr) {
+    const int t = o.sh_lo + i;
+    o.sorted_tok[P + i] = t;
+    o.pair_dst[P + i] = P + t;
+    o.pair_w[P + i] = shared_gate[t];
   }
 }
 

@@ -252,8 +252,8 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
     offsets[tid] = ex;
   }
   if (tid == 0) {
-    offsets[E] = T * K + sh_lo;
-    offsets[E + 1] = T * K + sh_hi;
+    offsets[E] = T * K;  // routed rows end here; the shared block is compacted
+    offsets[E + 1] = T * K + (sh_hi - sh_lo);
   }
   const int act = (with_routed && tid < E && tid >= lo && tid < hi && cnt > 0) ? 1 : 0;
   const int apos = scan_block_excl(act, s_wsum, &s_tot);
@@ -280,7 +280,8 @@ __global__ void __launch_bounds__(kScanThreads) route_scan_kernel(
 __global__ void __launch_bounds__(1024) route_scatter_kernel(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
     const float* __restrict__ shared_gate, const int32_t* __restrict__ base, int T, int H, int E,
-    int K, int32_t* __restrict__ sorted_tok, int32_t* __restrict__ sorted_slot,
+    int K, int sh_lo, int sh_hi, int32_t* __restrict__ sorted_tok,
+    int32_t* __restrict__ sorted_slot,
     int32_t* __restrict__ pair_dst, float* __restrict__ pair_w, float* __restrict__ y_acc) {
   __shared__ int s_wcnt[32 * 256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -305,10 +306,10 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
   const int tb = blockIdx.x * kRtM;
   for (int i = tid; i < kRtM; i += blockDim.x) {
     const int t = tb + i;
-    if (t < T) {
-      sorted_tok[P + t] = t;
-      pair_dst[P + t] = P + t;
-      pair_w[P + t] = shared_gate[t];
+    if (t >= sh_lo && t < sh_hi) {  // dispatched row P+(t-sh_lo) is token t
+      sorted_tok[P + t - sh_lo] = t;
+      pair_dst[P + t - sh_lo] = P + t;
+      pair_w[P + t - sh_lo] = shared_gate[t];
     }
   }
   // zero this tile's rows of the fp32 output accumulator
@@ -347,7 +348,8 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
                                                 ws.offsets, ws.active,
                                                 ws.n_active);
   route_scatter_kernel<<<nb, kRtM * d.K, 0, st>>>(ws.topk_idx, ws.topk_w, ws.shared_gate,
-                                                  ws.hist_base, d.T, d.H, d.E, d.K,
+                                                  ws.hist_base, d.T, d.H, d.E, d.K, d.sh_lo,
+                                                  d.sh_hi,
                                                   ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
                                                   ws.pair_w, ws.y_acc);
   return cudaGetLastError();

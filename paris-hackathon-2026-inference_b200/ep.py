@@ -130,15 +130,17 @@ class EPGroup:
                                                                  device=x.device)
         st = torch.cuda.current_stream(x.device).cuda_stream
         wp = [t.data_ptr() for t in w]
+        slo, shi = token_range(T, self.rank, self.world)
         if self.uses_exchange(T):
+            # each rank computes its experts and its share of the shared
+            # expert's tokens; every computed row is exchanged
             self.epoch += 1
             s = self.lib.pmoe_block_forward_ep(
-                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, 0, T, flags,
+                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
                 self.peer_arr, self.buf_bytes, self.rank, self.world, self.epoch, y.data_ptr(),
                 ws.data_ptr(), nbytes, st)
             _lib.check("pmoe_block_forward_ep", s)
             return y
-        slo, shi = token_range(T, self.rank, self.world)
         s = self.lib.pmoe_block_forward_ep(
             x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
             None, 0, self.rank, self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)

@@ -63,3 +63,33 @@ def test_missing_peer_times_out_without_hanging():
     z = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
     torch.cuda.synchronize()
     assert torch.isfinite(z.float()).all()
+
+
+@pytest.mark.parametrize("T,flags", [(200, 3), (64, 3), (64, 3 | 4), (200, 2), (200, 1)])
+def test_rank_partials_sum_to_full(T, flags):
+    """What each of 4 ranks returns without the exchange (its experts, its
+    shared-expert tokens) sums to the single-GPU block (the NCCL-comparator
+    semantics of ep_forward, engine/runtime/ep.py:97-143)."""
+    from oracle import moe_oracle as O
+    from paris_moe_b200 import _lib, ops, workload as W
+    from paris_moe_b200.ep import expert_range, token_range
+    lib = _lib.load()
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=5, device="cuda")
+    x = W.make_hidden(T, S, seed=7, device="cuda")
+    full = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, flags).float()
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    acc = torch.zeros_like(full)
+    for r in range(4):
+        ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+        y = torch.empty_like(x)
+        lo, hi = expert_range(S.E, r, 4)
+        slo, shi = token_range(T, r, 4)
+        st = lib.pmoe_block_forward_ep(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is,
+                                       *[t.data_ptr() for t in wts.tensors()], lo, hi, slo, shi,
+                                       flags, None, 0, r, 4, 0, y.data_ptr(), ws.data_ptr(), n,
+                                       torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        acc += y.float()
+    torch.cuda.synchronize()
+    assert O.rel_l2(acc.cpu().numpy(), full.cpu().numpy()) < 5e-3
