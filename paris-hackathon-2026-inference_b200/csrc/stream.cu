@@ -45,6 +45,7 @@ constexpr int kActRows = 32;                    // dispatched rows per pass
 constexpr int kActChunkBytes = kActRows * kKC * 2;  // 4 KiB activation chunk
 constexpr int kRingBudget = 200 * 1024;
 constexpr int kUnitSlots = 4;
+constexpr int kDnRowBlocks = 4;  // down unit = 4 x 64 output rows (amortises unit set-up)
 
 template <int KCH>
 struct GuCfg {
@@ -84,17 +85,23 @@ struct UnitRing {
       mbar_init(&empty[i], kConsumers);
     }
   }
-  // Producer: next unit from the global queue, heaviest (last) first; -1 = done.
-  __device__ bool publish(uint32_t ui, int* queue, int n_units, int* out_unit) {
+  // Next unit from the global queue, heaviest (last) first; -1 = done.
+  __device__ static int ticket(int* queue, int n_units) {
+    const int q = atomicAdd(queue, 1);
+    return q < n_units ? n_units - 1 - q : -1;
+  }
+  // Producer: hand unit `u` to the consumers in hand-off `ui`.
+  __device__ bool publish_unit(uint32_t ui, int u) {
     const int slot = ui % kUnitSlots;
     if (ui >= uint32_t(kUnitSlots) && !mbar_wait(&empty[slot], ((ui / kUnitSlots) & 1) ^ 1))
       return false;
-    const int q = atomicAdd(queue, 1);
-    const int u = q < n_units ? n_units - 1 - q : -1;
     unit[slot] = u;
     mbar_arrive(&full[slot]);
-    *out_unit = u;
     return true;
+  }
+  __device__ bool publish(uint32_t ui, int* queue, int n_units, int* out_unit) {
+    *out_unit = ticket(queue, n_units);
+    return publish_unit(ui, *out_unit);
   }
   // Consumer warp: unit published in hand-off `ui`.
   __device__ bool take(uint32_t ui, int lane, int* out_unit) {
@@ -153,14 +160,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     prefetch_tmap(&tm_x);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
+    int u_next = ur.ticket(queue, n_units);  // prefetched queue ticket
     for (uint32_t ui = 0;; ++ui) {
-      int u;
-      if (!ur.publish(ui, queue, n_units, &u)) {
+      const int u = u_next;
+      if (!ur.publish_unit(ui, u)) {
         set_status(status, kStatusTimeoutEmpty);
         drain(full, it, kStages);
         return;
       }
       if (u < 0) break;
+      u_next = ur.ticket(queue, n_units);
       const int e = tb.active[u / UJ], jb = u % UJ;
       const bool sh = (e == E);
       if (jb * kUnitRows >= (sh ? Is : I)) continue;
@@ -275,7 +284,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
 template <int KCH>
 __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
-    const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
+    const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h8,
+    ExpertTables tb, int H, int E, int I, int Is,
     float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep) {
   using C = DnCfg<KCH>;
   constexpr int kStages = C::kStages;
@@ -294,7 +304,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     mbar_fence_init();
   }
   __syncthreads();
-  const int UR = H / kUnitRows;
+  const int UR = H / (kUnitRows * kDnRowBlocks);
   const int n_units = tb.n_active[0] * UR;
 
   if (warp == 0) {
@@ -302,24 +312,35 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     prefetch_tmap(&tm_dn);
     prefetch_tmap(&tm_sd);
     prefetch_tmap(&tm_h);
+    prefetch_tmap(&tm_h8);
     const uint64_t pol = l2_policy_evict_first();
     uint32_t it = 0;
+    // The next unit's ticket is taken while this unit's stages are issued, so
+    // the queue's atomic round trip is off the producer's critical path.
+    int u_next = ur.ticket(queue, n_units);
     for (uint32_t ui = 0;; ++ui) {
-      int u;
-      if (!ur.publish(ui, queue, n_units, &u)) {
+      const int u = u_next;
+      if (!ur.publish_unit(ui, u)) {
         set_status(status, kStatusTimeoutEmpty);
         drain(full, it, kStages);
         return;
       }
       if (u < 0) break;
-      const int e = tb.active[u / UR], rb = u % UR;
+      u_next = ur.ticket(queue, n_units);
+      const int e = tb.active[u / UR], rbg = u % UR;
       const bool sh = (e == E);
       const int nkc = (sh ? Is : I) / (kKC * KCH);
       const int p0 = tb.offsets[e];
       const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
+      for (int sub = 0; sub < kDnRowBlocks; ++sub) {
+      const int rb = rbg * kDnRowBlocks + sub;
       const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
       for (int nb = 0; nb < n; nb += kActRows) {
+        // passes of at most 8 rows load an 8-row activation box (1 KiB/chunk)
+        const bool small = n - nb <= 8;
+        const CUtensorMap* mh = small ? &tm_h8 : &tm_h;
+        const uint32_t hbytes = small ? 8 * kKC * 2 : kActChunkBytes;
         for (int kc = 0; kc < nkc; ++kc, ++it) {
           const int s = it % kStages;
           if (it >= uint32_t(kStages) && !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1)) {
@@ -327,16 +348,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
             drain(full, it, kStages);
             return;
           }
-          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          mbar_arrive_expect_tx(&full[s], KCH * (kBoxBytes + hbytes));
           uint8_t* dst = smem + s * C::kStageBytes;
 #pragma unroll
           for (int j = 0; j < KCH; ++j) {
             const int k = (kc * KCH + j) * kKC;
             tma_load_2d_hint(dst + j * kBoxBytes, m, k, row, &full[s], pol);
-            tma_load_2d(dst + KCH * kBoxBytes + j * kActChunkBytes, &tm_h, k, p0 + nb, &full[s]);
+            tma_load_2d(dst + KCH * kBoxBytes + j * kActChunkBytes, mh, k, p0 + nb, &full[s]);
           }
         }
       }
+      }  // sub
     }
     return;
   }
@@ -352,11 +374,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
       return;
     }
     if (u < 0) break;
-    const int e = tb.active[u / UR], rb = u % UR;
+    const int e = tb.active[u / UR], rbg = u % UR;
     const bool sh = (e == E);
     const int nkc = (sh ? Is : I) / (kKC * KCH);
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
+    for (int sub = 0; sub < kDnRowBlocks; ++sub) {
+    const int rb = rbg * kDnRowBlocks + sub;
     for (int nb = 0; nb < n; nb += kActRows) {
       const int ng = min(4, (n - nb + 7) / 8);
       float acc[4][4] = {};
@@ -416,6 +440,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
         }
       }
     }
+    }  // sub
   }
   if (ep.world > 0) {
     // All of this warp's peer stores are made visible system-wide before it
@@ -535,7 +560,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
   float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
   const int kg = fit_kch(g_kch_gu, d.H, d.H);
   const int kd = fit_kch(g_kch_dn, d.I, d.Is);
-  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h;
+  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h, tm_h8;
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t R = T * d.K + T, ldh = d.ldh;
   if (!make_tmap_bf16_2d(&tm_gu, w_gate_up, H, E * 2 * I, H * 2, kKC, kUnitRows) ||
@@ -544,7 +569,8 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kKC, kUnitRows) ||
       !make_tmap_bf16_2d(&tm_x, x, H, T, H * 2, kKC * kg, 1, /*swizzle128=*/false) ||
-      !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kKC, kActRows))
+      !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kKC, kActRows) ||
+      !make_tmap_bf16_2d(&tm_h8, ws.h, ldh, R, ldh * 2, kKC, 8))
     return cudaErrorInvalidValue;
   ExpertTables tb{ws.active, ws.n_active, ws.offsets, ws.sorted_tok, ws.pair_dst, ws.pair_w};
   int* status = ws.status + 1;
@@ -553,7 +579,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
 #define PMOE_DN(KCH)                                                                  \
   down_tma_kernel<KCH><<<g_num_sms, kStreamThreads, DnCfg<KCH>::kSmem, st>>>(         \
-      tm_dn, tm_sd, tm_h, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep)
+      tm_dn, tm_sd, tm_h, tm_h8, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep)
   if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
