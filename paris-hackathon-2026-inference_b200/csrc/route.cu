@@ -127,6 +127,64 @@ __device__ __forceinline__ void warp_topk(const float* row, bool round_logits, i
   if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-row[E]));
 }
 
+// The same selection for NT tokens per warp (t_first + i * t_stride), their
+// K rounds interleaved so the warp reductions of different tokens overlap.
+template <int NT>
+__device__ __forceinline__ void warp_topk_multi(const float* lg, int Rpad, int t_first,
+                                                int t_stride, int T, int E, int K,
+                                                int32_t* __restrict__ topk_idx,
+                                                float* __restrict__ topk_w,
+                                                float* __restrict__ shared_gate, int* cnt) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[NT][8], mine[NT];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int t = t_first + i * t_stride;
+    mine[i] = 0u;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = j * 32 + lane;
+      key[i][j] = (t < T && e < E)
+                      ? (bf16_key(lg[size_t(t) * Rpad + e]) << 16) | uint32_t(0xFFFF - e)
+                      : 0u;
+    }
+  }
+  for (int k = 0; k < K; ++k) {
+    uint32_t wm[NT];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      uint32_t m = key[i][0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) m = max(m, key[i][j]);
+      wm[i] = __reduce_max_sync(0xffffffffu, m);
+    }
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (key[i][j] == wm[i]) key[i][j] = 0u;
+      if (lane == k) mine[i] = wm[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int t = t_first + i * t_stride;
+    if (t >= T) continue;  // warp-uniform
+    const float l0 = key_value(__shfl_sync(0xffffffffu, mine[i], 0));
+    const float ex = lane < K ? __expf(key_value(mine[i]) - l0) : 0.f;
+    float den = ex;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane < K) {
+      const int e = 0xFFFF - int(mine[i] & 0xFFFFu);
+      topk_idx[size_t(t) * K + lane] = e;
+      topk_w[size_t(t) * K + lane] = ex / den;
+      atomicAdd(&cnt[e], 1);
+    }
+    if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-lg[size_t(t) * Rpad + E]));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Block-level CSR dispatch (any blockDim that is a multiple of 32, >= E).
 //  1. exclusive scan of counts -> offsets[0..E]; offsets[E+1] = P + T
@@ -311,8 +369,8 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   for (int i = tid; i < T * Rpad / 4; i += kFusedRouteThreads) dst[i] = __ldcg(src + i);
   for (int e = tid; e < E; e += kFusedRouteThreads) s_cnt[e] = 0;
   __syncthreads();
-  for (int t = warp; t < T; t += kFusedRouteWarps)
-    warp_topk(s_lg + size_t(t) * Rpad, false, t, E, K, s_idx, s_w, s_sg, s_cnt);
+  static_assert(kFusedRouteMaxT <= 4 * kFusedRouteWarps, "4 tokens per warp");
+  warp_topk_multi<4>(s_lg, Rpad, warp, kFusedRouteWarps, T, E, K, s_idx, s_w, s_sg, s_cnt);
   __syncthreads();
   block_dispatch(s_cnt, s_idx, s_w, s_sg, T, E, K, lo, hi, with_shared, with_routed, o, s_off,
                  s_cur, s_wsum, s_tot, s_wcnt);
