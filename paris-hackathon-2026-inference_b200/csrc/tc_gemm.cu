@@ -20,6 +20,8 @@
 //            routed combine of moe_grouped_mlp.py:152-163 / the index_add_ of
 //            modeling_qwen3_5_moe.py:748-749, summed in fp32).
 // The shared expert is expert index E: rows P..P+T-1, weight = its sigmoid gate.
+#include <cstdlib>
+
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tc.cuh"
@@ -31,7 +33,8 @@ constexpr int kTcStages = 4;
 constexpr int kABytes = kBM * kBK * 2;   // 16 KiB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KiB
 constexpr int kTcStageBytes = kABytes + kBBytes;
-constexpr int kEpiStage = 4 * 32 * 33 * 4;  // down epilogue: one 32x33 fp32 tile per warp
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half the columns
+constexpr int kEpiStage = kEpiWarps * 32 * 33 * 4;  // down epilogue: one 32x33 fp32 tile per warp
 constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256 + kEpiStage;
 constexpr uint32_t kTmemCols = 512;      // two 256-column fp32 accumulators
 constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN);
@@ -47,7 +50,7 @@ struct TileTables {
 
 template <int MODE>
 struct TcCfg {
-  static constexpr int kWarps = MODE == kGateUp ? 10 : 6;
+  static constexpr int kWarps = MODE == kGateUp ? 2 + kEpiWarps + 4 : 2 + kEpiWarps;
   static constexpr int kThreads = 32 * kWarps;
   static constexpr uint32_t kFullCount = MODE == kGateUp ? 1 + 128 : 1;
 };
@@ -81,7 +84,7 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);
     }
     mbar_fence_init();
   }
@@ -177,9 +180,10 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
         umma_commit(&tfull[b]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + kEpiWarps) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;                // TMEM lane quadrant of this warp
+    const int half = (warp - 2) / 4;      // which half of the tile columns
     const int r = q * 32 + lane;           // tile row of this thread
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
         const int j0 = nb * (kBN / 2);
         __nv_bfloat16* hrow = h + size_t(row0 + r) * ldh + j0;
 #pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {
           uint32_t gv[32], uv[32];
           tmem_ld32(taddr + cc * 32, gv);
           tmem_ld32(taddr + 128 + cc * 32, uv);
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
         float* stg = reinterpret_cast<float*>(smem + kTcStages * kTcStageBytes + 256) +
                      (warp - 2) * 32 * 33;
 #pragma unroll 1
-        for (int cc = 0; cc < kBN / 32; ++cc) {
+        for (int cc = 4 * half; cc < 4 * half + 4; ++cc) {
           uint32_t v[32];
           tmem_ld32(taddr + cc * 32, v);
           tmem_ld_wait();
@@ -262,7 +266,7 @@ __global__ void __launch_bounds__(TcCfg<MODE>::kThreads, 1) tc_grouped_kernel(
     }
   } else if (MODE == kGateUp) {
     // ---------------- A gather (128 threads, one tile row each) ----------------
-    const int r = threadIdx.x - 6 * 32;
+    const int r = threadIdx.x - (2 + kEpiWarps) * 32;
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -381,6 +385,10 @@ int g_tc_sms = 148;
 
 cudaError_t tc_init(int num_sms) {
   g_tc_sms = num_sms;
+  if (const char* v = std::getenv("PMOE_TC_GRID")) {  // experiment knob: fewer persistent CTAs
+    const int n = std::atoi(v);
+    if (n > 0 && n < num_sms) g_tc_sms = n;
+  }
   cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<kGateUp>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   if (e != cudaSuccess) return e;
