@@ -28,9 +28,12 @@ struct Workspace {
   int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
+  __nv_bfloat16* x_perm; // [T*K+T][H] x rows in dispatch order (tensor-core path; aliases
+                         //            `rows`, which only the streaming path uses)
   int4* gu_tiles;       // tensor-core path tile lists: (expert, row0, nrows, n_block)
   int4* dn_tiles;
-  int32_t* tile_counts; // [2]
+  int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
+  int32_t* tile_counts; // [3] gate_up, down, M tiles
   float* y_acc;         // [T][H]     fp32 output accumulator (tensor-core path)
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
@@ -104,10 +107,12 @@ inline Workspace carve(void* base, const Dims& d) {
   w.status = (int32_t*)take(sizeof(int32_t) * 8);
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
   w.rows = (float*)take(sizeof(float) * R * d.H);
+  w.x_perm = reinterpret_cast<__nv_bfloat16*>(w.rows);
   const size_t mt_max = R / 128 + d.E + 2;  // M tiles over all experts, partial ones included
   const int imax = d.I > d.Is ? d.I : d.Is;
   w.gu_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(imax / 128 + 1));
   w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 256 + 1));
+  w.m_tiles = (int4*)take(sizeof(int4) * mt_max);
   w.tile_counts = (int32_t*)take(sizeof(int32_t) * 4);
   w.y_acc = (float*)take(sizeof(float) * size_t(d.T) * d.H);
   const size_t ntile = (size_t(d.T) + 127) / 128;
