@@ -102,7 +102,8 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
   auto cp = [&](void* dst, const void* src, size_t n) {
     return dst ? cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, st) : cudaSuccess;
   };
-  if (cp(topk_idx, ws.topk_idx, P * 4) != cudaSuccess || cp(topk_w, ws.topk_w, P * 4) != cudaSuccess ||
+  if (cp(topk_idx, ws.topk_idx, P * 4) != cudaSuccess ||
+      cp(topk_w, ws.topk_w, P * 4) != cudaSuccess ||
       cp(offsets, ws.offsets, size_t(E + 1) * 4) != cudaSuccess ||
       cp(sorted_tok, ws.sorted_tok, P * 4) != cudaSuccess ||
       cp(sorted_slot, ws.sorted_slot, P * 4) != cudaSuccess ||
@@ -170,7 +171,8 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     if (launch_tc_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
-                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), !route_tc, st,
+                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), expert_lo,
+                          expert_hi, with_shared, with_routed, st,
                           events && n_events > 2 ? events[2] : nullptr) != cudaSuccess)
       return PMOE_ERR_CUDA;
     if (mark(3) != cudaSuccess || mark(4) != cudaSuccess) return PMOE_ERR_CUDA;

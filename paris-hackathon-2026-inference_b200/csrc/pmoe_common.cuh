@@ -30,11 +30,12 @@ struct Workspace {
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
   __nv_bfloat16* x_perm; // [T*K+T][H] x rows in dispatch order (tensor-core path; aliases
                          //            `rows`, which only the streaming path uses)
+  __nv_bfloat16* rows_bf16; // [T*K+T][H] weighted expert outputs, token-major (tensor-core
+                            //  path, written by down after gate_up has consumed x_perm)
   int4* gu_tiles;       // tensor-core path tile lists: (expert, row0, nrows, n_block)
   int4* dn_tiles;
   int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
-  int32_t* tile_counts; // [3] gate_up, down, M tiles
-  float* y_acc;         // [T][H]     fp32 output accumulator (tensor-core path)
+  int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M; [4]/[5] gate_up/down queue tickets
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
@@ -108,13 +109,13 @@ inline Workspace carve(void* base, const Dims& d) {
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
   w.rows = (float*)take(sizeof(float) * R * d.H);
   w.x_perm = reinterpret_cast<__nv_bfloat16*>(w.rows);
+  w.rows_bf16 = reinterpret_cast<__nv_bfloat16*>(w.rows);
   const size_t mt_max = R / 128 + d.E + 2;  // M tiles over all experts, partial ones included
   const int imax = d.I > d.Is ? d.I : d.Is;
-  w.gu_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(imax / 128 + 1));
-  w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 256 + 1));
+  w.gu_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(imax / 64 + 1));
+  w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 128 + 1));
   w.m_tiles = (int4*)take(sizeof(int4) * mt_max);
-  w.tile_counts = (int32_t*)take(sizeof(int32_t) * 4);
-  w.y_acc = (float*)take(sizeof(float) * size_t(d.T) * d.H);
+  w.tile_counts = (int32_t*)take(sizeof(int32_t) * 8);
   const size_t ntile = (size_t(d.T) + 127) / 128;
   w.hist = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
   w.hist_base = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
@@ -162,7 +163,9 @@ __device__ __forceinline__ void mma_k32(float (&d)[4], const uint4& wa, const ui
   mma16816(d, wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+// silu(g) = g * sigmoid(g); fast division (for g << 0 the denominator
+// overflows to +inf and the quotient is 0, the limit).
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));

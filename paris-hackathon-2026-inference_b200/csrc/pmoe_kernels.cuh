@@ -23,8 +23,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, bool zero_acc, cudaStream_t st,
-                              void* mid_event);
+                              __nv_bfloat16* y, int lo, int hi, int with_shared,
+                              int with_routed, cudaStream_t st, void* mid_event);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch); also zeroes the fp32 output accumulator.

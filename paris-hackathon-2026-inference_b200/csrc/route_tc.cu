@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
     const float* __restrict__ shared_gate, const int32_t* __restrict__ base, int T, int H, int E,
     int K, int sh_lo, int sh_hi, int32_t* __restrict__ sorted_tok,
     int32_t* __restrict__ sorted_slot,
-    int32_t* __restrict__ pair_dst, float* __restrict__ pair_w, float* __restrict__ y_acc) {
+    int32_t* __restrict__ pair_dst, float* __restrict__ pair_w) {
   __shared__ int s_wcnt[32 * 256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const int P = T * K;
@@ -312,11 +312,6 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
       pair_w[P + t - sh_lo] = shared_gate[t];
     }
   }
-  // zero this tile's rows of the fp32 output accumulator
-  const int rows = min(kRtM, T - tb);
-  float4* acc = reinterpret_cast<float4*>(y_acc + size_t(tb) * H);
-  const int n4 = rows * H / 4;
-  for (int i = tid; i < n4; i += blockDim.x) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 cudaError_t route_tc_init() {
@@ -351,7 +346,7 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
                                                   ws.hist_base, d.T, d.H, d.E, d.K, d.sh_lo,
                                                   d.sh_hi,
                                                   ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
-                                                  ws.pair_w, ws.y_acc);
+                                                  ws.pair_w);
   return cudaGetLastError();
 }
 

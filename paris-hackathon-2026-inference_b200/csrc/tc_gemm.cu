@@ -1,56 +1,62 @@
 // tcgen05 grouped GEMMs for the compute-bound prefill regime (large T).
 //
-// gather_rows_kernel: x_perm[p] = x[sorted_tok[p]] for every dispatched row
-// of a planned gate_up tile, written once so that the GEMM loads A with
-// whole-tile TMA copies.  (Row gathers inside the GEMM, by cp.async or by
-// 4-row TMA gathers, cost more than this copy: each 128-row A tile is read
-// once per N block.)
-// tc_grouped_kernel: persistent, warp-specialised, over a tile list
-// (expert, first dispatched row, rows, N block) built on the device:
-//     warp 0        TMA producer: A (x_perm for gate_up, h for down) and B
-//                   (expert weights), 128-byte swizzle, one mbarrier per stage
-//     warp 1        TMEM owner + single-thread tcgen05.mma issuer
-//     warps 2..9    epilogue: TMEM -> registers -> global; two warps per TMEM
-//                   lane quadrant, each owning half of the tile's columns
-// Tiles are 128 (dispatched rows) x 256 (output columns), K staged 64 at a
-// time through a 4-deep ring of 48 KiB stages; the fp32 accumulator is
-// double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile
-// overlaps the main loop of the next.  Tiles are ordered (expert, M block,
-// N block), so the N blocks of one M block run side by side and share A in L2.
+//   plan_tiles_kernel   tile lists for both GEMMs from the dispatch offsets
+//   gather_rows_kernel  x_perm[p] = x[sorted_tok[p]] for every dispatched row
+//                       of a computed expert, once, so that the GEMM loads its
+//                       B operand with tiled TMA copies (row gathers inside the
+//                       GEMM, by cp.async or 4-row TMA gathers, cost more:
+//                       every row block is read once per feature block)
+//   tc_pair_kernel      the expert GEMM, persistent, warp-specialised, on CTA
+//                       pairs (cta_group::2):
+//     warp 0        TMA producer, 128-byte swizzle, a 6-deep ring of 32 KiB
+//                   stages per CTA
+//     warp 1        TMEM owner (both CTAs) + single-thread MMA issuer (even CTA)
+//     warps 2..17   epilogue: TMEM -> registers -> global; four warps per
+//                   TMEM lane quadrant, each owning 64 of the tile's columns
+//   combine_rows_kernel y = bf16(sum of each token's expert rows)
+// The fp32 accumulator is double-buffered in TMEM (2 x 256 columns) so the
+// epilogue of one tile overlaps the main loop of the next.
 //
-//   gate_up: N block = 128 gate rows + the 128 matching up rows of the
-//            expert; epilogue h = bf16(silu(gate) * up)   (Qwen3_5MoeExperts
+//   gate_up: epilogue h = bf16(silu(gate) * up)   (Qwen3_5MoeExperts
 //            :743-746, SiLU per configuration_qwen3_5_moe.py:84)
-//   down:    N block = 256 output columns; epilogue adds w * row to the
-//            token's fp32 accumulator with red.global.add.v4.f32 (the
-//            routed combine of moe_grouped_mlp.py:152-163 / the index_add_ of
-//            modeling_qwen3_5_moe.py:748-749, summed in fp32).
+//   down:    epilogue writes bf16(w * row) to the pair's token-major row;
+//            the combine then sums each token's rows in fp32 (the routed
+//            combine of moe_grouped_mlp.py:152-163 / the index_add_ of
+//            modeling_qwen3_5_moe.py:748-749).  Plain stores: fp32 atomic
+//            adds of every output row into L2 were the down GEMM's limit.
 // The shared expert is expert index E: rows P.. of the dispatch, one per
 // token of its range, weight = its sigmoid gate.
+
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tc.cuh"
 
 namespace pmoe {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kTcStages = 4;
-constexpr int kABytes = kBM * kBK * 2;   // 16 KiB
-constexpr int kBBytes = kBN * kBK * 2;   // 32 KiB
-constexpr int kTcStageBytes = kABytes + kBBytes;
-constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each owning half the columns
-constexpr int kEpiStage = kEpiWarps * 32 * 33 * 4;  // down epilogue: one 32x33 fp32 tile per warp
-constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256 + kEpiStage;
+constexpr int kBM = 128;                  // weight rows per CTA (the pair MMA has M = 256)
+constexpr int kBK = 64;                   // K per stage (one 128-byte swizzle atom)
+constexpr int kTok = 256;                 // dispatched rows per tile (UMMA N <= 256)
+constexpr int kHalfTok = kTok / 2;        // rows of B staged by each CTA of the pair
+constexpr int kGatherRows = 128;          // rows per x_perm copy block
+constexpr int kTcStages = 6;
+constexpr int kWBytes = kBM * kBK * 2;    // 16 KiB: this CTA's half of A (weights)
+constexpr int kRowBytes = kHalfTok * kBK * 2;  // 16 KiB: this CTA's half of B (rows)
+constexpr int kRowChunk = 32;             // rows per small B copy
+constexpr int kTcStageBytes = kWBytes + kRowBytes;  // 32 KiB
+constexpr int kEpiWarps = 16;  // four per TMEM lane quadrant, each owning 64 columns
+constexpr int kEpiWarpBytes = 32 * 16 * 2;  // per-warp gate_up staging tile (bf16 32 x 16)
+constexpr int kBarBytes = 256;            // mbarriers + TMEM slot
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps * kEpiWarpBytes;
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
-constexpr uint32_t kTmemCols = 512;      // two 256-column fp32 accumulators
-constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN);
+constexpr uint32_t kTmemCols = 512;       // two 256-column fp32 accumulators
+static_assert(kTcSmem <= 227 * 1024, "shared memory");
 
 enum TcMode { kGateUp = 0, kDown = 1 };
 
 struct TileTables {
-  const int4* tiles;     // (expert, row0, nrows, n_block)
+  const int4* tiles;     // (expert, row0, nrows, feature block)
   const int32_t* count;  // number of tiles
-  const int32_t* sorted_tok;
+  const int32_t* pair_dst;  // token-major output row of each dispatched row
   const float* pair_w;
 };
 
@@ -60,14 +66,38 @@ __device__ __forceinline__ uint8_t* tc_align1024(uint8_t* p) {
 
 __device__ __forceinline__ void tc_status(int* status, int code) { atomicCAS(status, 0, code); }
 
-// tm_b: routed weights, tm_b_sh0/1: shared-expert weights, tm_a: A (x_perm
-// for gate_up, h for down).
+// Tile t of the list, or an empty tile past its end (used to fetch the next
+// tile's descriptor one tile ahead).
+__device__ __forceinline__ int4 tile_at(const TileTables& tt, int t, int ntiles) {
+  return t < ntiles ? tt.tiles[t] : make_int4(0, 0, 0, 0);
+}
+
+// One persistent kernel per GEMM, launched as CTA pairs (clusters of 2).  A
+// pair computes a 256 (weight rows) x N (dispatched rows) tile with
+// cta_group::2 MMAs issued by the even CTA: each CTA stages 128 weight rows
+// (A) and N/2 dispatched rows (B) per K step, and holds its 128 accumulator
+// rows x N columns in its own TMEM.  N is the tile's rows rounded up to 16,
+// so an expert's last tile wastes at most 15 rows of MMA work, and only the
+// 32-row chunks of B holding its rows are loaded.
+//   gate_up: a pair tile covers 128 features; each CTA's A is 64 features as
+//            four groups of 16 gate rows each followed by the matching 16 up
+//            rows (a 5-D tensor-map box over the [E][2I][H] weights), so TMEM
+//            lane l < 16 of a quadrant holds the gate and lane l + 16 the up
+//            value of the same feature.  B = x_perm rows.
+//   down:    a pair tile covers 256 output features; B = h rows.
+// Every CTA's producer signals the even CTA's stage barrier; the MMA commit
+// releases the stage in both CTAs; both CTAs' epilogue warps release the
+// accumulator on the even CTA's barrier.
+// tm_b: routed weights (5-D for gate_up), tm_b_sh0/1: shared-expert weights
+// (16-row boxes for gate_up), tm_a / tm_a32: the dispatched rows (x_perm for
+// gate_up, h for down) in 128- and 32-row boxes.
 template <int MODE>
-__global__ void __launch_bounds__(kTcThreads, 1) tc_grouped_kernel(
+__global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b_sh0,
     const __grid_constant__ CUtensorMap tm_b_sh1, const __grid_constant__ CUtensorMap tm_a,
-    TileTables tt, int H, int E, int I, int Is,
-    int ldh, __nv_bfloat16* __restrict__ h, float* __restrict__ y_acc, int* __restrict__ status) {
+    const __grid_constant__ CUtensorMap tm_a32, TileTables tt, int H, int E, int I, int Is,
+    int ldh, __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ out_rows,
+    int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = tc_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
@@ -76,6 +106,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_grouped_kernel(
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -84,34 +116,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_grouped_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
     }
     mbar_fence_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int ntiles = tt.count[0];
   const uint32_t sbase = smem_u32(smem);
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_a);
+      const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // even CTA's stage barriers
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int4 tl = tt.tiles[t];
-        const int e = tl.x, row0 = tl.y, nb = tl.w;
+      int4 tl_next = tile_at(tt, pair, ntiles);
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        const int4 tl = tl_next;
+        tl_next = tile_at(tt, t + npairs, ntiles);
+        const int e = tl.x;
+        const int nh = ((tl.z + 15) & ~15) / 2;        // rows of B in this CTA
+        const int r0 = tl.y + int(rank) * nh;
         const bool sh = (e == E);
         const int Ke = MODE == kGateUp ? H : (sh ? Is : I);
         const int nk = Ke / kBK;
+        const int nchunks = (nh + kRowChunk - 1) / kRowChunk;
+        const bool whole = nh > kHalfTok / 2;  // one 128-row box, else 32-row boxes
+        const uint32_t tx = kWBytes + (whole ? kHalfTok : nchunks * kRowChunk) * kBK * 2;
+        const int f0 = MODE == kGateUp ? tl.w * 128 + 64 * int(rank) : tl.w * 256 + 128 * int(rank);
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kTcStages;
           if (it >= uint32_t(kTcStages) && !mbar_wait(&empty[s], ((it / kTcStages) & 1) ^ 1)) {
@@ -119,45 +160,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_grouped_kernel(
             ok = false;
             break;
           }
-          uint8_t* sa = smem + s * kTcStageBytes;
-          uint8_t* sb = sa + kABytes;
-          mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
-          tma_load_2d(sa, &tm_a, kc * kBK, row0, &full[s]);
+          uint8_t* st = smem + s * kTcStageBytes;
+          const uint32_t fb = full0 + s * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * tx);
           if (MODE == kGateUp) {
-            const int j0 = nb * (kBN / 2);
             if (sh) {
-              tma_load_2d(sb, &tm_b_sh0, kc * kBK, j0, &full[s]);
-              tma_load_2d(sb + kBBytes / 2, &tm_b_sh1, kc * kBK, j0, &full[s]);
+              for (int g = 0; g < 4; ++g) {
+                tma_load_2d_pair(st + g * 4096, &tm_b_sh0, kc * kBK, f0 + 16 * g, fb);
+                tma_load_2d_pair(st + g * 4096 + 2048, &tm_b_sh1, kc * kBK, f0 + 16 * g, fb);
+              }
             } else {
-              tma_load_2d(sb, &tm_b, kc * kBK, e * 2 * I + j0, &full[s]);
-              tma_load_2d(sb + kBBytes / 2, &tm_b, kc * kBK, e * 2 * I + I + j0, &full[s]);
+              tma_load_5d_pair(st, &tm_b, kc * kBK, 0, 0, f0 / 16, e, fb);
             }
           } else {
-            const int n0 = nb * kBN;
             if (sh)
-              tma_load_2d(sb, &tm_b_sh0, kc * kBK, n0, &full[s]);
+              tma_load_2d_pair(st, &tm_b_sh0, kc * kBK, f0, fb);
             else
-              tma_load_2d(sb, &tm_b, kc * kBK, e * H + n0, &full[s]);
+              tma_load_2d_pair(st, &tm_b, kc * kBK, e * H + f0, fb);
+          }
+          if (whole) {
+            tma_load_2d_pair(st + kWBytes, &tm_a, kc * kBK, r0, fb);
+          } else {
+            for (int j = 0; j < nchunks; ++j)
+              tma_load_2d_pair(st + kWBytes + j * kRowChunk * kBK * 2, &tm_a32, kc * kBK,
+                               r0 + j * kRowChunk, fb);
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
       uint32_t it = 0, lt = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
-        const int4 tl = tt.tiles[t];
+      int4 tl_next = tile_at(tt, pair, ntiles);
+      for (int t = pair; t < ntiles; t += npairs, ++lt) {
+        const int4 tl = tl_next;
+        tl_next = tile_at(tt, t + npairs, ntiles);
         const bool sh = (tl.x == E);
         const int Ke = MODE == kGateUp ? H : (sh ? Is : I);
         const int nk = Ke / kBK;
+        const uint32_t idesc = idesc_bf16_f32(2 * kBM, (tl.z + 15) & ~15);
         const uint32_t b = lt & 1, use = lt >> 1;
-        if (lt >= 2 && !mbar_wait(&tempty[b], (use - 1) & 1)) {
+        if (lt >= 2 && !mbar_wait_cluster(&tempty[b], (use - 1) & 1)) {
           tc_status(status, kStatusTimeoutTmem);
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * kBN;
+        const uint32_t d_tmem = tmem_base + b * 256;
         bool ok = true;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kTcStages;
@@ -167,173 +216,185 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_grouped_kernel(
             break;
           }
           tc_fence_after();
-          const uint32_t sa = sbase + s * kTcStageBytes, sb = sa + kABytes;
-          const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sb);
+          const uint32_t st = sbase + s * kTcStageBytes;
+          const uint64_t wd = sdesc_k_sw128(st), rd = sdesc_k_sw128(st + kWBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16(d_tmem, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), kIdesc,
-                      (kc | kk) != 0 ? 1u : 0u);
-          umma_commit(&empty[s]);
+            umma_bf16_pair(d_tmem, wd + uint64_t(kk * 2), rd + uint64_t(kk * 2), idesc,
+                           (kc | kk) != 0 ? 1u : 0u);
+          umma_commit_pair_both(&empty[s]);
         }
         if (!ok) break;
-        umma_commit(&tfull[b]);
+        umma_commit_pair_both(&tfull[b]);
       }
     }
   } else {
-    // ---------------- epilogue ----------------
-    const int q = warp & 3;                // TMEM lane quadrant of this warp
-    const int half = (warp - 2) / 4;      // which half of the tile columns
-    const int r = q * 32 + lane;           // tile row of this thread
+    // ---------------- epilogue (both CTAs) ----------------
+    // Warp (q, quarter): this CTA's weight rows q*32 .. q*32+31 (its TMEM
+    // lane quadrant), tile columns quarter*64 .. +63.
+    const int q = warp & 3;
+    const int quarter = (warp - 2) / 4;
+    const int cw = quarter * 64;
+    uint8_t* stg_raw = smem + kTcStages * kTcStageBytes + kBarBytes + (warp - 2) * kEpiWarpBytes;
+    const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     uint32_t lt = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
-      const int4 tl = tt.tiles[t];
-      const int row0 = tl.y, nrows = tl.z, nb = tl.w;
+    int4 tl_next = tile_at(tt, pair, ntiles);
+    for (int t = pair; t < ntiles; t += npairs, ++lt) {
+      const int4 tl = tl_next;
+      tl_next = tile_at(tt, t + npairs, ntiles);
+      const int row0 = tl.y, nrows = tl.z;
       const uint32_t b = lt & 1, use = lt >> 1;
+      // down: this lane's output rows of the two 32-row chunks, loaded
+      // before the accumulator wait so their latency overlaps it.
+      int ldst[2] = {0, 0};
+      if (MODE == kDown) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int r = cw + 32 * k + lane;
+          if (r < nrows) ldst[k] = tt.pair_dst[row0 + r];
+        }
+      }
       if (!mbar_wait(&tfull[b], use & 1)) {
         tc_status(status, kStatusTimeoutTmem);
         break;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + b * kBN;
-      const bool valid = r < nrows;
+      const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + b * 256;
       if (MODE == kGateUp) {
-        const int j0 = nb * (kBN / 2);
-        __nv_bfloat16* hrow = h + size_t(row0 + r) * ldh + j0;
-#pragma unroll 1
-        for (int cc = 2 * half; cc < 2 * half + 2; ++cc) {
-          uint32_t gv[32], uv[32];
-          tmem_ld32(taddr + cc * 32, gv);
-          tmem_ld32(taddr + 128 + cc * 32, uv);
+        // Quadrant q holds features f0 .. f0+15: lanes 0-15 their gate rows,
+        // lanes 16-31 their up rows.  Per 32-row chunk, lane l < 16 forms
+        // h for rows 0-15 and lane l + 16 for rows 16-31 (one shuffle per
+        // value), then a 32 x 16 transpose in shared memory gives each row's
+        // 32 bytes of h to one lane.
+        const int f0 = tl.w * 128 + 64 * int(rank) + q * 16;
+        const int fl = lane & 15, hi = lane >> 4;
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(stg_raw);  // [32 rows][16]
+        if (cw < nrows) {
+          uint32_t v[2][32];  // 64 columns: two loads, one wait
+          tmem_ld32(taddr + cw, v[0]);
+          tmem_ld32(taddr + cw + 32, v[1]);
           tmem_ld_wait();
-          if (valid) {
-            uint32_t packed[16];
+#pragma unroll
+          for (int sub = 0; sub < 2; ++sub) {
+            const int c = cw + 32 * sub;
+            if (c >= nrows) break;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float a0 = silu_f(__uint_as_float(gv[2 * i])) * __uint_as_float(uv[2 * i]);
-              const float a1 =
-                  silu_f(__uint_as_float(gv[2 * i + 1])) * __uint_as_float(uv[2 * i + 1]);
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(a0, a1);
-              packed[i] = *reinterpret_cast<uint32_t*>(&v2);
+              const float mine = __uint_as_float(hi ? v[sub][i] : v[sub][16 + i]);
+              const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+              const float g = hi ? other : __uint_as_float(v[sub][i]);
+              const float u = hi ? __uint_as_float(v[sub][16 + i]) : other;
+              stg[(hi * 16 + i) * 16 + fl] = __float2bfloat16_rn(silu_f(g) * u);
             }
-            uint4* dst = reinterpret_cast<uint4*>(hrow + cc * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                                  packed[4 * i + 3]);
+            __syncwarp();
+            if (c + lane < nrows) {
+              const uint4* sp = reinterpret_cast<const uint4*>(stg + lane * 16);
+              uint4* dp = reinterpret_cast<uint4*>(h + size_t(row0 + c + lane) * ldh + f0);
+              dp[0] = sp[0];
+              dp[1] = sp[1];
+            }
+            __syncwarp();
           }
         }
       } else {
-        const int n0 = nb * kBN;
-        int tok = 0;
-        float w = 0.f;
-        if (valid) {
-          tok = tt.sorted_tok[row0 + r];
-          w = tt.pair_w[row0 + r];
-        }
-        float* dst = y_acc + size_t(tok) * H + n0;
-        // Per-warp 32x32 staging tile: each reduction instruction then covers
-        // 4 rows x 128 contiguous bytes instead of 32 scattered 16-byte pieces.
-        float* stg = reinterpret_cast<float*>(smem + kTcStages * kTcStageBytes + 256) +
-                     (warp - 2) * 32 * 33;
-#pragma unroll 1
-        for (int cc = 4 * half; cc < 4 * half + 4; ++cc) {
+        // Lane = output feature f0 + lane; per column (dispatched row) the
+        // warp stores 64 contiguous bytes of that row (the routing weight is
+        // applied by the combine).
+        const int f0 = tl.w * 256 + 128 * int(rank) + q * 32;
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+          const int c = cw + 32 * sub;
+          if (c >= nrows) break;
           uint32_t v[32];
-          tmem_ld32(taddr + cc * 32, v);
+          tmem_ld32(taddr + c, v);
           tmem_ld_wait();
+          __nv_bfloat16* col = out_rows + f0 + lane;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = w * __uint_as_float(v[i]);
-          __syncwarp();
-          const int c4 = (lane & 7) * 4;
-#pragma unroll
-          for (int pass = 0; pass < 8; ++pass) {
-            const int rr = pass * 4 + (lane >> 3);
-            float* rdst = reinterpret_cast<float*>(
-                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), rr));
-            const int rvalid = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr);
-            if (rvalid) {
-              const float* sp = stg + rr * 33 + c4;
-              red_add_v4(rdst + cc * 32 + c4, sp[0], sp[1], sp[2], sp[3]);
-            }
+          for (int i = 0; i < 32; ++i) {
+            const int dst = __shfl_sync(0xffffffffu, ldst[sub], i);
+            if (c + i < nrows) col[size_t(dst) * H] = __float2bfloat16_rn(__uint_as_float(v[i]));
           }
-          __syncwarp();
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (lane == 0) mbar_arrive_cluster(tempty0 + b * 8);
     }
   }
 
   __syncwarp();  // reconverge warps whose work ran on one elected lane
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------------------
-// x_perm[p, :] = x[sorted_tok[p], :] for the rows of every M tile (each
-// dispatched row of a computed expert once).  Work item = 16 rows of one M
-// tile, one warp each, 16-byte copies with four in flight per lane.
+// x_perm[p, :] = x[sorted_tok[p], :] for the rows of every M block (each
+// dispatched row of a computed expert once).  Work item = 4 rows of one M
+// block; a warp copies two rows at a time with all of their 16-byte loads in
+// flight before the stores (H/256 loads per lane per row).
 // ---------------------------------------------------------------------------
 constexpr int kGatherThreads = 256;
+constexpr int kGatherItemRows = 4;
+constexpr int kGatherMaxH8 = 8;  // H <= 2048 for the unrolled row copy
 
 __global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(
     const __nv_bfloat16* __restrict__ x, const int4* __restrict__ m_tiles,
     const int32_t* __restrict__ count, const int32_t* __restrict__ sorted_tok, int H,
     __nv_bfloat16* __restrict__ x_perm) {
   const int lane = threadIdx.x & 31;
-  const int nw = count[0] * (kBM / 16);
-  const int h8 = H / 8;
+  constexpr int kItems = kGatherRows / kGatherItemRows;
+  const int nw = count[0] * kItems;
+  const int per_lane = H / 256;  // 16-byte pieces per lane per row
   for (int w = blockIdx.x * (kGatherThreads / 32) + (threadIdx.x >> 5); w < nw;
        w += gridDim.x * (kGatherThreads / 32)) {
-    const int4 tl = m_tiles[w / (kBM / 16)];
-    const int r_end = min(tl.z, (w % (kBM / 16) + 1) * 16);
-    for (int r = (w % (kBM / 16)) * 16; r < r_end; ++r) {
-      const int p = tl.y + r;
-      const uint4* src = reinterpret_cast<const uint4*>(x + size_t(sorted_tok[p]) * H);
-      uint4* dst = reinterpret_cast<uint4*>(x_perm + size_t(p) * H);
-      int i = lane;
-      for (; i + 96 < h8; i += 128) {
-        const uint4 a = __ldg(src + i), b = __ldg(src + i + 32), c = __ldg(src + i + 64),
-                    d = __ldg(src + i + 96);
-        dst[i] = a;
-        dst[i + 32] = b;
-        dst[i + 64] = c;
-        dst[i + 96] = d;
+    const int4 tl = m_tiles[w / kItems];
+    const int r_beg = (w % kItems) * kGatherItemRows;
+    const int r_end = min(tl.z, r_beg + kGatherItemRows);
+    for (int r = r_beg; r < r_end; r += 2) {
+      const bool two = r + 1 < r_end;
+      const int p0 = tl.y + r, p1 = two ? p0 + 1 : p0;
+      const uint4* s0 = reinterpret_cast<const uint4*>(x + size_t(sorted_tok[p0]) * H);
+      const uint4* s1 = reinterpret_cast<const uint4*>(x + size_t(sorted_tok[p1]) * H);
+      uint4 a[kGatherMaxH8], b[kGatherMaxH8];
+#pragma unroll
+      for (int i = 0; i < kGatherMaxH8; ++i) {
+        if (i < per_lane) {
+          a[i] = __ldg(s0 + lane + 32 * i);
+          b[i] = __ldg(s1 + lane + 32 * i);
+        }
       }
-      for (; i < h8; i += 32) dst[i] = __ldg(src + i);
+      uint4* d0 = reinterpret_cast<uint4*>(x_perm + size_t(p0) * H);
+      uint4* d1 = reinterpret_cast<uint4*>(x_perm + size_t(p1) * H);
+#pragma unroll
+      for (int i = 0; i < kGatherMaxH8; ++i) {
+        if (i < per_lane) {
+          d0[lane + 32 * i] = a[i];
+          if (two) d1[lane + 32 * i] = b[i];
+        }
+      }
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Tile planning (one CTA): for every active expert (in the active-list order,
-// the shared expert last) emit its (M block, N block) tiles for both GEMMs.
+// Tile planning (one CTA, one thread per active expert; the shared expert is
+// one of them): the gate_up and down tile lists (pair tiles of up to 256
+// dispatched rows x 128 features for gate_up, x 256 features for down) and
+// the 128-row blocks for the x_perm copy.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 512;
 
-__global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
-    const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-    const int32_t* __restrict__ n_active, int E, int H, int I, int Is, int4* __restrict__ gu_tiles,
-    int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles, int32_t* __restrict__ counts) {
-  __shared__ int s_wsum[3][32];
+// Exclusive block-wide scan of NV values per thread; totals[k] = sum.
+template <int NV>
+__device__ __forceinline__ void plan_scan(int (&v)[NV], int (&ex)[NV], int (*s_wsum)[32],
+                                          int* totals) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int na = n_active[0];
-  int e = -1, n = 0, p0 = 0, mt = 0, nb_gu = 0, nb_dn = H / kBN;
-  if (tid < na) {
-    e = active[tid];
-    p0 = offsets[e];
-    n = offsets[e + 1] - p0;
-    mt = (n + kBM - 1) / kBM;
-    nb_gu = (e == E ? Is : I) / (kBN / 2);
-  }
-  int v[3] = {mt * nb_gu, mt * nb_dn, mt};
-  int ex[3];
-  // block exclusive scan of the three tile counts
-  for (int k = 0; k < 3; ++k) {
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
     int incl = v[k];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -345,7 +406,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
   }
   __syncthreads();
   if (warp == 0) {
-    for (int k = 0; k < 3; ++k) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
       const int s = lane < kPlanThreads / 32 ? s_wsum[k][lane] : 0;
       int incl = s;
 #pragma unroll
@@ -354,96 +416,207 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
         if (lane >= o) incl += y;
       }
       if (lane < kPlanThreads / 32) s_wsum[k][lane] = incl - s;
-      if (lane == 31) counts[k] = incl;
+      if (lane == 31) totals[k] = incl;
     }
   }
   __syncthreads();
+#pragma unroll
+  for (int k = 0; k < NV; ++k) ex[k] += s_wsum[k][warp];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+    const int32_t* __restrict__ n_active, int E, int H, int I, int Is, int4* __restrict__ gu_tiles,
+    int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles, int32_t* __restrict__ counts) {
+  __shared__ int s_wsum[3][32];
+  __shared__ int s_tot[3];
+  __shared__ int4 s_ex[kPlanThreads];       // (expert, p0, rows, gate_up feature blocks)
+  __shared__ int4 s_base[kPlanThreads];     // first gate_up / down tile, first M block
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int na = n_active[0];
+  const int nb_dn = H / 256;
+  int e = -1, n = 0, p0 = 0, nbg = 0;
   if (tid < na) {
-    int base = s_wsum[0][warp] + ex[0];
-    for (int m = 0; m < mt; ++m)
-      for (int nb = 0; nb < nb_gu; ++nb)
-        gu_tiles[base++] = make_int4(e, p0 + m * kBM, min(kBM, n - m * kBM), nb);
-    base = s_wsum[1][warp] + ex[1];
-    for (int m = 0; m < mt; ++m)
-      for (int nb = 0; nb < nb_dn; ++nb)
-        dn_tiles[base++] = make_int4(e, p0 + m * kBM, min(kBM, n - m * kBM), nb);
-    base = s_wsum[2][warp] + ex[2];
-    for (int m = 0; m < mt; ++m)
-      m_tiles[base++] = make_int4(e, p0 + m * kBM, min(kBM, n - m * kBM), 0);
+    e = active[tid];
+    p0 = offsets[e];
+    n = offsets[e + 1] - p0;
+    nbg = (e == E ? Is : I) / 128;
+  }
+  // Tiles per expert: its 256-row blocks (the last one partial) x feature
+  // blocks, row block outer, experts in active-list order.
+  const int mt = (n + kTok - 1) / kTok;
+  int v[3] = {mt * nbg, mt * nb_dn, (n + kGatherRows - 1) / kGatherRows};
+  int ex[3];
+  plan_scan<3>(v, ex, s_wsum, s_tot);
+  s_ex[tid] = make_int4(e, p0, n, nbg);
+  s_base[tid] = make_int4(ex[0], ex[1], ex[2], 0);
+  if (tid == 0) {
+    counts[0] = s_tot[0];
+    counts[1] = s_tot[1];
+    counts[2] = s_tot[2];
+  }
+  __syncthreads();
+  // Write-out: one warp per active expert, lanes striding over its tiles.
+  for (int a = warp; a < na; a += kPlanThreads / 32) {
+    const int4 x = s_ex[a], bs = s_base[a];
+    const int mts = (x.z + kTok - 1) / kTok;
+    for (int i = lane; i < mts * x.w; i += 32) {
+      const int m = i / x.w;
+      gu_tiles[bs.x + i] = make_int4(x.x, x.y + m * kTok, min(kTok, x.z - m * kTok), i % x.w);
+    }
+    for (int i = lane; i < mts * nb_dn; i += 32) {
+      const int m = i / nb_dn;
+      dn_tiles[bs.y + i] = make_int4(x.x, x.y + m * kTok, min(kTok, x.z - m * kTok), i % nb_dn);
+    }
+    const int mgs = (x.z + kGatherRows - 1) / kGatherRows;
+    for (int m = lane; m < mgs; m += 32)
+      m_tiles[bs.z + m] = make_int4(x.x, x.y + m * kGatherRows,
+                                    min(kGatherRows, x.z - m * kGatherRows), 0);
   }
 }
 
-// y = bf16(y_acc)
-__global__ void __launch_bounds__(256) finalize_kernel(const float* __restrict__ y_acc, long n4,
-                                                       __nv_bfloat16* __restrict__ y) {
+// y[t, :] = bf16( sum_{s<K, expert in [lo,hi)} w[t,s] * rows[t*K+s, :]
+//                  + g[t] * rows[T*K+t, :] )
+// over the bf16 expert rows the down GEMM wrote (routing weights w, shared
+// gate g), in fp32 in a fixed order (the shared row for tokens in
+// [sh_lo, sh_hi)).  One thread per 8 columns.
+__global__ void __launch_bounds__(256) combine_rows_kernel(
+    const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ topk_idx,
+    const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
+    int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    __nv_bfloat16* __restrict__ y) {
   const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  const float4 v = reinterpret_cast<const float4*>(y_acc)[i];
-  __nv_bfloat162 lo2 = __floats2bfloat162_rn(v.x, v.y);
-  __nv_bfloat162 hi2 = __floats2bfloat162_rn(v.z, v.w);
-  uint2 packed;
-  packed.x = *reinterpret_cast<uint32_t*>(&lo2);
-  packed.y = *reinterpret_cast<uint32_t*>(&hi2);
-  reinterpret_cast<uint2*>(y)[i] = packed;
+  const int cols8 = H / 8;
+  if (i >= long(T) * cols8) return;
+  const int t = int(i / cols8), c8 = int(i % cols8);
+  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  auto add = [&](size_t row, float w) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(rows + row * H) + c8);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(b2[j]);
+      s[2 * j] = fmaf(w, f.x, s[2 * j]);
+      s[2 * j + 1] = fmaf(w, f.y, s[2 * j + 1]);
+    }
+  };
+  if (with_routed) {
+    for (int k = 0; k < K; ++k) {
+      const int e = topk_idx[size_t(t) * K + k];
+      if (e >= lo && e < hi) add(size_t(t) * K + k, topk_w[size_t(t) * K + k]);
+    }
+  }
+  if (with_shared && t >= sh_lo && t < sh_hi) add(size_t(T) * K + t, shared_gate[t]);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
+    op[j] = *reinterpret_cast<uint32_t*>(&b2);
+  }
+  reinterpret_cast<uint4*>(y + size_t(t) * H)[c8] = o;
 }
 
 namespace {
-int g_tc_sms = 148;
+int g_pairs = 74;  // co-resident CTA pairs of the GEMM kernels
+
+template <int MODE, typename... Args>
+cudaError_t launch_pairs(cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * g_pairs);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tc_pair_kernel<MODE>, args...);
 }
+}  // namespace
 
 cudaError_t tc_init(int num_sms) {
-  g_tc_sms = num_sms;
-  cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<kGateUp>,
+  cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel<kGateUp>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(tc_grouped_kernel<kDown>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+  e = cudaFuncSetAttribute(tc_pair_kernel<kDown>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kTcSmem);
+  if (e != cudaSuccess) return e;
+  // Persistent grid: as many pairs as can be co-resident (at most one CTA per SM).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (num_sms / 2));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, tc_pair_kernel<kGateUp>, &cfg);
+  if (e != cudaSuccess) return e;
+  g_pairs = n > 0 ? n : 1;
+  return cudaSuccess;
 }
 
 bool tc_supported(const Dims& d) {
-  return d.H % kBN == 0 && d.I % (kBN / 2) == 0 && d.Is % (kBN / 2) == 0 && d.E <= 511;
+  return d.H % 256 == 0 && d.H <= 256 * kGatherMaxH8 && d.I % 128 == 0 && d.Is % 128 == 0 &&
+         d.E <= 511;
 }
 
 cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, bool zero_acc, cudaStream_t st,
-                              void* mid_event) {
+                              __nv_bfloat16* y, int lo, int hi, int with_shared,
+                              int with_routed, cudaStream_t st, void* mid_event) {
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t P = T * d.K, R = P + T, ldh = d.ldh;
-  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h, tm_xp;
-  if (!make_tmap_bf16_2d(&tm_gu, w_gate_up, H, E * 2 * I, H * 2, kBK, kBN / 2) ||
-      !make_tmap_bf16_2d(&tm_sg, w_sh_gate, H, Is, H * 2, kBK, kBN / 2) ||
-      !make_tmap_bf16_2d(&tm_su, w_sh_up, H, Is, H * 2, kBK, kBN / 2) ||
-      !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kBK, kBN) ||
-      !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kBK, kBN) ||
-      !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kBK, kBM) ||
-      !make_tmap_bf16_2d(&tm_xp, ws.x_perm, H, R, H * 2, kBK, kBM))
+  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h, tm_h32, tm_xp, tm_xp32;
+  // gate_up weights [E][2I][H] seen as (k, row in group, gate|up, group, expert):
+  // one box = 4 groups of 16 gate rows, each followed by its 16 up rows.
+  const uint64_t gu_dims[5] = {H, 16, 2, I / 16, E};
+  const uint64_t gu_strides[4] = {H * 2, I * H * 2, 16 * H * 2, 2 * I * H * 2};
+  const uint32_t gu_box[5] = {kBK, 16, 2, 4, 1};
+  if (!make_tmap_bf16_nd(&tm_gu, w_gate_up, 5, gu_dims, gu_strides, gu_box) ||
+      !make_tmap_bf16_2d(&tm_sg, w_sh_gate, H, Is, H * 2, kBK, 16) ||
+      !make_tmap_bf16_2d(&tm_su, w_sh_up, H, Is, H * 2, kBK, 16) ||
+      !make_tmap_bf16_2d(&tm_dn, w_down, I, E * H, I * 2, kBK, kBM) ||
+      !make_tmap_bf16_2d(&tm_sd, w_sh_down, Is, H, Is * 2, kBK, kBM) ||
+      !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kBK, kHalfTok) ||
+      !make_tmap_bf16_2d(&tm_h32, ws.h, ldh, R, ldh * 2, kBK, kRowChunk) ||
+      !make_tmap_bf16_2d(&tm_xp, ws.x_perm, H, R, H * 2, kBK, kHalfTok) ||
+      !make_tmap_bf16_2d(&tm_xp32, ws.x_perm, H, R, H * 2, kBK, kRowChunk))
     return cudaErrorInvalidValue;
   plan_tiles_kernel<<<1, kPlanThreads, 0, st>>>(ws.offsets, ws.active, ws.n_active, d.E, d.H,
                                                 d.I, d.Is, ws.gu_tiles, ws.dn_tiles,
                                                 ws.m_tiles, ws.tile_counts);
-  gather_rows_kernel<<<g_tc_sms * 4, kGatherThreads, 0, st>>>(x, ws.m_tiles, ws.tile_counts + 2,
-                                                                ws.sorted_tok, d.H, ws.x_perm);
+  gather_rows_kernel<<<2 * g_pairs * 16, kGatherThreads, 0, st>>>(
+      x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, ws.x_perm);
   cudaError_t err = cudaSuccess;
-  if (zero_acc) {
-    err = cudaMemsetAsync(ws.y_acc, 0, sizeof(float) * size_t(T) * H, st);
-    if (err != cudaSuccess) return err;
-  }
   int* status = ws.status + 1;
-  TileTables gu{ws.gu_tiles, ws.tile_counts, ws.sorted_tok, ws.pair_w};
-  TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.sorted_tok, ws.pair_w};
-  tc_grouped_kernel<kGateUp><<<g_tc_sms, kTcThreads, kTcSmem, st>>>(
-      tm_gu, tm_sg, tm_su, tm_xp, gu, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.y_acc, status);
+  TileTables gu{ws.gu_tiles, ws.tile_counts, ws.pair_dst, ws.pair_w};
+  TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w};
+  err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, gu, d.H, d.E, d.I, d.Is,
+                              d.ldh, ws.h, ws.rows_bf16, status);
+  if (err != cudaSuccess) return err;
   if (mid_event) {
     err = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (err != cudaSuccess) return err;
   }
-  tc_grouped_kernel<kDown><<<g_tc_sms, kTcThreads, kTcSmem, st>>>(
-      tm_dn, tm_sd, tm_sd, tm_h, dn, d.H, d.E, d.I, d.Is, d.ldh, ws.h, ws.y_acc, status);
-  const long n4 = long(T) * d.H / 4;
-  finalize_kernel<<<unsigned((n4 + 255) / 256), 256, 0, st>>>(ws.y_acc, n4, y);
+  err = launch_pairs<kDown>(st, tm_dn, tm_sd, tm_sd, tm_h, tm_h32, dn, d.H, d.E, d.I, d.Is,
+                            d.ldh, ws.h, ws.rows_bf16, status);
+  if (err != cudaSuccess) return err;
+  const long n8 = long(T) * d.H / 8;
+  combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
+      ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
+      with_routed, d.sh_lo, d.sh_hi, y);
   return cudaGetLastError();
 }
 
