@@ -428,18 +428,18 @@ def main():
               "ms_per_step": pms, "algorithmic_flops": flops,
               "layer_tflops": flops / (pms * 1e-3) / 1e12,
               "layer_frac": flops / (pms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-              # router_tc, scan, scatter, plan, gate_up, down, finalize per step
-              "gpu_launches": 7 * psteps, "clocks": pclk,
+              # router_tc, scan, scatter, plan, row copy, gate_up, down, combine per step
+              "gpu_launches": 8 * psteps, "clocks": pclk,
               "e2e": pre.e2e(max(5, min(a.steps, 50)))}
         if pphase is not None:
-            pl["phase_ms"] = dict(zip(("route", "gate_up", "down_finalize", "tail"), pphase))
+            pl["phase_ms"] = dict(zip(("route_plan_copy", "gate_up", "down", "combine"), pphase))
             P = a.prefill_T * S.K
             gu_flops = 2 * (P + a.prefill_T) * S.H * 2 * S.I
             ach = gu_flops / (pphase[1] * 1e-3) / 1e12
-            pl["roofline"] = {"kernel": "tc_grouped_kernel<gate_up>", "bound": "tensor",
+            pl["roofline"] = {"kernel": "tc_pair_kernel<gate_up>", "bound": "tensor",
                               "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                               "frac": ach / peaks["bf16_tflops"], "traffic": profiled_traffic(
-                                  "tc_gate_up_prefill_T8192"),
+                                  "tc_pair_gate_up_prefill_T8192"),
                               "algorithmic_flops": gu_flops, "avg_launch_ms": pphase[1],
                               "peak_source": f"{peak_kind} (bf16_tflops, burst)"}
         line["prefill"] = pl

@@ -95,10 +95,11 @@ int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int
 
 /* pmoe_block_forward that also records CUDA events on `stream` between its
  * phases, for per-kernel timing by a benchmark: events[0] before routing,
- * [1] after routing (router, top-k, dispatch), [2] after gate_up+SiLU*mul,
- * [3] after down+weighting, [4] after the combine.  NULL entries and
- * n_events < 5 skip the corresponding records.  No reference counterpart
- * (instrumentation of pmoe_block_forward). */
+ * [1] after routing (router, top-k, dispatch; on the tensor-core path also
+ * the tile plan and the row copy, i.e. right before the gate_up GEMM), [2]
+ * after gate_up+SiLU*mul, [3] after down, [4] after the combine.  NULL
+ * entries and n_events < 5 skip the corresponding records.  No reference
+ * counterpart (instrumentation of pmoe_block_forward). */
 int pmoe_block_forward_profiled(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
                                 const uint16_t* w_router, const uint16_t* w_gate_up,
                                 const uint16_t* w_down, const uint16_t* w_sh_gate,

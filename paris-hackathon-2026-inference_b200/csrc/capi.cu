@@ -168,16 +168,18 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                : launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
                               with_shared, with_routed, ws, st);
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
-  if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
+    void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
+    for (int i = 0; i < 3; ++i)
+      if (events && i + 1 < n_events) ev[i] = events[i + 1];
     if (launch_tc_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                           bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), expert_lo,
-                          expert_hi, with_shared, with_routed, st,
-                          events && n_events > 2 ? events[2] : nullptr) != cudaSuccess)
+                          expert_hi, with_shared, with_routed, st, ev) != cudaSuccess)
       return PMOE_ERR_CUDA;
-    if (mark(3) != cudaSuccess || mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
+    if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
     return PMOE_OK;
   }
+  if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
   if (launch_stream_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                             bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr,
                             ep) != cudaSuccess)

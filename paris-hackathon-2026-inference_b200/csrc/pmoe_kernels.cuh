@@ -24,7 +24,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               __nv_bfloat16* y, int lo, int hi, int with_shared,
-                              int with_routed, cudaStream_t st, void* mid_event);
+                              int with_routed, cudaStream_t st, void* const events[3]);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch); also zeroes the fp32 output accumulator.

@@ -575,7 +575,11 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               __nv_bfloat16* y, int lo, int hi, int with_shared,
-                              int with_routed, cudaStream_t st, void* mid_event) {
+                              int with_routed, cudaStream_t st, void* const events[3]) {
+  // events (each may be null): before gate_up, after gate_up, after down
+  auto mark = [&](int i) {
+    return events[i] ? cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st) : cudaSuccess;
+  };
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t P = T * d.K, R = P + T, ldh = d.ldh;
   CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h, tm_h32, tm_xp, tm_xp32;
@@ -599,19 +603,20 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                                                 ws.m_tiles, ws.tile_counts);
   gather_rows_kernel<<<2 * g_pairs * 16, kGatherThreads, 0, st>>>(
       x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, ws.x_perm);
-  cudaError_t err = cudaSuccess;
+  cudaError_t err = mark(0);
+  if (err != cudaSuccess) return err;
   int* status = ws.status + 1;
   TileTables gu{ws.gu_tiles, ws.tile_counts, ws.pair_dst, ws.pair_w};
   TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w};
   err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, gu, d.H, d.E, d.I, d.Is,
                               d.ldh, ws.h, ws.rows_bf16, status);
   if (err != cudaSuccess) return err;
-  if (mid_event) {
-    err = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
-    if (err != cudaSuccess) return err;
-  }
+  err = mark(1);
+  if (err != cudaSuccess) return err;
   err = launch_pairs<kDown>(st, tm_dn, tm_sd, tm_sd, tm_h, tm_h32, dn, d.H, d.E, d.I, d.Is,
                             d.ldh, ws.h, ws.rows_bf16, status);
+  if (err != cudaSuccess) return err;
+  err = mark(2);
   if (err != cudaSuccess) return err;
   const long n8 = long(T) * d.H / 8;
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
