@@ -131,7 +131,10 @@ int pmoe_ep_buffer_bytes(int T_max, int H, int K, size_t* bytes);
  *                     pmoe_read_status) and sums -- y is the full block output on
  *                     every rank, no separate collective.  Streaming path only
  *                     (T <= 64 unless PMOE_F_FORCE_STREAM).
- *   epoch             > 0, increasing by one per call on every rank. */
+ *   epoch             > 0: increasing by one per call on every rank (host
+ *                     counter); 0: a counter in this rank's exchange buffer that
+ *                     every call bumps on the device, so a captured CUDA graph
+ *                     replays correctly.  One group uses one of the two modes. */
 int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
                           const uint16_t* w_router, const uint16_t* w_gate_up,
                           const uint16_t* w_down, const uint16_t* w_sh_gate,
@@ -140,6 +143,32 @@ int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, 
                           int shared_lo, int shared_hi, int flags, void* const* peer_bufs,
                           size_t peer_buf_bytes, int rank, int world, int epoch, uint16_t* y,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* One decoder layer of the MoE-only stack: y = x + block(RMSNorm(x)), with
+ * RMSNorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w_norm)) in fp32 and the
+ * residual added as bf16(x + bf16(block)) -- Qwen3_5MoeDecoderLayer's
+ * post_attention_layernorm, mlp and residual add
+ * (modeling_qwen3_5_moe.py:795-812, 862-868), attention omitted.  The norm is
+ * one kernel ahead of the router; the residual is folded into the combine.
+ * y may alias x (in-place update of the residual stream).  Other arguments as
+ * pmoe_block_forward_ep (peer_bufs NULL: one GPU, or a partial for the caller
+ * to sum -- then the residual is added on every rank, so only one rank should
+ * pass x as residual: use pmoe_block_forward for the other partials). */
+int pmoe_layer_forward(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                       const uint16_t* w_norm, float eps, const uint16_t* w_router,
+                       const uint16_t* w_gate_up, const uint16_t* w_down,
+                       const uint16_t* w_sh_gate, const uint16_t* w_sh_up,
+                       const uint16_t* w_sh_down, const uint16_t* w_sh_gvec, int expert_lo,
+                       int expert_hi, int shared_lo, int shared_hi, int flags,
+                       void* const* peer_bufs, size_t peer_buf_bytes, int rank, int world,
+                       int epoch, uint16_t* y, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* out[T][H] = Qwen3_5MoeRMSNorm(x; w_norm, eps) in fp32, cast to bf16
+ * (modeling_qwen3_5_moe.py:795-812): the first step of pmoe_layer_forward,
+ * exported for tests and for callers that normalise separately. */
+int pmoe_rmsnorm(const uint16_t* x, int T, int H, const uint16_t* w_norm, float eps,
+                 uint16_t* out, void* stream);
 
 /* Synchronously read the kernel status word of the last call that used this
  * workspace (0 ok, 1/2/3 a bounded pipeline wait ran out, 4 a peer's flag never

@@ -178,6 +178,18 @@ def rmsnorm(x_bits: np.ndarray, w_bits: np.ndarray, eps: float = 1e-6) -> np.nda
     return f32_to_bf16((x * r * (1.0 + w)).astype(np.float32))
 
 
+def decoder_layer(x_bits: np.ndarray, w_norm_bits: np.ndarray, block_weights, k: int,
+                  eps: float = 1e-6, route=None):
+    """MoE-only ``Qwen3_5MoeDecoderLayer`` half (modeling_qwen3_5_moe.py:862-868):
+    ``residual + mlp(post_attention_layernorm(x))`` in bf16, i.e.
+    bf16(x + bf16(moe_block(rmsnorm(x)))).  ``route`` (optional) is the routing
+    of the normalised input.  Returns (y fp32 values of the bf16 result, xn bits)."""
+    xn = rmsnorm(x_bits, w_norm_bits, eps)
+    y, _, _ = moe_block(xn, *block_weights, k=k, route=route)
+    out = round_bf16(bf16_to_f32(x_bits) + round_bf16(y.astype(np.float32)))
+    return out, xn
+
+
 # ------------------------------------------------------------- comparisons --
 
 def rel_l2(a, b) -> float:

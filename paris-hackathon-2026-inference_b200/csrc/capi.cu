@@ -112,9 +112,16 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
   return PMOE_OK;
 }
 
+// Decoder-layer extras: y = x + block(RMSNorm(x; w_norm, eps)).
+struct LayerArgs {
+  const uint16_t* w_norm;
+  float eps;
+};
+
 // Shared implementation of the forward entry points.  `ep` (world > 0)
 // selects the expert-parallel NVLink exchange; sh_lo/sh_hi is the token range
-// whose shared-expert rows this call computes.
+// whose shared-expert rows this call computes; `layer` (may be null) adds the
+// RMSNorm before and the residual after the block.
 static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
                         const uint16_t* w_router, const uint16_t* w_gate_up,
                         const uint16_t* w_down, const uint16_t* w_sh_gate,
@@ -122,7 +129,7 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                         const uint16_t* w_sh_gvec, int expert_lo, int expert_hi, int sh_lo,
                         int sh_hi, int flags, uint16_t* y, void* workspace,
                         size_t workspace_bytes, void* stream, void* const* events, int n_events,
-                        const EpPeers& ep) {
+                        const EpPeers& ep, const LayerArgs* layer = nullptr) {
   int s = check_shape(T, H, E, K, I, Is);
   if (s != PMOE_OK) return s;
   if (expert_lo < 0 || expert_hi > E || expert_lo > expert_hi) return PMOE_ERR_ARG;
@@ -135,6 +142,10 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   for (const void* p : ptrs) {
     if (!p) return PMOE_ERR_ARG;
     if (!aligned16(p)) return PMOE_ERR_ALIGN;
+  }
+  if (layer) {
+    if (!layer->w_norm || !(layer->eps >= 0.f)) return PMOE_ERR_ARG;
+    if (!aligned16(layer->w_norm)) return PMOE_ERR_ALIGN;
   }
   if ((s = ensure_device()) != PMOE_OK) return s;
   Dims d = make_dims(T, H, E, K, I, Is);
@@ -159,28 +170,41 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
     return cudaSuccess;
   };
   if (mark(0) != cudaSuccess) return PMOE_ERR_CUDA;
-  // Prefill-sized batches route on the tensor cores (that path also zeroes
-  // the fp32 accumulator of the expert GEMMs).
+  if (ep.world > 0 && ep.epoch_dev &&
+      launch_epoch_bump(const_cast<int*>(ep.epoch_dev), st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  // The block reads xin; a decoder layer normalises x first and adds it back
+  // in the combine (in place, y == x, is allowed: each combine thread reads
+  // its residual chunk before writing the same chunk).
+  const __nv_bfloat16* xin = bf(x);
+  const __nv_bfloat16* resid = nullptr;
+  if (layer) {
+    if (launch_rmsnorm(bf(x), bf(layer->w_norm), layer->eps, T, H, ws.xn, st) != cudaSuccess)
+      return PMOE_ERR_CUDA;
+    xin = ws.xn;
+    resid = bf(x);
+  }
+  // Prefill-sized batches route on the tensor cores.
   const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
   const cudaError_t rerr =
-      route_tc ? launch_route_tc(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+      route_tc ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
                                  with_shared, with_routed, ws, st)
-               : launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+               : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
                               with_shared, with_routed, ws, st);
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
     for (int i = 0; i < 3; ++i)
       if (events && i + 1 < n_events) ev[i] = events[i + 1];
-    if (launch_tc_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
-                          bf(w_sh_down), ws, reinterpret_cast<__nv_bfloat16*>(y), expert_lo,
-                          expert_hi, with_shared, with_routed, st, ev) != cudaSuccess)
+    if (launch_tc_experts(d, xin, bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
+                          bf(w_sh_down), ws, resid, reinterpret_cast<__nv_bfloat16*>(y),
+                          expert_lo, expert_hi, with_shared, with_routed, st, ev) != cudaSuccess)
       return PMOE_ERR_CUDA;
     if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
     return PMOE_OK;
   }
   if (mark(1) != cudaSuccess) return PMOE_ERR_CUDA;
-  if (launch_stream_experts(d, bf(x), bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
+  if (launch_stream_experts(d, xin, bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                             bf(w_sh_down), ws, st, events && n_events > 2 ? events[2] : nullptr,
                             ep) != cudaSuccess)
     return PMOE_ERR_CUDA;
@@ -192,7 +216,7 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
     dc.sh_hi = T;
   }
   if (launch_combine(dc, ws, ep.world > 0 ? 0 : expert_lo, ep.world > 0 ? E : expert_hi,
-                     ep.world > 0 ? 1 : with_shared, ep.world > 0 ? 1 : with_routed,
+                     ep.world > 0 ? 1 : with_shared, ep.world > 0 ? 1 : with_routed, resid,
                      reinterpret_cast<__nv_bfloat16*>(y), st, ep) != cudaSuccess)
     return PMOE_ERR_CUDA;
   if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
@@ -226,12 +250,44 @@ int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int
 
 // ---- expert parallelism ------------------------------------------------------
 
-static const size_t kEpHeader = 512;  // flags [0,256), ticket at 256
+// Exchange buffer header: flags [0,256), CTA ticket at 256, device epoch at 384.
+static const size_t kEpHeader = 512;
+static const size_t kEpTicket = 256;
+static const size_t kEpEpoch = 384;
 
 int pmoe_ep_buffer_bytes(int T_max, int H, int K, size_t* bytes) {
   if (!bytes || T_max <= 0 || H <= 0 || K <= 0) return PMOE_ERR_ARG;
   const size_t rows = (size_t(T_max) * K + T_max) * H * sizeof(float);
   *bytes = kEpHeader + 2 * ((rows + 255) / 256 * 256);
+  return PMOE_OK;
+}
+
+// Fills `ep` for an exchange over peer_bufs (null peer_bufs: no exchange).
+// epoch > 0: host epoch; epoch == 0: the device counter in this rank's buffer
+// header (bumped by every call; CUDA-graph capturable).
+static int setup_ep(int T, int H, int K, int flags, void* const* peer_bufs,
+                    size_t peer_buf_bytes, int rank, int world, int epoch, EpPeers& ep) {
+  ep = EpPeers{};
+  if (!peer_bufs) return PMOE_OK;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch < 0)
+    return PMOE_ERR_ARG;
+  if (T > kFusedRouteMaxT && !(flags & PMOE_F_FORCE_STREAM)) return PMOE_ERR_UNSUPPORTED;
+  const size_t half = (peer_buf_bytes - kEpHeader) / 2;
+  const size_t need = (size_t(T) * K + T) * H * sizeof(float);
+  if (peer_buf_bytes < kEpHeader || need > half) return PMOE_ERR_WORKSPACE;
+  for (int r = 0; r < world; ++r) {
+    if (!peer_bufs[r] || !aligned16(peer_bufs[r])) return PMOE_ERR_ARG;
+    char* b = static_cast<char*>(peer_bufs[r]);
+    ep.rows[r] = reinterpret_cast<float*>(b + kEpHeader);
+    ep.flags[r] = reinterpret_cast<int*>(b);
+  }
+  ep.par_stride = (half / 256 * 256) / sizeof(float);
+  char* own = static_cast<char*>(peer_bufs[rank]);
+  ep.ticket = reinterpret_cast<int*>(own + kEpTicket);
+  ep.epoch_dev = epoch == 0 ? reinterpret_cast<const int*>(own + kEpEpoch) : nullptr;
+  ep.world = world;
+  ep.rank = rank;
+  ep.epoch = epoch;
   return PMOE_OK;
 }
 
@@ -243,28 +299,44 @@ int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, 
                           int shared_lo, int shared_hi, int flags, void* const* peer_bufs,
                           size_t peer_buf_bytes, int rank, int world, int epoch, uint16_t* y,
                           void* workspace, size_t workspace_bytes, void* stream) {
-  EpPeers ep{};
-  if (peer_bufs) {
-    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch <= 0)
-      return PMOE_ERR_ARG;
-    if (T > kFusedRouteMaxT && !(flags & PMOE_F_FORCE_STREAM)) return PMOE_ERR_UNSUPPORTED;
-    const size_t half = (peer_buf_bytes - kEpHeader) / 2;
-    const size_t need = (size_t(T) * K + T) * H * sizeof(float);
-    if (peer_buf_bytes < kEpHeader || need > half) return PMOE_ERR_WORKSPACE;
-    for (int r = 0; r < world; ++r) {
-      if (!peer_bufs[r] || !aligned16(peer_bufs[r])) return PMOE_ERR_ARG;
-      char* b = static_cast<char*>(peer_bufs[r]);
-      ep.rows[r] = reinterpret_cast<float*>(b + kEpHeader + size_t(epoch & 1) * (half / 256 * 256));
-      ep.flags[r] = reinterpret_cast<int*>(b);
-    }
-    ep.ticket = reinterpret_cast<int*>(static_cast<char*>(peer_bufs[rank]) + 256);
-    ep.world = world;
-    ep.rank = rank;
-    ep.epoch = epoch;
-  }
+  EpPeers ep;
+  const int s = setup_ep(T, H, K, flags, peer_bufs, peer_buf_bytes, rank, world, epoch, ep);
+  if (s != PMOE_OK) return s;
   return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
                       w_sh_down, w_sh_gvec, expert_lo, expert_hi, shared_lo, shared_hi, flags, y,
                       workspace, workspace_bytes, stream, nullptr, 0, ep);
+}
+
+int pmoe_layer_forward(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                       const uint16_t* w_norm, float eps, const uint16_t* w_router,
+                       const uint16_t* w_gate_up, const uint16_t* w_down,
+                       const uint16_t* w_sh_gate, const uint16_t* w_sh_up,
+                       const uint16_t* w_sh_down, const uint16_t* w_sh_gvec, int expert_lo,
+                       int expert_hi, int shared_lo, int shared_hi, int flags,
+                       void* const* peer_bufs, size_t peer_buf_bytes, int rank, int world,
+                       int epoch, uint16_t* y, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  EpPeers ep;
+  const int s = setup_ep(T, H, K, flags, peer_bufs, peer_buf_bytes, rank, world, epoch, ep);
+  if (s != PMOE_OK) return s;
+  const LayerArgs layer{w_norm, eps};
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, expert_lo, expert_hi, shared_lo, shared_hi, flags, y,
+                      workspace, workspace_bytes, stream, nullptr, 0, ep, &layer);
+}
+
+int pmoe_rmsnorm(const uint16_t* x, int T, int H, const uint16_t* w_norm, float eps,
+                 uint16_t* out, void* stream) {
+  if (T < 0 || H <= 0 || H % 8 != 0 || !(eps >= 0.f)) return PMOE_ERR_ARG;
+  if (T == 0) return PMOE_OK;
+  if (!x || !w_norm || !out) return PMOE_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_norm) || !aligned16(out)) return PMOE_ERR_ALIGN;
+  int s = ensure_device();
+  if (s != PMOE_OK) return s;
+  return launch_rmsnorm(bf(x), bf(w_norm), eps, T, H, reinterpret_cast<__nv_bfloat16*>(out),
+                        static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
 }
 
 int pmoe_read_status(const void* workspace, int T, int H, int E, int K, int I, int Is,

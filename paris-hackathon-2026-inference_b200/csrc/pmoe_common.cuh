@@ -27,6 +27,7 @@ struct Workspace {
   float* logit_part;    // [T][Rpad]   router logits (bf16-rounded) + raw shared-gate sum
   int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
+  __nv_bfloat16* xn;    // [T][H]     RMSNorm(x) (decoder-layer entry points)
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
   __nv_bfloat16* x_perm; // [T*K+T][H] x rows in dispatch order (tensor-core path; aliases
                          //            `rows`, which only the streaming path uses)
@@ -57,15 +58,29 @@ struct Dims {
 // (peer stores), then the last of its CTAs to finish raises flags[q][r] =
 // epoch on every rank q.  The combine on rank q waits (bounded) for
 // flags[q][0..world) >= epoch and sums locally: no separate collective.
+// The epoch is either passed per call (host counter) or read from a counter
+// in this rank's exchange buffer that a one-thread kernel bumps at the start
+// of every call, so that a captured CUDA graph replays correctly.  Rows go to
+// one of two copies by epoch parity (a rank one call ahead never overwrites
+// rows still being combined).
 constexpr int kMaxRanks = 8;
 struct EpPeers {
-  float* rows[kMaxRanks];  // each rank's rows buffer for this call (peer-mapped)
+  float* rows[kMaxRanks];  // each rank's rows buffer, parity-0 copy (peer-mapped)
+  size_t par_stride;       // floats from the parity-0 to the parity-1 copy
   int* flags[kMaxRanks];   // each rank's flag array, indexed by the writing rank
   int* ticket;             // this rank's CTA-completion counter (starts and ends at 0)
+  const int* epoch_dev;    // device epoch counter, or null: use `epoch`
   int world;               // 0: no exchange
   int rank;
-  int epoch;               // strictly increasing per call, > 0
+  int epoch;               // host epoch (> 0) when epoch_dev is null
 };
+
+__device__ __forceinline__ int ep_epoch(const EpPeers& ep) {
+  return ep.epoch_dev ? *ep.epoch_dev : ep.epoch;
+}
+__device__ __forceinline__ float* ep_rows(const EpPeers& ep, int r, int epoch) {
+  return ep.rows[r] + size_t(epoch & 1) * ep.par_stride;
+}
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   int v;
@@ -107,6 +122,7 @@ inline Workspace carve(void* base, const Dims& d) {
   w.logit_part = (float*)take(sizeof(float) * size_t(d.KS) * d.T * d.Rpad);
   w.status = (int32_t*)take(sizeof(int32_t) * 8);
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
+  w.xn = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * size_t(d.T) * d.H);
   w.rows = (float*)take(sizeof(float) * R * d.H);
   w.x_perm = reinterpret_cast<__nv_bfloat16*>(w.rows);
   w.rows_bf16 = reinterpret_cast<__nv_bfloat16*>(w.rows);

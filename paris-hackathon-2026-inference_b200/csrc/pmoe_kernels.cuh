@@ -23,19 +23,26 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, int lo, int hi, int with_shared,
-                              int with_routed, cudaStream_t st, void* const events[3]);
+                              const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
+                              int with_shared, int with_routed, cudaStream_t st,
+                              void* const events[3]);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
-// stable dispatch); also zeroes the fp32 output accumulator.
+// stable dispatch).
 cudaError_t route_tc_init();
 bool route_tc_supported(const Dims& d);
 cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                             const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                             int with_routed, const Workspace& ws, cudaStream_t st);
 
+// resid (may be null): y = bf16(resid + bf16(sum)), the decoder layer's residual.
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
-                           int with_routed, __nv_bfloat16* y, cudaStream_t st,
-                           const EpPeers& ep);
+                           int with_routed, const __nv_bfloat16* resid, __nv_bfloat16* y,
+                           cudaStream_t st, const EpPeers& ep);
+cudaError_t launch_epoch_bump(int* epoch, cudaStream_t st);
+
+// out = Qwen3_5MoeRMSNorm(x; w, eps), bf16 [T][H].
+cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int T,
+                           int H, __nv_bfloat16* out, cudaStream_t st);
 
 }  // namespace pmoe

@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     ExpertTables tb, int H, int E, int I, int Is,
     float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep) {
   using C = DnCfg<KCH>;
+  const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
               if (ep.world > 0) {
                 // every computed row goes to every rank (peer stores over NVLink)
                 for (int rr = 0; rr < ep.world; ++rr) {
-                  float* out = ep.rows[rr] + off;
+                  float* out = ep_rows(ep, rr, epoch) + off;
                   out[orow] = v0;
                   out[orow + 8] = v1;
                 }
@@ -452,7 +453,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
       if (prev == int(gridDim.x) * kConsumers - 1) {
         __threadfence_system();
         *ep.ticket = 0;
-        for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, ep.epoch);
+        for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, epoch);
       }
     }
   }
@@ -460,14 +461,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
 
 // y[t, :] = bf16( sum_{s<K, expert in [lo,hi)} rows[t*K+s, :] + rows[T*K+t, :] )
 // fp32, fixed summation order.  One thread per 4 columns.  The shared row is
-// added for tokens in [sh_lo, sh_hi).  With an expert-parallel exchange
-// (world > 0) every block first waits, bounded, until all ranks' completion
-// flags for this epoch are up.
+// added for tokens in [sh_lo, sh_hi).  With a residual (decoder layer),
+// y = bf16(resid + bf16(sum)), the two roundings of `residual + mlp(x)` in
+// bf16 (modeling_qwen3_5_moe.py:867-868).  With an expert-parallel exchange
+// (world > 0) the rows are this call's parity copy of the exchange buffer and
+// every block first waits, bounded, until all ranks' completion flags for
+// this epoch are up.
 __global__ void __launch_bounds__(256) combine_kernel(
-    const float* __restrict__ rows, const int32_t* __restrict__ topk_idx, int T, int H, int K,
-    int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
-    const int* __restrict__ wait_flags, int world, int epoch, int* __restrict__ status,
+    const float* __restrict__ rows, size_t par_stride, const int32_t* __restrict__ topk_idx,
+    int T, int H, int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    const int* __restrict__ wait_flags, int world, const int* __restrict__ epoch_dev,
+    int epoch_host, int* __restrict__ status, const __nv_bfloat16* __restrict__ resid,
     __nv_bfloat16* __restrict__ y) {
+  const int epoch = epoch_dev ? *epoch_dev : epoch_host;
+  if (world > 0) rows += size_t(epoch & 1) * par_stride;
   if (world > 0) {
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
@@ -503,6 +510,15 @@ __global__ void __launch_bounds__(256) combine_kernel(
   if (with_shared && t >= sh_lo && t < sh_hi) {
     const float4 v = reinterpret_cast<const float4*>(rows + (size_t(T) * K + t) * H)[c4];
     s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  }
+  if (resid) {
+    const uint2 rb = reinterpret_cast<const uint2*>(resid + size_t(t) * H)[c4];
+    const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rb.x));
+    const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rb.y));
+    s.x = r0.x + bf16_round(s.x);
+    s.y = r0.y + bf16_round(s.y);
+    s.z = r1.x + bf16_round(s.z);
+    s.w = r1.y + bf16_round(s.w);
   }
   __nv_bfloat162 lo2 = __floats2bfloat162_rn(s.x, s.y);
   __nv_bfloat162 hi2 = __floats2bfloat162_rn(s.z, s.w);
@@ -592,15 +608,24 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
 }
 
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,
-                           int with_routed, __nv_bfloat16* y, cudaStream_t st,
-                           const EpPeers& ep) {
+                           int with_routed, const __nv_bfloat16* resid, __nv_bfloat16* y,
+                           cudaStream_t st, const EpPeers& ep) {
   const long n = long(d.T) * (d.H / 4);
   if (n == 0) return cudaSuccess;
   const float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
   const int* flags = ep.world > 0 ? ep.flags[ep.rank] : nullptr;
   combine_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(
-      rows, ws.topk_idx, d.T, d.H, d.K, lo, hi, with_shared, with_routed, d.sh_lo, d.sh_hi, flags,
-      ep.world, ep.epoch, ws.status + 1, y);
+      rows, ep.par_stride, ws.topk_idx, d.T, d.H, d.K, lo, hi, with_shared, with_routed, d.sh_lo,
+      d.sh_hi, flags, ep.world, ep.epoch_dev, ep.epoch, ws.status + 1, resid, y);
+  return cudaGetLastError();
+}
+
+// One thread: the device epoch counter of an exchange buffer, bumped at the
+// start of every call that uses it.
+__global__ void ep_epoch_bump_kernel(int* epoch) { *epoch += 1; }
+
+cudaError_t launch_epoch_bump(int* epoch, cudaStream_t st) {
+  ep_epoch_bump_kernel<<<1, 1, 0, st>>>(epoch);
   return cudaGetLastError();
 }
 

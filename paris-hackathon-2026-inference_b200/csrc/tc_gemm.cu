@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
 }
 
 // y[t, :] = bf16( sum_{s<K, expert in [lo,hi)} w[t,s] * rows[t*K+s, :]
-//                  + g[t] * rows[T*K+t, :] )
+//                  + g[t] * rows[T*K+t, :] )      (+ resid: see below)
 // over the bf16 expert rows the down GEMM wrote (routing weights w, shared
 // gate g), in fp32 in a fixed order (the shared row for tokens in
 // [sh_lo, sh_hi)).  One thread per 8 columns.
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
     const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ topk_idx,
     const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
     int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
-    __nv_bfloat16* __restrict__ y) {
+    const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
   const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int cols8 = H / 8;
   if (i >= long(T) * cols8) return;
@@ -508,6 +508,16 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
     }
   }
   if (with_shared && t >= sh_lo && t < sh_hi) add(size_t(T) * K + t, shared_gate[t]);
+  if (resid) {  // decoder layer: y = bf16(resid + bf16(sum)), as residual + mlp(x) in bf16
+    const uint4 rv = reinterpret_cast<const uint4*>(resid + size_t(t) * H)[c8];
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(r2[j]);
+      s[2 * j] = f.x + bf16_round(s[2 * j]);
+      s[2 * j + 1] = f.y + bf16_round(s[2 * j + 1]);
+    }
+  }
   uint4 o;
   uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -574,8 +584,9 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
-                              __nv_bfloat16* y, int lo, int hi, int with_shared,
-                              int with_routed, cudaStream_t st, void* const events[3]) {
+                              const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
+                              int with_shared, int with_routed, cudaStream_t st,
+                              void* const events[3]) {
   // events (each may be null): before gate_up, after gate_up, after down
   auto mark = [&](int i) {
     return events[i] ? cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st) : cudaSuccess;
@@ -621,7 +632,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   const long n8 = long(T) * d.H / 8;
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
       ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
-      with_routed, d.sh_lo, d.sh_hi, y);
+      with_routed, d.sh_lo, d.sh_hi, resid, y);
   return cudaGetLastError();
 }
 

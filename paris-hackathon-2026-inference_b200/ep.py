@@ -133,11 +133,11 @@ class EPGroup:
         slo, shi = token_range(T, self.rank, self.world)
         if self.uses_exchange(T):
             # each rank computes its experts and its share of the shared
-            # expert's tokens; every computed row is exchanged
-            self.epoch += 1
+            # expert's tokens; every computed row is exchanged.  Epoch 0: the
+            # device-side counter, so the call can be captured in a CUDA graph.
             s = self.lib.pmoe_block_forward_ep(
                 x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
-                self.peer_arr, self.buf_bytes, self.rank, self.world, self.epoch, y.data_ptr(),
+                self.peer_arr, self.buf_bytes, self.rank, self.world, 0, y.data_ptr(),
                 ws.data_ptr(), nbytes, st)
             _lib.check("pmoe_block_forward_ep", s)
             return y
@@ -147,6 +147,34 @@ class EPGroup:
         _lib.check("pmoe_block_forward_ep", s)
         if self.world > 1:
             dist.all_reduce(y, group=self.group)
+        return y
+
+    def layer_forward(self, x: torch.Tensor, w_norm: torch.Tensor, eps: float, weights,
+                      flags: int = 3, out: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None):
+        """One MoE-only decoder layer, x + block(RMSNorm(x)), full output on every
+        rank (pmoe_layer_forward over the NVLink exchange; T <= t_max).  ``out``
+        may be ``x`` (in-place residual update)."""
+        T, H = x.shape
+        if not self.uses_exchange(T) and self.world > 1:
+            raise ValueError("layer_forward across ranks needs the fused exchange (T <= t_max)")
+        w = list(weights)
+        I, Is = w[1].shape[1] // 2, w[4].shape[0]
+        y = out if out is not None else torch.empty((T, H), dtype=_BF16, device=x.device)
+        if T == 0:
+            return y
+        nbytes = _lib.workspace_size(T, H, self.E, self.K, I, Is)
+        ws = workspace if workspace is not None else torch.empty(nbytes, dtype=torch.uint8,
+                                                                 device=x.device)
+        st = torch.cuda.current_stream(x.device).cuda_stream
+        wp = [t.data_ptr() for t in w]
+        slo, shi = token_range(T, self.rank, self.world)
+        peers = self.peer_arr if self.world > 1 else None
+        s = self.lib.pmoe_layer_forward(
+            x.data_ptr(), T, H, self.E, self.K, I, Is, w_norm.data_ptr(), float(eps), *wp,
+            self.lo, self.hi, slo, shi, flags, peers, self.buf_bytes if peers else 0, self.rank,
+            self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)
+        _lib.check("pmoe_layer_forward", s)
         return y
 
     def close(self):

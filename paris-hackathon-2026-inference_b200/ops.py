@@ -71,6 +71,57 @@ def _moe_block_fake(x, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up, w_sh_dow
     return x.new_empty(x.shape)
 
 
+@torch.library.custom_op("paris_moe::moe_layer", mutates_args=())
+def moe_layer(x: torch.Tensor, w_norm: torch.Tensor, eps: float, w_router: torch.Tensor,
+              w_gate_up: torch.Tensor, w_down: torch.Tensor, w_sh_gate: torch.Tensor,
+              w_sh_up: torch.Tensor, w_sh_down: torch.Tensor, w_sh_gvec: torch.Tensor,
+              top_k: int, flags: int) -> torch.Tensor:
+    """One MoE-only decoder layer: x + block(RMSNorm(x)) (see pmoe_layer_forward)."""
+    _check_cuda("moe_layer", x, w_norm, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                w_sh_down, w_sh_gvec)
+    T, H = x.shape
+    E = w_router.shape[0]
+    I = w_gate_up.shape[1] // 2
+    Is = w_sh_gate.shape[0]
+    with torch.cuda.device(x.device):
+        y = torch.empty((T, H), dtype=_BF16, device=x.device)
+        if T == 0:
+            return y
+        nbytes = _lib.workspace_size(T, H, E, top_k, I, Is)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        st = _lib.load().pmoe_layer_forward(
+            x.data_ptr(), T, H, E, top_k, I, Is, w_norm.data_ptr(), float(eps),
+            w_router.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), w_sh_gate.data_ptr(),
+            w_sh_up.data_ptr(), w_sh_down.data_ptr(), w_sh_gvec.data_ptr(), 0, E, 0, T, flags,
+            None, 0, 0, 1, 0, y.data_ptr(), ws.data_ptr(), nbytes, _stream_ptr(x.device))
+    _lib.check("pmoe_layer_forward", st)
+    return y
+
+
+@moe_layer.register_fake
+def _moe_layer_fake(x, w_norm, eps, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                    w_sh_down, w_sh_gvec, top_k, flags):
+    return x.new_empty(x.shape)
+
+
+@torch.library.custom_op("paris_moe::rmsnorm", mutates_args=())
+def rmsnorm(x: torch.Tensor, w_norm: torch.Tensor, eps: float) -> torch.Tensor:
+    """Qwen3_5MoeRMSNorm(x): bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)), fp32 inside."""
+    _check_cuda("rmsnorm", x, w_norm)
+    T, H = x.shape
+    with torch.cuda.device(x.device):
+        y = torch.empty((T, H), dtype=_BF16, device=x.device)
+        st = _lib.load().pmoe_rmsnorm(x.data_ptr(), T, H, w_norm.data_ptr(), float(eps),
+                                      y.data_ptr(), _stream_ptr(x.device))
+    _lib.check("pmoe_rmsnorm", st)
+    return y
+
+
+@rmsnorm.register_fake
+def _rmsnorm_fake(x, w_norm, eps):
+    return x.new_empty(x.shape)
+
+
 @torch.library.custom_op("paris_moe::moe_route", mutates_args=())
 def moe_route(x: torch.Tensor, w_router: torch.Tensor, w_sh_gvec: torch.Tensor,
               k: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,

@@ -39,6 +39,27 @@ def main():
             ok &= good
             print(f"rank{rank} {name} T={T} exchange={g.uses_exchange(T)} rel_l2={r:.2e} "
                   f"max_abs={m:.2e} {'ok' if good else 'FAIL'}", flush=True)
+    # MoE-only stack (3 layers, decode T=64): across ranks over the exchange
+    # equals the single-GPU layers bit for bit, eagerly and as a CUDA graph.
+    from paris_moe_b200 import stack
+    norms, blocks = stack.make_stack_weights(3, seed=11, device=dev)
+    h0 = W.make_hidden(64, S, seed=13, device=dev)
+    ref = h0.clone()
+    for l, b in enumerate(blocks):
+        ref = ops.moe_layer(ref, norms[l], 1e-6, *b.tensors(), S.K, 3)
+    st = stack.MoEStack(norms, blocks, group=fused)
+    got = st.forward(h0.clone())
+    good = torch.equal(got, ref)
+    hs = h0.clone()
+    graph = st.capture(hs)
+    for _ in range(2):
+        hs.copy_(h0)
+        graph.replay()
+        good &= torch.equal(hs, ref)
+    torch.cuda.synchronize()
+    ok &= good
+    print(f"rank{rank} stack 3 layers T=64 eager+graph bit-identical to 1 GPU "
+          f"{'ok' if good else 'FAIL'}", flush=True)
     fused.close()
     dist.barrier()
     print(f"rank{rank} EP_{'OK' if ok else 'FAIL'}", flush=True)

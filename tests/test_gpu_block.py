@@ -161,6 +161,17 @@ def test_block_tc_matches_stream(full):
     assert O.rel_l2(a, b) < 3e-3
 
 
+def test_block_prefill_tc_deterministic():
+    """The tensor-core path has no atomics: repeated calls are bit-identical."""
+    from paris_moe_b200 import workload as W
+    wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=1.1)
+    g = wts.to("cuda")
+    xg = W.make_hidden(2048, W.MoEShape(), seed=0, zipf=True).cuda()
+    a = block(xg, g)
+    b = block(xg, g)
+    assert torch.equal(a, b)
+
+
 def test_block_prefill_zipf_tc():
     """Default path at T=8192 (tensor cores), skewed routing; 256 sampled rows."""
     from paris_moe_b200 import workload as W
