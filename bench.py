@@ -2,12 +2,15 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--T 64] [--prefill-T 8192] [--zipf 1.1] [--no-prefill]
+                    [--stack-layers 40] [--stack-T 64] [--no-stack]
 
 A step is one call of the Qwen3.5-35B-A3B MoE layer.  The headline
 (``metric``/``value``) is the decode configuration of BASELINE.json
 configs[1] at its largest batch, T=64 tokens; the same run also measures the
 prefill configuration (configs[2]: T=8192, Zipf(s=1.1)-skewed routing) and
-reports it under ``"prefill"``.  Weights are random-init bf16 of the real
+reports it under ``"prefill"``, and the 40-layer MoE-only decoder stack at
+batch 64 (configs[4]: RMSNorm + block + residual per layer, attention omitted,
+one CUDA graph per step, EP over all ranks) under ``"stack"``.  Weights are random-init bf16 of the real
 shape (1.5 GB, larger than the 126 MB L2, so every decode step streams them
 from HBM; no L2 flush is needed) and hidden states are synthetic N(0,1).
 
@@ -312,6 +315,63 @@ class Ctx:
         return float(t.item())
 
 
+def stack_bench(c, a, peaks, peak_kind):
+    """Config 5: the MoE-only decoder stack (RMSNorm + MoE block + residual per
+    layer, attention omitted), one decode step of batch ``stack_T`` through all
+    layers, replayed as one CUDA graph; EP over all ranks of the job."""
+    import torch
+    from paris_moe_b200 import stack, workload as W
+    S, L, T = c.S, a.stack_layers, a.stack_T
+    norms, blocks = stack.make_stack_weights(L, seed=1000, device=c.dev)
+    st = stack.MoEStack(norms, blocks, group=c.group)
+    h0 = W.make_hidden(T, S, seed=3, device=c.dev)
+    hs = h0.clone()
+    graph = st.capture(hs)
+    steps = max(5, min(a.steps, 50))
+    for _ in range(a.warmup):
+        hs.copy_(h0)
+        graph.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(c.local) as clk:
+        t0.record(c.st)
+        for _ in range(steps):
+            hs.copy_(h0)          # the step's input (256 KiB device copy)
+            graph.replay()
+        t1.record(c.st)
+        torch.cuda.synchronize()
+    c.barrier()
+    ms = c.max_over_ranks(t0.elapsed_time(t1)) / steps
+    # HBM roofline per rank: every layer streams the routed experts it hits
+    # (in its expert range) plus router, shared expert and activations.
+    from paris_moe_b200 import ops
+    lo, hi = c.rank * S.E // c.world, (c.rank + 1) * S.E // c.world
+    byts = 0
+    h = h0.clone()
+    for l in range(L):
+        xn = ops.rmsnorm(h, norms[l], 1e-6)
+        idx = ops.moe_route(xn, blocks[l].w_router, blocks[l].w_sh_gvec, S.K)[0]
+        hit = torch.unique(idx)
+        byts += W.decode_bytes(S, T, int(((hit >= lo) & (hit < hi)).sum().item()))
+        h = ops.moe_layer(h, norms[l], 1e-6, *blocks[l].tensors(), S.K, 3)
+    ach = byts / (ms * 1e-3) / 1e9
+    per_layer = 6 if c.world > 1 else 5   # rmsnorm, [epoch bump], route, gate_up, down, combine
+    out = {"metric": f"MoE-only stack decode step ({L} layers, batch {T}) tokens/s",
+           "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+           "ms_per_layer": ms / L, "steps": steps, "layers": L, "batch": T,
+           "parallelism": f"ep{c.world}" if c.world > 1 else "single",
+           "cuda_graph": True, "gpu_launches": per_layer * L * steps, "clocks": clk.summary(),
+           "roofline": {"bound": "hbm", "algorithmic_bytes_per_rank": byts, "unit": "GB/s",
+                        "achieved": ach, "peak": peaks["hbm_gbs"],
+                        "frac": ach / peaks["hbm_gbs"],
+                        "peak_source": f"{peak_kind} (hbm_gbs)"}}
+    del graph, st, blocks, norms
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -322,6 +382,9 @@ def main():
     ap.add_argument("--prefill-T", type=int, default=8192)
     ap.add_argument("--zipf", type=float, default=1.1)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-stack", action="store_true")
+    ap.add_argument("--stack-layers", type=int, default=40)
+    ap.add_argument("--stack-T", type=int, default=64)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
@@ -443,6 +506,10 @@ def main():
                               "algorithmic_flops": gu_flops, "avg_launch_ms": pphase[1],
                               "peak_source": f"{peak_kind} (bf16_tflops, burst)"}
         line["prefill"] = pl
+
+    # ------------------------------------------------------------- stack --
+    if not a.no_stack:
+        line["stack"] = stack_bench(c, a, peaks, peak_kind)
 
     if world == 1 and rank == 0 and not a.no_cpu_baseline:
         ref = cpu_reference(c.wts.to("cpu"), x.cpu(), budget_s=a.cpu_budget)
