@@ -144,6 +144,35 @@ int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, 
                           size_t peer_buf_bytes, int rank, int world, int epoch, uint16_t* y,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* Row-split expert parallelism for prefill-sized batches (the tensor-core
+ * path), in two steps per rank:
+ *  1. pmoe_route_slice routes tokens [t0, t1) (router GEMM, softmax, top-k,
+ *     renormalisation, shared-expert gate) into rows t0.. of the caller's
+ *     full-size arrays topk_idx [T][K] i32, topk_w [T][K] f32,
+ *     shared_gate [T] f32; each rank routes its own slice and the caller
+ *     all-gathers the arrays (a few hundred KiB).
+ *  2. pmoe_block_forward_rows takes the complete routing, dispatches all
+ *     T*K + T rows exactly as a single GPU would, and computes only this
+ *     rank's share: the 256-row blocks of the experts (shared expert
+ *     included) whose middle row falls in [rank*R/world, (rank+1)*R/world) of
+ *     the R dispatched rows -- one contiguous range, so heavy experts are
+ *     split across ranks instead of loading one rank.  y is this rank's
+ *     partial, to be summed across ranks by the caller (as ep.py:140 sums the
+ *     expert-range partials of engine/runtime/ep.py:97-143).
+ * Workspace as pmoe_workspace_size(T, ...). */
+int pmoe_route_slice(const uint16_t* x, int T, int H, int E, int K, int I, int Is, int t0,
+                     int t1, const uint16_t* w_router, const uint16_t* w_sh_gvec,
+                     int32_t* topk_idx, float* topk_w, float* shared_gate, void* workspace,
+                     size_t workspace_bytes, void* stream);
+int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                            const uint16_t* w_router, const uint16_t* w_gate_up,
+                            const uint16_t* w_down, const uint16_t* w_sh_gate,
+                            const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                            const uint16_t* w_sh_gvec, const int32_t* topk_idx,
+                            const float* topk_w, const float* shared_gate, int rank, int world,
+                            int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* One decoder layer of the MoE-only stack: y = x + block(RMSNorm(x)), with
  * RMSNorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w_norm)) in fp32 and the
  * residual added as bf16(x + bf16(block)) -- Qwen3_5MoeDecoderLayer's

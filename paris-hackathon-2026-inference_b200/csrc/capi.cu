@@ -118,6 +118,15 @@ struct LayerArgs {
   float eps;
 };
 
+// Row-split expert parallelism: routing given (every rank holds all of it)
+// and this rank computes its share of the dispatched rows.
+struct RowSplit {
+  const int32_t* topk_idx;
+  const float* topk_w;
+  const float* shared_gate;
+  int rank, world;
+};
+
 // Shared implementation of the forward entry points.  `ep` (world > 0)
 // selects the expert-parallel NVLink exchange; sh_lo/sh_hi is the token range
 // whose shared-expert rows this call computes; `layer` (may be null) adds the
@@ -129,7 +138,8 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                         const uint16_t* w_sh_gvec, int expert_lo, int expert_hi, int sh_lo,
                         int sh_hi, int flags, uint16_t* y, void* workspace,
                         size_t workspace_bytes, void* stream, void* const* events, int n_events,
-                        const EpPeers& ep, const LayerArgs* layer = nullptr) {
+                        const EpPeers& ep, const LayerArgs* layer = nullptr,
+                        const RowSplit* rs = nullptr) {
   int s = check_shape(T, H, E, K, I, Is);
   if (s != PMOE_OK) return s;
   if (expert_lo < 0 || expert_hi > E || expert_lo > expert_hi) return PMOE_ERR_ARG;
@@ -160,9 +170,16 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   if ((flags & PMOE_F_FORCE_TC) && !tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
   // Weight streaming while the layer is HBM-bound (decode), tcgen05 grouped
   // GEMMs beyond.  The NVLink exchange rides on the streaming kernels.
-  const bool use_tc = ep.world == 0 &&
-                      ((flags & PMOE_F_FORCE_TC) ||
-                       (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d)));
+  bool use_tc = ep.world == 0 &&
+                ((flags & PMOE_F_FORCE_TC) ||
+                 (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d)));
+  if (rs) {
+    if (rs->world < 1 || rs->rank < 0 || rs->rank >= rs->world || !rs->topk_idx ||
+        !rs->topk_w || !rs->shared_gate || ep.world > 0 || (flags & PMOE_F_FORCE_STREAM))
+      return PMOE_ERR_ARG;
+    if (!tc_supported(d) || !route_tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
+    use_tc = true;
+  }
   if (ep.world > 0 && (flags & PMOE_F_FORCE_TC)) return PMOE_ERR_UNSUPPORTED;
   auto mark = [&](int i) {
     if (events && i < n_events && events[i])
@@ -187,10 +204,12 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   // Prefill-sized batches route on the tensor cores.
   const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
   const cudaError_t rerr =
-      route_tc ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
-                                 with_shared, with_routed, ws, st)
-               : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
-                              with_shared, with_routed, ws, st);
+      rs ? launch_dispatch_given(d, rs->topk_idx, rs->topk_w, rs->shared_gate, expert_lo,
+                                 expert_hi, with_shared, with_routed, ws, st)
+      : route_tc ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+                                   with_shared, with_routed, ws, st)
+                 : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+                                with_shared, with_routed, ws, st);
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
@@ -198,7 +217,8 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
       if (events && i + 1 < n_events) ev[i] = events[i + 1];
     if (launch_tc_experts(d, xin, bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                           bf(w_sh_down), ws, resid, reinterpret_cast<__nv_bfloat16*>(y),
-                          expert_lo, expert_hi, with_shared, with_routed, st, ev) != cudaSuccess)
+                          expert_lo, expert_hi, with_shared, with_routed, rs ? rs->rank : 0,
+                          rs ? rs->world : 1, st, ev) != cudaSuccess)
       return PMOE_ERR_CUDA;
     if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
     return PMOE_OK;
@@ -323,6 +343,49 @@ int pmoe_layer_forward(const uint16_t* x, int T, int H, int E, int K, int I, int
   return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
                       w_sh_down, w_sh_gvec, expert_lo, expert_hi, shared_lo, shared_hi, flags, y,
                       workspace, workspace_bytes, stream, nullptr, 0, ep, &layer);
+}
+
+int pmoe_route_slice(const uint16_t* x, int T, int H, int E, int K, int I, int Is, int t0,
+                     int t1, const uint16_t* w_router, const uint16_t* w_sh_gvec,
+                     int32_t* topk_idx, float* topk_w, float* shared_gate, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  int s = check_shape(T, H, E, K, I, Is);
+  if (s != PMOE_OK) return s;
+  if (t0 < 0 || t1 > T || t0 > t1) return PMOE_ERR_ARG;
+  if (t0 == t1) return PMOE_OK;
+  const void* ptrs[] = {x, w_router, w_sh_gvec, topk_idx, topk_w, shared_gate, workspace};
+  for (const void* p : ptrs)
+    if (!p) return PMOE_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_router) || !aligned16(w_sh_gvec) || !aligned16(workspace))
+    return PMOE_ERR_ALIGN;
+  if ((s = ensure_device()) != PMOE_OK) return s;
+  Dims d = make_dims(T, H, E, K, I, Is);
+  if (!route_tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
+  Workspace ws = carve(workspace, d);
+  if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Dims ds = make_dims(t1 - t0, H, E, K, I, Is);
+  if (cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st) != cudaSuccess ||
+      launch_router_tc(ds, bf(x) + size_t(t0) * H, bf(w_router), bf(w_sh_gvec),
+                       topk_idx + size_t(t0) * K, topk_w + size_t(t0) * K, shared_gate + t0,
+                       ws.hist, ws.status + 1, st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  return PMOE_OK;
+}
+
+int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I, int Is,
+                            const uint16_t* w_router, const uint16_t* w_gate_up,
+                            const uint16_t* w_down, const uint16_t* w_sh_gate,
+                            const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                            const uint16_t* w_sh_gvec, const int32_t* topk_idx,
+                            const float* topk_w, const float* shared_gate, int rank, int world,
+                            int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  const EpPeers none{};
+  const RowSplit rs{topk_idx, topk_w, shared_gate, rank, world};
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, 0, E, 0, T, flags, y, workspace, workspace_bytes,
+                      stream, nullptr, 0, none, nullptr, &rs);
 }
 
 int pmoe_rmsnorm(const uint16_t* x, int T, int H, const uint16_t* w_norm, float eps,

@@ -23,6 +23,7 @@ struct Workspace {
   int32_t* sorted_tok;  // [T*K+T]    source token of each dispatched row
   int32_t* sorted_slot; // [T*K]
   int32_t* pair_dst;    // [T*K+T]    destination row in `rows` (t*K+s, or T*K+t)
+  int32_t* pair_pos;    // [T*K+T]    inverse: dispatched row of destination row q (prefill path)
   float* pair_w;        // [T*K+T]    routing weight (or shared gate) of each row
   float* logit_part;    // [T][Rpad]   router logits (bf16-rounded) + raw shared-gate sum
   int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
@@ -31,12 +32,13 @@ struct Workspace {
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
   __nv_bfloat16* x_perm; // [T*K+T][H] x rows in dispatch order (tensor-core path; aliases
                          //            `rows`, which only the streaming path uses)
-  __nv_bfloat16* rows_bf16; // [T*K+T][H] weighted expert outputs, token-major (tensor-core
+  __nv_bfloat16* rows_bf16; // [T*K+T][H] expert outputs (unweighted), token-major (tensor-core
                             //  path, written by down after gate_up has consumed x_perm)
   int4* gu_tiles;       // tensor-core path tile lists: (expert, row0, nrows, n_block)
   int4* dn_tiles;
   int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
-  int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M; [4]/[5] gate_up/down queue tickets
+  int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M blocks; [4]/[5] the dispatched
+                        //     rows [lo, hi) this call computes (row-split expert parallelism)
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
@@ -118,6 +120,7 @@ inline Workspace carve(void* base, const Dims& d) {
   w.sorted_tok = (int32_t*)take(sizeof(int32_t) * R);
   w.sorted_slot = (int32_t*)take(sizeof(int32_t) * P);
   w.pair_dst = (int32_t*)take(sizeof(int32_t) * R);
+  w.pair_pos = (int32_t*)take(sizeof(int32_t) * R);
   w.pair_w = (float*)take(sizeof(float) * R);
   w.logit_part = (float*)take(sizeof(float) * size_t(d.KS) * d.T * d.Rpad);
   w.status = (int32_t*)take(sizeof(int32_t) * 8);

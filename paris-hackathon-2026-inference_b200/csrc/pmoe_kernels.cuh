@@ -24,8 +24,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
-                              int with_shared, int with_routed, cudaStream_t st,
-                              void* const events[3]);
+                              int with_shared, int with_routed, int rank, int world,
+                              cudaStream_t st, void* const events[3]);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch).
@@ -34,6 +34,15 @@ bool route_tc_supported(const Dims& d);
 cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                             const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                             int with_routed, const Workspace& ws, cudaStream_t st);
+// The router GEMM + top-k alone, for d.T tokens starting at x, into the given
+// arrays (hist: per-128-token-tile expert counts, status: error word).
+cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                             const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
+                             float* shared_gate, int32_t* hist, int* status, cudaStream_t st);
+// Dispatch (histogram, scan, scatter) from routing computed elsewhere.
+cudaError_t launch_dispatch_given(const Dims& d, const int32_t* topk_idx, const float* topk_w,
+                                  const float* shared_gate, int lo, int hi, int with_shared,
+                                  int with_routed, const Workspace& ws, cudaStream_t st);
 
 // resid (may be null): y = bf16(resid + bf16(sum)), the decoder layer's residual.
 cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, int with_shared,

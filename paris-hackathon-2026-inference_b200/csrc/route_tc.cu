@@ -14,8 +14,7 @@
 //   route_scatter_kernel  one CTA per tile: stable ranks of the tile's pairs
 //                      within their expert (pair order kept, as the stable
 //                      torch.sort of engine/kernels/moe_dispatch.py:129), the
-//                      permuted rows, the shared-expert rows, and zeroes the
-//                      tile's rows of the fp32 output accumulator.
+//                      permuted rows and the shared-expert rows.
 // Reference: Qwen3_5MoeTopKRouter.forward (modeling_qwen3_5_moe.py:762-770).
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
@@ -281,8 +280,8 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
     const float* __restrict__ shared_gate, const int32_t* __restrict__ base, int T, int H, int E,
     int K, int sh_lo, int sh_hi, int32_t* __restrict__ sorted_tok,
-    int32_t* __restrict__ sorted_slot,
-    int32_t* __restrict__ pair_dst, float* __restrict__ pair_w) {
+    int32_t* __restrict__ sorted_slot, int32_t* __restrict__ pair_dst,
+    int32_t* __restrict__ pair_pos, float* __restrict__ pair_w) {
   __shared__ int s_wcnt[32 * 256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const int P = T * K;
@@ -301,6 +300,7 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
     sorted_tok[pos] = p / K;
     sorted_slot[pos] = p % K;
     pair_dst[pos] = p;
+    pair_pos[p] = pos;
     pair_w[pos] = topk_w[p];
   }
   const int tb = blockIdx.x * kRtM;
@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(1024) route_scatter_kernel(
     if (t >= sh_lo && t < sh_hi) {  // dispatched row P+(t-sh_lo) is token t
       sorted_tok[P + t - sh_lo] = t;
       pair_dst[P + t - sh_lo] = P + t;
+      pair_pos[P + t] = P + t - sh_lo;
       pair_w[P + t - sh_lo] = shared_gate[t];
     }
   }
@@ -323,31 +324,80 @@ bool route_tc_supported(const Dims& d) {
   return d.E <= kRtN && d.K <= kRtMaxK && d.H % kRtK == 0;
 }
 
-cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
-                            const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
-                            int with_routed, const Workspace& ws, cudaStream_t st) {
+// Per-tile expert histogram of given routing (the router kernel produces it
+// in its epilogue; this is for routing computed elsewhere): one CTA per
+// 128-token tile.
+__global__ void __launch_bounds__(256) route_hist_kernel(const int32_t* __restrict__ topk_idx,
+                                                         int T, int E, int K,
+                                                         int32_t* __restrict__ hist) {
+  __shared__ int s_hist[kRtN];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * kRtM * K, p1 = min(T, (blockIdx.x + 1) * kRtM) * K;
+  for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) atomicAdd(&s_hist[topk_idx[p]], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[size_t(blockIdx.x) * E + e] = s_hist[e];
+}
+
+cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                             const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
+                             float* shared_gate, int32_t* hist, int* status, cudaStream_t st) {
   CUtensorMap tm_x, tm_w, tm_g;
   const uint64_t H = d.H;
   if (!make_tmap_bf16_2d(&tm_x, x, H, d.T, H * 2, kRtK, kRtM) ||
       !make_tmap_bf16_2d(&tm_w, w_router, H, d.E, H * 2, kRtK, kRtN) ||
       !make_tmap_bf16_2d(&tm_g, w_gvec, H, 1, H * 2, kRtK, kRtN2))
     return cudaErrorInvalidValue;
-  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
-  if (err != cudaSuccess) return err;
   const int nb = (d.T + kRtM - 1) / kRtM;
   router_tc_kernel<<<nb, kRtThreads, kRtSmem, st>>>(tm_x, tm_w, tm_g, d.T, d.H, d.E, d.K,
-                                                    ws.topk_idx, ws.topk_w, ws.shared_gate,
-                                                    ws.hist, ws.status + 1);
+                                                    topk_idx, topk_w, shared_gate, hist, status);
+  return cudaGetLastError();
+}
+
+// Scan + scatter from the routing in ws.topk_idx / topk_w / shared_gate and
+// the tile histograms in ws.hist.
+static cudaError_t launch_dispatch(const Dims& d, int lo, int hi, int with_shared,
+                                   int with_routed, const Workspace& ws, cudaStream_t st) {
+  const int nb = (d.T + kRtM - 1) / kRtM;
   route_scan_kernel<<<1, kScanThreads, 0, st>>>(ws.hist, nb, d.T, d.E, d.K, lo, hi, with_shared,
                                                 with_routed, d.sh_lo, d.sh_hi, ws.hist_base,
-                                                ws.offsets, ws.active,
-                                                ws.n_active);
+                                                ws.offsets, ws.active, ws.n_active);
   route_scatter_kernel<<<nb, kRtM * d.K, 0, st>>>(ws.topk_idx, ws.topk_w, ws.shared_gate,
                                                   ws.hist_base, d.T, d.H, d.E, d.K, d.sh_lo,
-                                                  d.sh_hi,
-                                                  ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
-                                                  ws.pair_w);
+                                                  d.sh_hi, ws.sorted_tok, ws.sorted_slot,
+                                                  ws.pair_dst, ws.pair_pos, ws.pair_w);
   return cudaGetLastError();
+}
+
+cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
+                            const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
+                            int with_routed, const Workspace& ws, cudaStream_t st) {
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  if (err != cudaSuccess) return err;
+  err = launch_router_tc(d, x, w_router, w_gvec, ws.topk_idx, ws.topk_w, ws.shared_gate, ws.hist,
+                         ws.status + 1, st);
+  if (err != cudaSuccess) return err;
+  return launch_dispatch(d, lo, hi, with_shared, with_routed, ws, st);
+}
+
+cudaError_t launch_dispatch_given(const Dims& d, const int32_t* topk_idx, const float* topk_w,
+                                  const float* shared_gate, int lo, int hi, int with_shared,
+                                  int with_routed, const Workspace& ws, cudaStream_t st) {
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  const size_t P = size_t(d.T) * d.K;
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(ws.topk_idx, topk_idx, P * 4, cudaMemcpyDeviceToDevice, st);
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(ws.topk_w, topk_w, P * 4, cudaMemcpyDeviceToDevice, st);
+  if (err == cudaSuccess)
+    err = cudaMemcpyAsync(ws.shared_gate, shared_gate, size_t(d.T) * 4, cudaMemcpyDeviceToDevice,
+                          st);
+  if (err != cudaSuccess) return err;
+  const int nb = (d.T + kRtM - 1) / kRtM;
+  route_hist_kernel<<<nb, 256, 0, st>>>(ws.topk_idx, d.T, d.E, d.K, ws.hist);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  return launch_dispatch(d, lo, hi, with_shared, with_routed, ws, st);
 }
 
 }  // namespace pmoe

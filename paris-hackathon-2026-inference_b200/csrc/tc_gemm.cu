@@ -427,34 +427,58 @@ __device__ __forceinline__ void plan_scan(int (&v)[NV], int (&ex)[NV], int (*s_w
 
 __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-    const int32_t* __restrict__ n_active, int E, int H, int I, int Is, int4* __restrict__ gu_tiles,
-    int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles, int32_t* __restrict__ counts) {
+    const int32_t* __restrict__ n_active, int E, int H, int I, int Is, int rank, int world,
+    int4* __restrict__ gu_tiles, int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles,
+    int32_t* __restrict__ counts) {
   __shared__ int s_wsum[3][32];
   __shared__ int s_tot[3];
-  __shared__ int4 s_ex[kPlanThreads];       // (expert, p0, rows, gate_up feature blocks)
+  __shared__ int4 s_ex[kPlanThreads];       // (expert, first owned row, owned rows, nb_gu)
   __shared__ int4 s_base[kPlanThreads];     // first gate_up / down tile, first M block
+  __shared__ int s_lo, s_hi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int na = n_active[0];
   const int nb_dn = H / 256;
-  int e = -1, n = 0, p0 = 0, nbg = 0;
+  if (tid == 0) {
+    s_lo = 0x7fffffff;
+    s_hi = 0;
+  }
+  __syncthreads();
+  // Row split across `world` ranks: the 256-row blocks of every expert, in
+  // dispatch order, go to the rank whose share of the R dispatched rows holds
+  // the block's middle row, so each rank owns one contiguous row range.
+  const long R = offsets[E + 1];
+  int e = -1, r0 = 0, nrow = 0, nbg = 0;
   if (tid < na) {
     e = active[tid];
-    p0 = offsets[e];
-    n = offsets[e + 1] - p0;
+    const int p0 = offsets[e], n = offsets[e + 1] - p0;
     nbg = (e == E ? Is : I) / 128;
+    const int mt = (n + kTok - 1) / kTok;
+    int ma = mt, mb = mt;
+    for (int m = 0; m < mt; ++m) {
+      const long mid = p0 + m * kTok + min(kTok, n - m * kTok) / 2;
+      const bool own = mid * world >= long(rank) * R && mid * world < long(rank + 1) * R;
+      if (own && ma == mt) ma = m;
+      if (own) mb = m + 1;
+    }
+    if (ma < mb) {
+      r0 = p0 + ma * kTok;
+      nrow = min(n, mb * kTok) - ma * kTok;
+      atomicMin(&s_lo, r0);
+      atomicMax(&s_hi, r0 + nrow);
+    }
   }
-  // Tiles per expert: its 256-row blocks (the last one partial) x feature
-  // blocks, row block outer, experts in active-list order.
-  const int mt = (n + kTok - 1) / kTok;
-  int v[3] = {mt * nbg, mt * nb_dn, (n + kGatherRows - 1) / kGatherRows};
+  const int mt = (nrow + kTok - 1) / kTok;
+  int v[3] = {mt * nbg, mt * nb_dn, (nrow + kGatherRows - 1) / kGatherRows};
   int ex[3];
   plan_scan<3>(v, ex, s_wsum, s_tot);
-  s_ex[tid] = make_int4(e, p0, n, nbg);
+  s_ex[tid] = make_int4(e, r0, nrow, nbg);
   s_base[tid] = make_int4(ex[0], ex[1], ex[2], 0);
   if (tid == 0) {
     counts[0] = s_tot[0];
     counts[1] = s_tot[1];
     counts[2] = s_tot[2];
+    counts[4] = s_lo <= s_hi ? s_lo : 0;
+    counts[5] = s_lo <= s_hi ? s_hi : 0;
   }
   __syncthreads();
   // Write-out: one warp per active expert, lanes striding over its tiles.
@@ -485,6 +509,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
     const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ topk_idx,
     const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
     int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ row_range,
     const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
   const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int cols8 = H / 8;
@@ -501,13 +526,22 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
       s[2 * j + 1] = fmaf(w, f.y, s[2 * j + 1]);
     }
   };
+  // Row split: only rows this rank computed (dispatched position in range).
+  const int p_lo = pair_pos ? row_range[0] : 0, p_hi = pair_pos ? row_range[1] : 0;
+  auto mine = [&](size_t q) {
+    if (!pair_pos) return true;
+    const int p = pair_pos[q];
+    return p >= p_lo && p < p_hi;
+  };
   if (with_routed) {
     for (int k = 0; k < K; ++k) {
-      const int e = topk_idx[size_t(t) * K + k];
-      if (e >= lo && e < hi) add(size_t(t) * K + k, topk_w[size_t(t) * K + k]);
+      const size_t q = size_t(t) * K + k;
+      const int e = topk_idx[q];
+      if (e >= lo && e < hi && mine(q)) add(q, topk_w[q]);
     }
   }
-  if (with_shared && t >= sh_lo && t < sh_hi) add(size_t(T) * K + t, shared_gate[t]);
+  if (with_shared && t >= sh_lo && t < sh_hi && mine(size_t(T) * K + t))
+    add(size_t(T) * K + t, shared_gate[t]);
   if (resid) {  // decoder layer: y = bf16(resid + bf16(sum)), as residual + mlp(x) in bf16
     const uint4 rv = reinterpret_cast<const uint4*>(resid + size_t(t) * H)[c8];
     const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
@@ -585,8 +619,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_gate, const __nv_bfloat16* w_sh_up,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
-                              int with_shared, int with_routed, cudaStream_t st,
-                              void* const events[3]) {
+                              int with_shared, int with_routed, int rank, int world,
+                              cudaStream_t st, void* const events[3]) {
   // events (each may be null): before gate_up, after gate_up, after down
   auto mark = [&](int i) {
     return events[i] ? cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st) : cudaSuccess;
@@ -610,8 +644,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
       !make_tmap_bf16_2d(&tm_xp32, ws.x_perm, H, R, H * 2, kBK, kRowChunk))
     return cudaErrorInvalidValue;
   plan_tiles_kernel<<<1, kPlanThreads, 0, st>>>(ws.offsets, ws.active, ws.n_active, d.E, d.H,
-                                                d.I, d.Is, ws.gu_tiles, ws.dn_tiles,
-                                                ws.m_tiles, ws.tile_counts);
+                                                d.I, d.Is, rank, world, ws.gu_tiles,
+                                                ws.dn_tiles, ws.m_tiles, ws.tile_counts);
   gather_rows_kernel<<<2 * g_pairs * 16, kGatherThreads, 0, st>>>(
       x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, ws.x_perm);
   cudaError_t err = mark(0);
@@ -632,7 +666,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   const long n8 = long(T) * d.H / 8;
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
       ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
-      with_routed, d.sh_lo, d.sh_hi, resid, y);
+      with_routed, d.sh_lo, d.sh_hi, world > 1 ? ws.pair_pos : nullptr, ws.tile_counts + 4,
+      resid, y);
   return cudaGetLastError();
 }
 

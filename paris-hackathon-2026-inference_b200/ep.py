@@ -73,8 +73,10 @@ def exchange_handles(local: bytes, group=None) -> list[bytes]:
 class EPGroup:
     """One rank's state for expert-parallel MoE calls.
 
-    ``mode`` is "fused" (NVLink exchange for T <= 64, NCCL partials beyond)
-    or "nccl" (always partials + all_reduce: the comparator)."""
+    ``mode`` is "fused" (T <= t_max: NVLink exchange inside the kernels;
+    beyond: sliced routing + row-split expert GEMMs + NCCL all_reduce) or
+    "nccl" (contiguous expert ranges, replicated routing, partials summed with
+    all_reduce: the reference's ep_forward, the comparator)."""
 
     def __init__(self, num_experts: int, hidden: int, top_k: int, mode: str = "fused",
                  t_max: int = FUSED_MAX_T, group=None):
@@ -141,12 +143,46 @@ class EPGroup:
                 ws.data_ptr(), nbytes, st)
             _lib.check("pmoe_block_forward_ep", s)
             return y
+        if self.mode == "fused" and self.world > 1:
+            return self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st)
         s = self.lib.pmoe_block_forward_ep(
             x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
             None, 0, self.rank, self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)
         _lib.check("pmoe_block_forward_ep", s)
         if self.world > 1:
             dist.all_reduce(y, group=self.group)
+        return y
+
+    def _forward_rows(self, x, wp, I, Is, flags, y, ws, nbytes, st):
+        """Prefill-sized batches: each rank routes its slice of the tokens into
+        its record of one packed buffer ([idx chunk*K | w chunk*K | gate chunk]
+        per rank, 4-byte words), one NCCL all_gather shares the records, every
+        rank computes its share of the dispatched rows
+        (pmoe_block_forward_rows) and the partials are summed with an NCCL
+        all_reduce."""
+        T, H = x.shape
+        K, world, rank = self.K, self.world, self.rank
+        chunk = (T + world - 1) // world
+        rec = chunk * (2 * K + 1)
+        buf = torch.empty((world, rec), dtype=torch.int32, device=x.device)
+        mine = buf[rank]
+        t0 = min(rank * chunk, T)
+        t1 = min(t0 + chunk, T)
+        # the slice writes rows t0..t1 of arrays addressed from token 0, so
+        # hand it base pointers shifted back by t0 rows into this record
+        base = mine.data_ptr()
+        _lib.check("pmoe_route_slice", self.lib.pmoe_route_slice(
+            x.data_ptr(), T, H, self.E, K, I, Is, t0, t1, wp[0], wp[6],
+            base - t0 * K * 4, base + (chunk * K - t0 * K) * 4,
+            base + (2 * chunk * K - t0) * 4, ws.data_ptr(), nbytes, st))
+        dist.all_gather_into_tensor(buf, mine, group=self.group)
+        idx = buf[:, :chunk * K].reshape(world * chunk, K)[:T].contiguous()
+        wts = buf[:, chunk * K:2 * chunk * K].reshape(world * chunk, K)[:T].contiguous()
+        gate = buf[:, 2 * chunk * K:].reshape(world * chunk)[:T].contiguous()
+        _lib.check("pmoe_block_forward_rows", self.lib.pmoe_block_forward_rows(
+            x.data_ptr(), T, H, self.E, K, I, Is, *wp, idx.data_ptr(), wts.data_ptr(),
+            gate.data_ptr(), rank, world, flags, y.data_ptr(), ws.data_ptr(), nbytes, st))
+        dist.all_reduce(y, group=self.group)
         return y
 
     def layer_forward(self, x: torch.Tensor, w_norm: torch.Tensor, eps: float, weights,

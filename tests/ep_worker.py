@@ -29,7 +29,7 @@ def main():
     fused = ep.EPGroup(S.E, S.H, S.K, mode="fused")
     nccl = ep.EPGroup(S.E, S.H, S.K, mode="nccl")
     ok = True
-    for T in (1, 5, 64, 64, 64, 200):
+    for T in (1, 5, 64, 64, 64, 200, 1024):
         x = W.make_hidden(T, S, seed=100 + T, device=dev)
         ref = ops.moe_block(x, *tensors, S.K, 0, S.E, 3).float().cpu().numpy()
         for name, g in (("fused", fused), ("nccl", nccl)):

@@ -93,3 +93,42 @@ def test_rank_partials_sum_to_full(T, flags):
         acc += y.float()
     torch.cuda.synchronize()
     assert O.rel_l2(acc.cpu().numpy(), full.cpu().numpy()) < 5e-3
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_split_partials_sum_to_full(world):
+    """Row-split EP for prefill-sized batches, its ranks run one after another
+    on one GPU: sliced routing equals full routing bit for bit, and the
+    ranks' row-share partials sum to the single-GPU block."""
+    from oracle import moe_oracle as O
+    from paris_moe_b200 import _lib, ops, workload as W
+    lib = _lib.load()
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=5, device="cuda", zipf_s=1.1)
+    T = 1000
+    x = W.make_hidden(T, S, seed=8, device="cuda", zipf=True)
+    full = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3).float()
+    ref_idx, ref_w, *_ = ops.moe_route(x, wts.w_router, wts.w_sh_gvec, S.K)
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    wp = [t.data_ptr() for t in wts.tensors()]
+    idx = torch.empty((T, S.K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, S.K), dtype=torch.float32, device="cuda")
+    gate = torch.empty((T,), dtype=torch.float32, device="cuda")
+    chunk = (T + world - 1) // world
+    for r in range(world):
+        t0, t1 = min(r * chunk, T), min((r + 1) * chunk, T)
+        assert lib.pmoe_route_slice(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, t0, t1, wp[0],
+                                    wp[6], idx.data_ptr(), w.data_ptr(), gate.data_ptr(),
+                                    ws.data_ptr(), n, st) == 0
+    assert torch.equal(idx.long(), ref_idx.long())
+    assert torch.equal(w, ref_w)
+    total = torch.zeros_like(full)
+    for r in range(world):
+        y = torch.empty((T, S.H), dtype=torch.bfloat16, device="cuda")
+        assert lib.pmoe_block_forward_rows(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *wp,
+                                           idx.data_ptr(), w.data_ptr(), gate.data_ptr(), r,
+                                           world, 3, y.data_ptr(), ws.data_ptr(), n, st) == 0
+        total += y.float()
+    assert O.rel_l2(total.cpu().numpy(), full.cpu().numpy()) < 5e-3
