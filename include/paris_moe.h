@@ -173,6 +173,23 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
                             int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* Sum of the row-split partials over NVLink, in place of the caller's NCCL
+ * all_reduce (ep.py:140): each rank owns a buffer of pmoe_rows_buffer_bytes
+ * (pmoe_ipc_alloc'ed, zeroed, IPC-mapped on every rank; bufs[q] = rank q's
+ * buffer as mapped here).  Per call with epoch e (> 0, +1 per call, same on
+ * every rank): write this rank's partial [T][H] bf16 into the region that
+ * pmoe_rows_partial(own buffer, T_max, H, e) returns (e.g. as the y of
+ * pmoe_block_forward_rows), then pmoe_rows_allreduce: every rank's flags say
+ * its partial is complete; rank r sums token slice [r*T/N, (r+1)*T/N) over
+ * ranks 0..N-1 in that order in fp32 (deterministic), raises a second set of
+ * flags, and y = the reduced slices of all ranks.  Waits are bounded
+ * (status 4 via pmoe_rows_status on timeout).  No collective kernel. */
+int pmoe_rows_buffer_bytes(int T_max, int H, size_t* bytes);
+int pmoe_rows_partial(void* own_buf, int T_max, int H, int epoch, void** partial);
+int pmoe_rows_allreduce(void* const* bufs, int T_max, int T, int H, int rank, int world,
+                        int epoch, uint16_t* y, void* stream);
+int pmoe_rows_status(const void* own_buf, int* status);
+
 /* One decoder layer of the MoE-only stack: y = x + block(RMSNorm(x)), with
  * RMSNorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w_norm)) in fp32 and the
  * residual added as bf16(x + bf16(block)) -- Qwen3_5MoeDecoderLayer's

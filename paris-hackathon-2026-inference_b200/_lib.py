@@ -38,6 +38,10 @@ SIGNATURES = {
                                 _P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_P), _SZ, _I,
                                 _I, _I, _P, _P, _SZ, _P]),
     "pmoe_rmsnorm": (_I, [_P, _I, _I, _P, ctypes.c_float, _P, _P]),
+    "pmoe_rows_buffer_bytes": (_I, [_I, _I, ctypes.POINTER(_SZ)]),
+    "pmoe_rows_partial": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
+    "pmoe_rows_allreduce": (_I, [ctypes.POINTER(_P), _I, _I, _I, _I, _I, _I, _P, _P]),
+    "pmoe_rows_status": (_I, [_P, ctypes.POINTER(_I)]),
     "pmoe_route_slice": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ,
                               _P]),
     "pmoe_block_forward_rows": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,

@@ -388,6 +388,46 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
                       stream, nullptr, 0, none, nullptr, &rs);
 }
 
+int pmoe_rows_buffer_bytes(int T_max, int H, size_t* bytes) {
+  if (!bytes || T_max <= 0 || H <= 0 || H % 8 != 0) return PMOE_ERR_ARG;
+  *bytes = rx_buffer_bytes(T_max, H);
+  return PMOE_OK;
+}
+
+int pmoe_rows_partial(void* own_buf, int T_max, int H, int epoch, void** partial) {
+  if (!own_buf || !partial || T_max <= 0 || H <= 0 || epoch <= 0) return PMOE_ERR_ARG;
+  *partial = static_cast<char*>(own_buf) + rx_region_offset(T_max, H, epoch);
+  return PMOE_OK;
+}
+
+int pmoe_rows_allreduce(void* const* bufs, int T_max, int T, int H, int rank, int world,
+                        int epoch, uint16_t* y, void* stream) {
+  if (!bufs || !y || world < 1 || world > kMaxRanks || rank < 0 || rank >= world ||
+      epoch <= 0 || T < 0 || T > T_max || H <= 0 || H % 8 != 0)
+    return PMOE_ERR_ARG;
+  for (int q = 0; q < world; ++q)
+    if (!bufs[q] || !aligned16(bufs[q])) return PMOE_ERR_ARG;
+  if (!aligned16(y)) return PMOE_ERR_ALIGN;
+  if (T == 0) return PMOE_OK;
+  int s = ensure_device();
+  if (s != PMOE_OK) return s;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  return launch_rows_allreduce(bufs, T_max, world, rank, epoch, T, H,
+                               reinterpret_cast<__nv_bfloat16*>(y), sms,
+                               static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
+int pmoe_rows_status(const void* own_buf, int* status) {
+  if (!own_buf || !status) return PMOE_ERR_ARG;
+  return cudaMemcpy(status, static_cast<const char*>(own_buf) + rx_status_offset(), sizeof(int),
+                    cudaMemcpyDeviceToHost) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
 int pmoe_rmsnorm(const uint16_t* x, int T, int H, const uint16_t* w_norm, float eps,
                  uint16_t* out, void* stream) {
   if (T < 0 || H <= 0 || H % 8 != 0 || !(eps >= 0.f)) return PMOE_ERR_ARG;

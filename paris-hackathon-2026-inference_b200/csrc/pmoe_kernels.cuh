@@ -50,6 +50,13 @@ cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, i
                            cudaStream_t st, const EpPeers& ep);
 cudaError_t launch_epoch_bump(int* epoch, cudaStream_t st);
 
+// NVLink all-reduce of row-split partials (rows_exchange.cu).
+size_t rx_buffer_bytes(int T_max, int H);
+size_t rx_region_offset(int T_max, int H, int epoch);
+size_t rx_status_offset();
+cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                  int T, int H, __nv_bfloat16* y, int num_sms, cudaStream_t st);
+
 // out = Qwen3_5MoeRMSNorm(x; w, eps), bf16 [T][H].
 cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int T,
                            int H, __nv_bfloat16* out, cudaStream_t st);

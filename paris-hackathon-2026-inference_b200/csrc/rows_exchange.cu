@@ -1,0 +1,154 @@
+// All-reduce of the per-rank partial outputs of row-split expert parallelism
+// (prefill) over NVLink, replacing the NCCL all_reduce of ep.py:140.
+//
+// Buffer of each rank (CUDA-IPC mapped on every rank):
+//   [0, 256)     flags A: flagsA[q] = epoch when rank q's partial is complete
+//   [256, 512)   flags B: flagsB[q] = epoch when rank q's token slice is reduced
+//   [512, 520)   ticket (CTA completion counter), status word
+//   [1024, ...)  two parity regions of T_max x H bf16
+// Per call (epoch e > 0, parity e & 1), after this rank wrote its partial into
+// its own region:
+//   publish      raise flagsA[rank] = e on every rank
+//   reduce       wait (bounded) for every rank's flagsA; rank r sums its token
+//                slice [r*T/N, (r+1)*T/N) over ranks 0..N-1 in that order (fp32,
+//                peer loads), stores the bf16 result into its own region, and
+//                its last CTA raises flagsB[r] = e on every rank
+//   gather       wait (bounded) for every rank's flagsB; y[t] = region of the
+//                slice owner of t (peer loads)
+// A rank one call ahead writes the other parity; it cannot be two calls ahead
+// (its reduce of call e+1 waits for every rank's partial of e+1, written after
+// that rank's gather of e).
+#include "pmoe_common.cuh"
+#include "pmoe_kernels.cuh"
+#include "pmoe_tma.cuh"
+
+namespace pmoe {
+
+constexpr size_t kRxHeader = 1024;
+constexpr int kRxFlagsA = 0, kRxFlagsB = 256, kRxTicket = 512, kRxStatus = 516;
+constexpr int kRxThreads = 256;
+
+struct RxPeers {
+  char* base[kMaxRanks];
+  int world, rank, epoch;
+  size_t region;  // bytes per parity region
+};
+
+__device__ __forceinline__ __nv_bfloat16* rx_rows(const RxPeers& p, int q) {
+  return reinterpret_cast<__nv_bfloat16*>(p.base[q] + kRxHeader + size_t(p.epoch & 1) * p.region);
+}
+__device__ __forceinline__ int* rx_flags(const RxPeers& p, int q, int off) {
+  return reinterpret_cast<int*>(p.base[q] + off);
+}
+
+// Bounded wait of one thread for flags[0..world) >= epoch; false on timeout.
+__device__ bool rx_wait(const RxPeers& p, int off) {
+  const long long t0 = clock64();
+  const int* f = rx_flags(p, p.rank, off);
+  for (int q = 0; q < p.world; ++q) {
+    while (ld_acquire_sys(f + q) < p.epoch) {
+      if (clock64() - t0 > kWaitBudgetCycles) {
+        atomicCAS(rx_flags(p, p.rank, kRxStatus), 0, kStatusTimeoutPeer);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__global__ void rx_publish_kernel(RxPeers p) {
+  __threadfence_system();
+  for (int q = 0; q < p.world; ++q) st_release_sys(rx_flags(p, q, kRxFlagsA) + p.rank, p.epoch);
+}
+
+__global__ void __launch_bounds__(kRxThreads) rx_reduce_kernel(RxPeers p, int T, int H) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = rx_wait(p, kRxFlagsA) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  const int t0 = int(long(p.rank) * T / p.world), t1 = int(long(p.rank + 1) * T / p.world);
+  const int h8 = H / 8;
+  const long n = long(t1 - t0) * h8;
+  __nv_bfloat16* own = rx_rows(p, p.rank);
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += long(gridDim.x) * blockDim.x) {
+    const size_t off = size_t(t0) * H + size_t(i) * 8;  // row-major: slice rows are contiguous
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < p.world; ++q) {  // fixed order: deterministic
+      const uint4 v = *reinterpret_cast<const uint4*>(rx_rows(p, q) + off);
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b[j]);
+        s[2 * j] += f.x;
+        s[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
+      op[j] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    *reinterpret_cast<uint4*>(own + off) = o;
+  }
+  // The last CTA to finish raises flagsB[rank] on every rank.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ticket = rx_flags(p, p.rank, kRxTicket);
+    if (atomicAdd(ticket, 1) == int(gridDim.x) - 1) {
+      __threadfence_system();
+      *ticket = 0;
+      for (int q = 0; q < p.world; ++q)
+        st_release_sys(rx_flags(p, q, kRxFlagsB) + p.rank, p.epoch);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRxThreads) rx_gather_kernel(RxPeers p, int T, int H,
+                                                               __nv_bfloat16* __restrict__ y) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = rx_wait(p, kRxFlagsB) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  const int h8 = H / 8;
+  const long n = long(T) * h8;
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += long(gridDim.x) * blockDim.x) {
+    const int t = int(i / h8);
+    // owner of token t: the rank r with r*T/N <= t < (r+1)*T/N
+    int r = int((long(t) * p.world + p.world - 1) / T);
+    while (r > 0 && long(r) * T / p.world > t) --r;
+    while (r + 1 < p.world && long(r + 1) * T / p.world <= t) ++r;
+    const size_t off = size_t(i) * 8;
+    *reinterpret_cast<uint4*>(y + off) = *reinterpret_cast<const uint4*>(rx_rows(p, r) + off);
+  }
+}
+
+size_t rx_buffer_bytes(int T_max, int H) {
+  return kRxHeader + 2 * ((size_t(T_max) * H * 2 + 255) / 256 * 256);
+}
+
+size_t rx_status_offset() { return kRxStatus; }
+
+size_t rx_region_offset(int T_max, int H, int epoch) {
+  return kRxHeader + size_t(epoch & 1) * ((size_t(T_max) * H * 2 + 255) / 256 * 256);
+}
+
+cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                  int T, int H, __nv_bfloat16* y, int num_sms, cudaStream_t st) {
+  RxPeers p{};
+  for (int q = 0; q < world; ++q) p.base[q] = static_cast<char*>(bufs[q]);
+  p.world = world;
+  p.rank = rank;
+  p.epoch = epoch;
+  p.region = (size_t(T_max) * H * 2 + 255) / 256 * 256;
+  rx_publish_kernel<<<1, 1, 0, st>>>(p);
+  rx_reduce_kernel<<<num_sms * 2, kRxThreads, 0, st>>>(p, T, H);
+  rx_gather_kernel<<<num_sms * 4, kRxThreads, 0, st>>>(p, T, H, y);
+  return cudaGetLastError();
+}
+
+}  // namespace pmoe

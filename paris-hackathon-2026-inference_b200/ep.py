@@ -74,7 +74,7 @@ class EPGroup:
     """One rank's state for expert-parallel MoE calls.
 
     ``mode`` is "fused" (T <= t_max: NVLink exchange inside the kernels;
-    beyond: sliced routing + row-split expert GEMMs + NCCL all_reduce) or
+    beyond: sliced routing + row-split expert GEMMs + NVLink all-reduce) or
     "nccl" (contiguous expert ranges, replicated routing, partials summed with
     all_reduce: the reference's ep_forward, the comparator)."""
 
@@ -90,6 +90,9 @@ class EPGroup:
         self.lib = _lib.load()
         self.local_buf = None
         self.peer_ptrs = None
+        self.rx_local = None    # row-split partial buffers (prefill), allocated on first use
+        self.rx_tmax = 0
+        self.rx_epoch = 0
         if mode == "fused" and self.world > 1:
             nbytes = ctypes.c_size_t(0)
             _lib.check("pmoe_ep_buffer_bytes",
@@ -158,8 +161,8 @@ class EPGroup:
         its record of one packed buffer ([idx chunk*K | w chunk*K | gate chunk]
         per rank, 4-byte words), one NCCL all_gather shares the records, every
         rank computes its share of the dispatched rows
-        (pmoe_block_forward_rows) and the partials are summed with an NCCL
-        all_reduce."""
+        (pmoe_block_forward_rows) into its NVLink exchange buffer, and
+        pmoe_rows_allreduce sums the partials (deterministic, fp32) into y."""
         T, H = x.shape
         K, world, rank = self.K, self.world, self.rank
         chunk = (T + world - 1) // world
@@ -179,11 +182,57 @@ class EPGroup:
         idx = buf[:, :chunk * K].reshape(world * chunk, K)[:T].contiguous()
         wts = buf[:, chunk * K:2 * chunk * K].reshape(world * chunk, K)[:T].contiguous()
         gate = buf[:, 2 * chunk * K:].reshape(world * chunk)[:T].contiguous()
+        # this rank's partial goes straight into its exchange buffer, then the
+        # NVLink all-reduce (pmoe_rows_allreduce) writes the sum into y
+        self._rows_buffers(T)
+        self.rx_epoch += 1
+        part = ctypes.c_void_p()
+        _lib.check("pmoe_rows_partial", self.lib.pmoe_rows_partial(
+            self.rx_local, self.rx_tmax, H, self.rx_epoch, ctypes.byref(part)))
         _lib.check("pmoe_block_forward_rows", self.lib.pmoe_block_forward_rows(
             x.data_ptr(), T, H, self.E, K, I, Is, *wp, idx.data_ptr(), wts.data_ptr(),
-            gate.data_ptr(), rank, world, flags, y.data_ptr(), ws.data_ptr(), nbytes, st))
-        dist.all_reduce(y, group=self.group)
+            gate.data_ptr(), rank, world, flags, part.value, ws.data_ptr(), nbytes, st))
+        _lib.check("pmoe_rows_allreduce", self.lib.pmoe_rows_allreduce(
+            self.rx_arr, self.rx_tmax, T, H, rank, world, self.rx_epoch, y.data_ptr(), st))
         return y
+
+    def _rows_buffers(self, T: int):
+        """(Re)allocate the IPC-mapped partial buffers for batches of T tokens
+        (collective: every rank calls forward with the same T)."""
+        if self.rx_local is not None and T <= self.rx_tmax:
+            return
+        self._close_rows()
+        nb = ctypes.c_size_t(0)
+        _lib.check("pmoe_rows_buffer_bytes",
+                   self.lib.pmoe_rows_buffer_bytes(T, self.H, ctypes.byref(nb)))
+        ptr = ctypes.c_void_p()
+        _lib.check("pmoe_ipc_alloc", self.lib.pmoe_ipc_alloc(nb.value, ctypes.byref(ptr)))
+        self.rx_local, self.rx_tmax, self.rx_epoch = ptr.value, T, 0
+        h = ctypes.create_string_buffer(64)
+        _lib.check("pmoe_ipc_handle", self.lib.pmoe_ipc_handle(self.rx_local, h))
+        ptrs = []
+        for r, hr in enumerate(exchange_handles(h.raw, self.group)):
+            if r == self.rank:
+                ptrs.append(self.rx_local)
+                continue
+            p = ctypes.c_void_p()
+            _lib.check("pmoe_ipc_open", self.lib.pmoe_ipc_open(hr, ctypes.byref(p)))
+            ptrs.append(p.value)
+        self.rx_ptrs = ptrs
+        self.rx_arr = (ctypes.c_void_p * self.world)(*ptrs)
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+
+    def _close_rows(self):
+        if self.rx_local is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        for r, p in enumerate(self.rx_ptrs):
+            if r != self.rank:
+                self.lib.pmoe_ipc_close(p)
+        self.lib.pmoe_ipc_free(self.rx_local)
+        self.rx_local = None
 
     def layer_forward(self, x: torch.Tensor, w_norm: torch.Tensor, eps: float, weights,
                       flags: int = 3, out: torch.Tensor | None = None,
@@ -214,6 +263,7 @@ class EPGroup:
         return y
 
     def close(self):
+        self._close_rows()
         if self.peer_ptrs is not None:
             torch.cuda.synchronize()
             for r, p in enumerate(self.peer_ptrs):
