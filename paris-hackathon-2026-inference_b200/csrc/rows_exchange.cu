@@ -74,9 +74,14 @@ __global__ void __launch_bounds__(kRxThreads) rx_reduce_kernel(RxPeers p, int T,
        i += long(gridDim.x) * blockDim.x) {
     const size_t off = size_t(t0) * H + size_t(i) * 8;  // row-major: slice rows are contiguous
     float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < p.world; ++q) {  // fixed order: deterministic
-      const uint4 v = *reinterpret_cast<const uint4*>(rx_rows(p, q) + off);
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+    uint4 v[kMaxRanks];  // all ranks' loads in flight at once
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (q < p.world) v[q] = *reinterpret_cast<const uint4*>(rx_rows(p, q) + off);
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {  // fixed order: deterministic
+      if (q >= p.world) break;
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v[q]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(b[j]);
@@ -115,15 +120,28 @@ __global__ void __launch_bounds__(kRxThreads) rx_gather_kernel(RxPeers p, int T,
   if (!s_ok) return;
   const int h8 = H / 8;
   const long n = long(T) * h8;
-  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += long(gridDim.x) * blockDim.x) {
-    const int t = int(i / h8);
-    // owner of token t: the rank r with r*T/N <= t < (r+1)*T/N
-    int r = int((long(t) * p.world + p.world - 1) / T);
+  const long stride = long(gridDim.x) * blockDim.x;
+  // owner of token t: the rank r with r*T/N <= t < (r+1)*T/N
+  auto owner = [&](int t) {
+    int r = int(long(t) * p.world / T);
     while (r > 0 && long(r) * T / p.world > t) --r;
     while (r + 1 < p.world && long(r + 1) * T / p.world <= t) ++r;
-    const size_t off = size_t(i) * 8;
-    *reinterpret_cast<uint4*>(y + off) = *reinterpret_cast<const uint4*>(rx_rows(p, r) + off);
+    return r;
+  };
+  // four independent copies per thread per iteration (peer loads in flight)
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long j = i + u * stride;
+      if (j < n)
+        v[u] = *reinterpret_cast<const uint4*>(rx_rows(p, owner(int(j / h8))) + size_t(j) * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long j = i + u * stride;
+      if (j < n) *reinterpret_cast<uint4*>(y + size_t(j) * 8) = v[u];
+    }
   }
 }
 

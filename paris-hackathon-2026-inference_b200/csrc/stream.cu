@@ -45,7 +45,7 @@ constexpr int kActRows = 32;                    // dispatched rows per pass
 constexpr int kActChunkBytes = kActRows * kKC * 2;  // 4 KiB activation chunk
 constexpr int kRingBudget = 200 * 1024;
 constexpr int kUnitSlots = 4;
-constexpr int kDnRowBlocks = 4;  // down unit = 4 x 64 output rows (amortises unit set-up)
+constexpr int kDnRowBlocks = 8;  // default down unit = 8 x 64 output rows (4: 99.9 us, 8: 98.4, 16: 117.8)
 
 template <int KCH>
 struct GuCfg {
@@ -286,7 +286,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
     const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h8,
     ExpertTables tb, int H, int E, int I, int Is,
-    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep) {
+    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep,
+    int row_blocks) {
   using C = DnCfg<KCH>;
   const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
   constexpr int kStages = C::kStages;
@@ -305,7 +306,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     mbar_fence_init();
   }
   __syncthreads();
-  const int UR = H / (kUnitRows * kDnRowBlocks);
+  const int UR = H / (kUnitRows * row_blocks);
   const int n_units = tb.n_active[0] * UR;
 
   if (warp == 0) {
@@ -334,8 +335,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
       const int p0 = tb.offsets[e];
       const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
-      for (int sub = 0; sub < kDnRowBlocks; ++sub) {
-      const int rb = rbg * kDnRowBlocks + sub;
+      for (int sub = 0; sub < row_blocks; ++sub) {
+      const int rb = rbg * row_blocks + sub;
       const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
       for (int nb = 0; nb < n; nb += kActRows) {
         // passes of at most 8 rows load an 8-row activation box (1 KiB/chunk)
@@ -380,8 +381,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     const int nkc = (sh ? Is : I) / (kKC * KCH);
     const int p0 = tb.offsets[e];
     const int n = tb.offsets[e + 1] - p0;
-    for (int sub = 0; sub < kDnRowBlocks; ++sub) {
-    const int rb = rbg * kDnRowBlocks + sub;
+    for (int sub = 0; sub < row_blocks; ++sub) {
+    const int rb = rbg * row_blocks + sub;
     for (int nb = 0; nb < n; nb += kActRows) {
       const int ng = min(4, (n - nb + 7) / 8);
       float acc[4][4] = {};
@@ -531,6 +532,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
 namespace {
 int g_num_sms = 148;
 int g_kch_gu = 4;  // k-chunks per gate_up stage (512 B per weight row)
+int g_dn_row_blocks = kDnRowBlocks;
 int g_kch_dn = 8;  // k-chunks per down stage (two 96 KiB stages: measured 101 vs 106 us at 4)
 
 template <int KCH>
@@ -562,6 +564,10 @@ cudaError_t stream_init(int num_sms) {
   g_num_sms = num_sms;
   g_kch_gu = env_kch("PMOE_STREAM_KCH_GU", g_kch_gu);
   g_kch_dn = env_kch("PMOE_STREAM_KCH_DN", g_kch_dn);
+  if (const char* v = std::getenv("PMOE_DN_ROWBLOCKS")) {
+    const int r = std::atoi(v);
+    if (r == 1 || r == 2 || r == 4 || r == 8 || r == 16) g_dn_row_blocks = r;
+  }
   cudaError_t e = set_attrs<1>();
   if (e == cudaSuccess) e = set_attrs<2>();
   if (e == cudaSuccess) e = set_attrs<4>();
@@ -579,6 +585,8 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
   float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
   const int kg = fit_kch(g_kch_gu, d.H, d.H);
   const int kd = fit_kch(g_kch_dn, d.I, d.Is);
+  int rbk = g_dn_row_blocks;  // 64-row blocks per down unit, dividing H / 64
+  while (rbk > 1 && (d.H / kUnitRows) % rbk != 0) rbk >>= 1;
   CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_x, tm_h, tm_h8;
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t R = T * d.K + T, ldh = d.ldh;
@@ -598,7 +606,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
 #define PMOE_DN(KCH)                                                                  \
   down_tma_kernel<KCH><<<g_num_sms, kStreamThreads, DnCfg<KCH>::kSmem, st>>>(         \
-      tm_dn, tm_sd, tm_h, tm_h8, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep)
+      tm_dn, tm_sd, tm_h, tm_h8, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep, rbk)
   if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
