@@ -45,7 +45,7 @@ constexpr int kActRows = 32;                    // dispatched rows per pass
 constexpr int kActChunkBytes = kActRows * kKC * 2;  // 4 KiB activation chunk
 constexpr int kRingBudget = 200 * 1024;
 constexpr int kUnitSlots = 4;
-constexpr int kDnRowBlocks = 8;  // default down unit = 8 x 64 output rows (4: 99.9 us, 8: 98.4, 16: 117.8)
+constexpr int kDnRowBlocks = 8;  // down unit = 8 x 64 output rows (4: 99.9 us, 8: 98.4, 16: 117.8)
 
 template <int KCH>
 struct GuCfg {
@@ -468,6 +468,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
 // (world > 0) the rows are this call's parity copy of the exchange buffer and
 // every block first waits, bounded, until all ranks' completion flags for
 // this epoch are up.
+constexpr int kCombMaxK = 8;  // top-k sizes up to this take the all-loads-in-flight path
+
 __global__ void __launch_bounds__(256) combine_kernel(
     const float* __restrict__ rows, size_t par_stride, const int32_t* __restrict__ topk_idx,
     int T, int H, int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
@@ -500,17 +502,44 @@ __global__ void __launch_bounds__(256) combine_kernel(
   if (i >= long(T) * cols4) return;
   const int t = int(i / cols4), c4 = int(i % cols4);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (with_routed) {
-    for (int k = 0; k < K; ++k) {
-      const int e = topk_idx[size_t(t) * K + k];
-      if (e < lo || e >= hi) continue;
-      const float4 v = reinterpret_cast<const float4*>(rows + (size_t(t) * K + k) * H)[c4];
+  const bool sh_sel = with_shared && t >= sh_lo && t < sh_hi;
+  if (K <= kCombMaxK) {
+    // select, then issue all selected row loads before the fixed-order sum
+    bool sel[kCombMaxK];
+    float4 v[kCombMaxK + 1];
+#pragma unroll
+    for (int k = 0; k < kCombMaxK; ++k) {
+      sel[k] = false;
+      if (k < K && with_routed) {
+        const int e = topk_idx[size_t(t) * K + k];
+        sel[k] = e >= lo && e < hi;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kCombMaxK; ++k)
+      if (sel[k]) v[k] = reinterpret_cast<const float4*>(rows + (size_t(t) * K + k) * H)[c4];
+    if (sh_sel) v[kCombMaxK] = reinterpret_cast<const float4*>(rows + (size_t(T) * K + t) * H)[c4];
+#pragma unroll
+    for (int k = 0; k < kCombMaxK; ++k)
+      if (sel[k]) {
+        s.x += v[k].x; s.y += v[k].y; s.z += v[k].z; s.w += v[k].w;
+      }
+    if (sh_sel) {
+      s.x += v[kCombMaxK].x; s.y += v[kCombMaxK].y; s.z += v[kCombMaxK].z; s.w += v[kCombMaxK].w;
+    }
+  } else {
+    if (with_routed) {
+      for (int k = 0; k < K; ++k) {
+        const int e = topk_idx[size_t(t) * K + k];
+        if (e < lo || e >= hi) continue;
+        const float4 v = reinterpret_cast<const float4*>(rows + (size_t(t) * K + k) * H)[c4];
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      }
+    }
+    if (sh_sel) {
+      const float4 v = reinterpret_cast<const float4*>(rows + (size_t(T) * K + t) * H)[c4];
       s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
     }
-  }
-  if (with_shared && t >= sh_lo && t < sh_hi) {
-    const float4 v = reinterpret_cast<const float4*>(rows + (size_t(T) * K + t) * H)[c4];
-    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
   }
   if (resid) {
     const uint2 rb = reinterpret_cast<const uint2*>(resid + size_t(t) * H)[c4];

@@ -505,6 +505,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
 // over the bf16 expert rows the down GEMM wrote (routing weights w, shared
 // gate g), in fp32 in a fixed order (the shared row for tokens in
 // [sh_lo, sh_hi)).  One thread per 8 columns.
+constexpr int kCombineMaxK = 8;  // top-k sizes up to this take the all-loads-in-flight path
+
 __global__ void __launch_bounds__(256) combine_rows_kernel(
     const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ topk_idx,
     const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
@@ -533,15 +535,52 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
     const int p = pair_pos[q];
     return p >= p_lo && p < p_hi;
   };
-  if (with_routed) {
-    for (int k = 0; k < K; ++k) {
-      const size_t q = size_t(t) * K + k;
-      const int e = topk_idx[q];
-      if (e >= lo && e < hi && mine(q)) add(q, topk_w[q]);
+  if (K <= kCombineMaxK) {
+    // Select first, then issue every selected row's load before summing, so
+    // the (up to) 9 row reads are in flight together.
+    bool sel[kCombineMaxK + 1];
+    float w[kCombineMaxK + 1];
+    size_t q[kCombineMaxK + 1];
+#pragma unroll
+    for (int k = 0; k < kCombineMaxK; ++k) {
+      q[k] = size_t(t) * K + k;
+      sel[k] = false;
+      w[k] = 0.f;
+      if (k < K && with_routed) {
+        const int e = topk_idx[q[k]];
+        sel[k] = e >= lo && e < hi && mine(q[k]);
+        if (sel[k]) w[k] = topk_w[q[k]];
+      }
     }
+    q[kCombineMaxK] = size_t(T) * K + t;
+    sel[kCombineMaxK] = with_shared && t >= sh_lo && t < sh_hi && mine(q[kCombineMaxK]);
+    w[kCombineMaxK] = sel[kCombineMaxK] ? shared_gate[t] : 0.f;
+    uint4 v[kCombineMaxK + 1];
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxK; ++k)
+      if (sel[k]) v[k] = __ldg(reinterpret_cast<const uint4*>(rows + q[k] * H) + c8);
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxK; ++k) {
+      if (!sel[k]) continue;
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        s[2 * j] = fmaf(w[k], f.x, s[2 * j]);
+        s[2 * j + 1] = fmaf(w[k], f.y, s[2 * j + 1]);
+      }
+    }
+  } else {
+    if (with_routed) {
+      for (int k = 0; k < K; ++k) {
+        const size_t qk = size_t(t) * K + k;
+        const int e = topk_idx[qk];
+        if (e >= lo && e < hi && mine(qk)) add(qk, topk_w[qk]);
+      }
+    }
+    if (with_shared && t >= sh_lo && t < sh_hi && mine(size_t(T) * K + t))
+      add(size_t(T) * K + t, shared_gate[t]);
   }
-  if (with_shared && t >= sh_lo && t < sh_hi && mine(size_t(T) * K + t))
-    add(size_t(T) * K + t, shared_gate[t]);
   if (resid) {  // decoder layer: y = bf16(resid + bf16(sum)), as residual + mlp(x) in bf16
     const uint4 rv = reinterpret_cast<const uint4*>(resid + size_t(t) * H)[c8];
     const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
