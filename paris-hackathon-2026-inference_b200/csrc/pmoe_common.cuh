@@ -49,7 +49,7 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 struct Dims {
   int T, H, E, K, I, Is;
   int Rpad;   // router rows (E experts + shared gate) padded to 16
-  int KS;     // router split-K factor (1)
+  int KS;     // decode router split-K factor (CTAs per logit tile)
   int ldh;    // row stride of h
   int sh_lo, sh_hi;  // token range this call computes the shared expert for
 };
@@ -99,7 +99,7 @@ constexpr int kFusedRouteMaxT = 64;
 inline Dims make_dims(int T, int H, int E, int K, int I, int Is) {
   Dims d{T, H, E, K, I, Is, 0, 0, 0, 0, T};
   d.Rpad = ((E + 1) + 15) / 16 * 16;
-  d.KS = 1;
+  d.KS = (T <= kFusedRouteMaxT && H % (4 * 32) == 0) ? 4 : 1;
   d.ldh = I > Is ? I : Is;
   return d;
 }

@@ -6,10 +6,12 @@
 //
 // Two paths:
 //  * T <= kFusedRouteMaxT (decode): ONE launch.  Each CTA computes a
-//    16-expert x 32-token tile of bf16 logits with its K dimension split
-//    over 8 warps and reduced in shared memory in a fixed order; the last
-//    CTA to finish (threadfence + atomic ticket) does top-k, the histogram,
-//    the CSR offsets and the stable permutation for all tokens.
+//    16-expert x 32-token tile of partial logits over one of KS K-ranges,
+//    split over its 16 warps and reduced in shared memory in a fixed order;
+//    the last CTA of each 32-token group (threadfence + atomic ticket) sums
+//    the KS partials in a fixed order, rounds to bf16 and selects the
+//    group's top-k; the last group does the histogram, the CSR offsets and
+//    the stable permutation for all tokens.
 //  * larger T: router GEMM tiles -> warp-per-token top-k -> one-CTA dispatch.
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
@@ -300,14 +302,14 @@ __device__ void block_dispatch(const int* cnt_src, const int32_t* __restrict__ t
 
 // ---------------------------------------------------------------------------
 // Fused decode routing (T <= kFusedRouteMaxT), grid = (Rpad/16) * ceil(T/32)
-// CTAs of 512 threads; the K dimension of each CTA's 16 x 32 logit tile is
-// split over its 16 warps and reduced in shared memory in a fixed order.
-// The last CTA (ticket in sync[0], which the launcher clears with a memset
-// node and the last CTA resets) stages all logits into shared memory with
-// one coherent bulk read, then runs top-k and the dispatch out of shared
-// memory, so its serial tail sees no global-memory latency.
+// * KS CTAs of 512 threads (KS K-ranges per logit tile: 136 CTAs at T=64, so
+// each warp's loads are one 32-column step).  Tickets in sync[4 + group] and
+// sync[0] (cleared by the launcher's memset and by the winners) pick the
+// last CTA of each 32-token group for the top-k and the last group for the
+// dispatch, so the serial tail runs on two CTAs and then one.
 // ---------------------------------------------------------------------------
 constexpr int kFusedRouteThreads = 512;
+constexpr int kMaxRouteKS = 4;  // split-K factor of the decode router (Dims::KS)
 constexpr int kFusedRouteWarps = kFusedRouteThreads / 32;
 
 size_t fused_route_smem_bytes(int T, int E, int K, int Rpad) {
@@ -318,27 +320,29 @@ size_t fused_route_smem_bytes(int T, int E, int K, int Rpad) {
 
 __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_router,
-    const __nv_bfloat16* __restrict__ w_gvec, int T, int H, int E, int K, int Rpad, int lo,
-    int hi, int with_shared, int with_routed, float* __restrict__ logits,
+    const __nv_bfloat16* __restrict__ w_gvec, int T, int H, int E, int K, int Rpad, int KS,
+    int lo, int hi, int with_shared, int with_routed, float* __restrict__ logit_part,
     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
     DispatchOut o, int32_t* __restrict__ sync) {
   __shared__ float s_part[kFusedRouteWarps][32][17];
   __shared__ int s_cnt[256], s_off[256], s_cur[256], s_wsum[32], s_tot[2], s_last;
   extern __shared__ float s_dyn[];
-  float* s_lg = s_dyn;                                       // [T][Rpad]
+  float* s_lg = s_dyn;                                       // [32][Rpad] (one token group)
   int* s_idx = reinterpret_cast<int*>(s_lg + size_t(T) * Rpad);  // [T*K]
   float* s_w = reinterpret_cast<float*>(s_idx + T * K);      // [T*K]
   float* s_sg = s_w + T * K;                                  // [T]
   int* s_wcnt = reinterpret_cast<int*>(s_sg + T);             // [warps][E]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const int RG = Rpad / 16;
-  const int rg = blockIdx.x % RG, tt = blockIdx.x / RG;
-  // K slices are whole 32-column steps; with small H the trailing warps get
-  // an empty slice and contribute zeros.
-  const int slice = (H / kFusedRouteWarps + 31) / 32 * 32;
-  const int k_begin = min(H, warp * slice);
+  const int RG = Rpad / 16, TT = (T + 31) / 32;
+  const int kg = blockIdx.x % KS, rest = blockIdx.x / KS;
+  const int rg = rest % RG, tt = rest / RG;
+  // This CTA's K range [kb, kb + Hk), split over the warps in whole 32-column
+  // steps; with small H the trailing warps get an empty slice.
+  const int Hk = H / KS, kb = kg * Hk;
+  const int slice = (Hk / kFusedRouteWarps + 31) / 32 * 32;
+  const int k_off = min(Hk, warp * slice);
   float acc[4][4];
-  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, k_begin, min(slice, H - k_begin), acc);
+  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, kb + k_off, min(slice, Hk - k_off), acc);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     s_part[warp][q * 8 + 2 * c][g] = acc[q][0];
@@ -347,6 +351,7 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     s_part[warp][q * 8 + 2 * c + 1][g + 8] = acc[q][3];
   }
   __syncthreads();
+  float* part = logit_part + size_t(kg) * T * Rpad;
   for (int i = tid; i < 32 * 16; i += kFusedRouteThreads) {
     const int tl = i >> 4, rl = i & 15;
     const int t = tt * 32 + tl, r = rg * 16 + rl;
@@ -354,31 +359,66 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < kFusedRouteWarps; ++w) s += s_part[w][tl][rl];
-      logits[size_t(t) * Rpad + r] = r < E ? bf16_round(s) : s;
+      part[size_t(t) * Rpad + r] = s;
     }
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(&sync[0], 1) == int(gridDim.x) - 1);
+  // Level 1: the last CTA of this 32-token group sums the KS partials in a
+  // fixed order, rounds the logits to bf16 and selects the group's top-k.
+  if (tid == 0) s_last = (atomicAdd(&sync[4 + tt], 1) == RG * KS - 1);
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // Rpad is a multiple of 16, so the [T][Rpad] block is a whole number of float4.
-  const float4* src = reinterpret_cast<const float4*>(logits);
-  float4* dst = reinterpret_cast<float4*>(s_lg);
-  for (int i = tid; i < T * Rpad / 4; i += kFusedRouteThreads) dst[i] = __ldcg(src + i);
-  for (int e = tid; e < E; e += kFusedRouteThreads) s_cnt[e] = 0;
+  const int t0 = tt * 32, nt = min(32, T - t0);
+  // Rpad is a multiple of 16: whole float4s; all KS partial loads in flight.
+  for (int i = tid; i < nt * Rpad / 4; i += kFusedRouteThreads) {
+    const size_t gi = size_t(t0) * Rpad / 4 + i;
+    float4 v[kMaxRouteKS];
+#pragma unroll
+    for (int k = 0; k < kMaxRouteKS; ++k)
+      if (k < KS)
+        v[k] = __ldcg(reinterpret_cast<const float4*>(logit_part + size_t(k) * T * Rpad) + gi);
+    float4 sum = v[0];
+#pragma unroll
+    for (int k = 1; k < kMaxRouteKS; ++k)
+      if (k < KS) {
+        sum.x += v[k].x; sum.y += v[k].y; sum.z += v[k].z; sum.w += v[k].w;
+      }
+    const int r = (4 * i) % Rpad;  // the 4 logits are experts r .. r+3 of one token
+    sum.x = r < E ? bf16_round(sum.x) : sum.x;
+    sum.y = r + 1 < E ? bf16_round(sum.y) : sum.y;
+    sum.z = r + 2 < E ? bf16_round(sum.z) : sum.z;
+    sum.w = r + 3 < E ? bf16_round(sum.w) : sum.w;
+    reinterpret_cast<float4*>(s_lg)[i] = sum;
+  }
+  for (int e = tid; e < 256; e += kFusedRouteThreads) s_cnt[e] = 0;
   __syncthreads();
-  static_assert(kFusedRouteMaxT <= 4 * kFusedRouteWarps, "4 tokens per warp");
-  warp_topk_multi<4>(s_lg, Rpad, warp, kFusedRouteWarps, T, E, K, s_idx, s_w, s_sg, s_cnt);
+  static_assert(32 <= 2 * kFusedRouteWarps, "2 tokens per warp");
+  warp_topk_multi<2>(s_lg, Rpad, warp, kFusedRouteWarps, nt, E, K, topk_idx + size_t(t0) * K,
+                     topk_w + size_t(t0) * K, shared_gate + t0, s_cnt);
+  __threadfence();
+  __syncthreads();
+  // Level 2: the last group to finish builds the dispatch for all tokens.
+  if (tid == 0) {
+    sync[4 + tt] = 0;
+    s_last = (atomicAdd(&sync[0], 1) == TT - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = tid; e < 256; e += kFusedRouteThreads) s_cnt[e] = 0;
+  __syncthreads();
+  for (int p = tid; p < T * K; p += kFusedRouteThreads) {
+    const int e = __ldcg(topk_idx + p);
+    s_idx[p] = e;
+    s_w[p] = __ldcg(topk_w + p);
+    atomicAdd(&s_cnt[e], 1);
+  }
+  for (int t = tid; t < T; t += kFusedRouteThreads) s_sg[t] = __ldcg(shared_gate + t);
   __syncthreads();
   block_dispatch(s_cnt, s_idx, s_w, s_sg, T, E, K, lo, hi, with_shared, with_routed, o, s_off,
                  s_cur, s_wsum, s_tot, s_wcnt);
-  for (int i = tid; i < T * K; i += kFusedRouteThreads) {
-    topk_idx[i] = s_idx[i];
-    topk_w[i] = s_w[i];
-  }
-  for (int t = tid; t < T; t += kFusedRouteThreads) shared_gate[t] = s_sg[t];
   if (tid == 0) sync[0] = 0;
 }
 
@@ -452,10 +492,10 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
   cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
   if (d.T <= kFusedRouteMaxT) {
-    route_fused_kernel<<<RG * TT, kFusedRouteThreads,
+    route_fused_kernel<<<RG * TT * d.KS, kFusedRouteThreads,
                          fused_route_smem_bytes(d.T, d.E, d.K, d.Rpad), st>>>(
-        x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, lo, hi, with_shared, with_routed,
-        ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status);
+        x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, d.KS, lo, hi, with_shared,
+        with_routed, ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status);
     return cudaGetLastError();
   }
   const long items = long(RG) * TT;
