@@ -28,10 +28,13 @@ from HBM; no L2 flush is needed) and hidden states are synthetic N(0,1).
 
 ``--impl reference`` times that CPU path alone, on rank 0 (other ranks exit).
 Multi-GPU (N>1, one process per GPU under torch.distributed.run): expert
-parallel, experts split in contiguous ranges by rank (engine/runtime/ep.py:78-86),
-strong scaling over the same tokens.  Decode exchanges the weighted expert
-rows over NVLink from the down-projection epilogue (no collective kernel);
-prefill sums per-rank partials with NCCL all_reduce.
+parallel, strong scaling over the same tokens.  Decode: contiguous expert
+ranges by rank (engine/runtime/ep.py:78-86), the weighted expert rows cross
+NVLink from the down-projection epilogue (no collective kernel).  Prefill:
+sliced routing + one all_gather, a row-balanced share of the dispatched rows
+per rank, partials summed over NVLink.  ``comparators`` (decode and prefill)
+times the same call with the reference's NCCL all_reduce exchange and with a
+token-dispatch all_to_all_single exchange.
 """
 from __future__ import annotations
 
@@ -315,6 +318,34 @@ class Ctx:
         return float(t.item())
 
 
+def comparators(c, x, tensors, T, steps, warmup):
+    """N > 1: the same call through the two comparator exchanges -- contiguous
+    expert ranges + NCCL all_reduce (the reference's ep_forward) and token
+    dispatch with all_to_all_single -- tokens/s, device-timed, max over ranks."""
+    import torch
+    from paris_moe_b200 import ep
+    out = {}
+    for mode, label in (("nccl", "nccl_all_reduce"), ("a2a", "all_to_all")):
+        g = ep.EPGroup(c.S.E, c.S.H, c.S.K, mode=mode)
+        y = torch.empty_like(x)
+        for _ in range(warmup):
+            g.forward(x, tensors, out=y)
+        torch.cuda.synchronize()
+        c.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(c.st)
+        for _ in range(steps):
+            g.forward(x, tensors, out=y)
+        t1.record(c.st)
+        torch.cuda.synchronize()
+        c.barrier()
+        ms = c.max_over_ranks(t0.elapsed_time(t1)) / steps
+        out[label] = {"value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+                      "steps": steps}
+        g.close()
+    return out
+
+
 def stack_bench(c, a, peaks, peak_kind):
     """Config 5: the MoE-only decoder stack (RMSNorm + MoE block + residual per
     layer, attention omitted), one decode step of batch ``stack_T`` through all
@@ -456,6 +487,8 @@ def main():
         "clocks": clocks,
     }
     layer_bytes = W.decode_bytes(S, a.T, hit)
+    if c.world > 1:
+        line["comparators"] = comparators(c, x, c.wts.tensors(), a.T, steps=20, warmup=3)
     line["layer_roofline"] = {"bound": "hbm", "algorithmic_bytes": layer_bytes,
                               "experts_hit": hit, "unit": "GB/s",
                               "achieved": layer_bytes / (ms * 1e-3) / 1e9,
@@ -505,6 +538,9 @@ def main():
                                   "tc_pair_gate_up_prefill_T8192"),
                               "algorithmic_flops": gu_flops, "avg_launch_ms": pphase[1],
                               "peak_source": f"{peak_kind} (bf16_tflops, burst)"}
+        if c.world > 1:
+            pl["comparators"] = comparators(c, xp, [wr] + c.wts.tensors()[1:], a.prefill_T,
+                                            steps=5, warmup=2)
         line["prefill"] = pl
 
     # ------------------------------------------------------------- stack --

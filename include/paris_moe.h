@@ -158,7 +158,12 @@ int pmoe_block_forward_ep(const uint16_t* x, int T, int H, int E, int K, int I, 
  *     the R dispatched rows -- one contiguous range, so heavy experts are
  *     split across ranks instead of loading one rank.  y is this rank's
  *     partial, to be summed across ranks by the caller (as ep.py:140 sums the
- *     expert-range partials of engine/runtime/ep.py:97-143).
+ *     expert-range partials of engine/runtime/ep.py:97-143).  expert_lo/hi
+ *     restrict the routed experts computed and summed (0, E: all); with
+ *     world = 1 and an expert range this is the expert side of a
+ *     token-dispatch (all-to-all) exchange.  topk_idx, topk_w and shared_gate
+ *     all NULL: the call routes all T tokens itself (identically on every
+ *     rank) instead of taking the routing.
  * Workspace as pmoe_workspace_size(T, ...). */
 int pmoe_route_slice(const uint16_t* x, int T, int H, int E, int K, int I, int Is, int t0,
                      int t1, const uint16_t* w_router, const uint16_t* w_sh_gvec,
@@ -169,9 +174,9 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
                             const uint16_t* w_down, const uint16_t* w_sh_gate,
                             const uint16_t* w_sh_up, const uint16_t* w_sh_down,
                             const uint16_t* w_sh_gvec, const int32_t* topk_idx,
-                            const float* topk_w, const float* shared_gate, int rank, int world,
-                            int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
-                            void* stream);
+                            const float* topk_w, const float* shared_gate, int expert_lo,
+                            int expert_hi, int rank, int world, int flags, uint16_t* y,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* Sum of the row-split partials over NVLink, in place of the caller's NCCL
  * all_reduce (ep.py:140): each rank owns a buffer of pmoe_rows_buffer_bytes

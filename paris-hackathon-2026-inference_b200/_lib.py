@@ -45,7 +45,7 @@ SIGNATURES = {
     "pmoe_route_slice": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ,
                               _P]),
     "pmoe_block_forward_rows": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
-                                     _P, _P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
+                                     _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "pmoe_read_status": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
     "pmoe_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
     "pmoe_ipc_free": (_I, [_P]),

@@ -174,8 +174,10 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                 ((flags & PMOE_F_FORCE_TC) ||
                  (!(flags & PMOE_F_FORCE_STREAM) && T > kFusedRouteMaxT && tc_supported(d)));
   if (rs) {
-    if (rs->world < 1 || rs->rank < 0 || rs->rank >= rs->world || !rs->topk_idx ||
-        !rs->topk_w || !rs->shared_gate || ep.world > 0 || (flags & PMOE_F_FORCE_STREAM))
+    const bool given = rs->topk_idx || rs->topk_w || rs->shared_gate;
+    if (rs->world < 1 || rs->rank < 0 || rs->rank >= rs->world ||
+        (given && (!rs->topk_idx || !rs->topk_w || !rs->shared_gate)) || ep.world > 0 ||
+        (flags & PMOE_F_FORCE_STREAM))
       return PMOE_ERR_ARG;
     if (!tc_supported(d) || !route_tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
     use_tc = true;
@@ -187,9 +189,13 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
     return cudaSuccess;
   };
   if (mark(0) != cudaSuccess) return PMOE_ERR_CUDA;
-  if (ep.world > 0 && ep.epoch_dev &&
-      launch_epoch_bump(const_cast<int*>(ep.epoch_dev), st) != cudaSuccess)
-    return PMOE_ERR_CUDA;
+  // The exchange's device epoch: bumped by the decode router kernel itself, or
+  // by a one-thread kernel when another routing path runs.
+  int* epoch_bump = ep.world > 0 ? const_cast<int*>(ep.epoch_dev) : nullptr;
+  if (epoch_bump && !route_bumps_epoch(d)) {
+    if (launch_epoch_bump(epoch_bump, st) != cudaSuccess) return PMOE_ERR_CUDA;
+    epoch_bump = nullptr;
+  }
   // The block reads xin; a decoder layer normalises x first and adds it back
   // in the combine (in place, y == x, is allowed: each combine thread reads
   // its residual chunk before writing the same chunk).
@@ -204,12 +210,15 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   // Prefill-sized batches route on the tensor cores.
   const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
   const cudaError_t rerr =
-      rs ? launch_dispatch_given(d, rs->topk_idx, rs->topk_w, rs->shared_gate, expert_lo,
-                                 expert_hi, with_shared, with_routed, ws, st)
+      rs && rs->topk_idx
+          ? launch_dispatch_given(d, rs->topk_idx, rs->topk_w, rs->shared_gate, expert_lo,
+                                  expert_hi, with_shared, with_routed, ws, st)
+      : rs ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
+                             with_shared, with_routed, ws, st)
       : route_tc ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
                                    with_shared, with_routed, ws, st)
                  : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
-                                with_shared, with_routed, ws, st);
+                                with_shared, with_routed, ws, st, epoch_bump);
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
@@ -378,14 +387,14 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
                             const uint16_t* w_down, const uint16_t* w_sh_gate,
                             const uint16_t* w_sh_up, const uint16_t* w_sh_down,
                             const uint16_t* w_sh_gvec, const int32_t* topk_idx,
-                            const float* topk_w, const float* shared_gate, int rank, int world,
-                            int flags, uint16_t* y, void* workspace, size_t workspace_bytes,
-                            void* stream) {
+                            const float* topk_w, const float* shared_gate, int expert_lo,
+                            int expert_hi, int rank, int world, int flags, uint16_t* y,
+                            void* workspace, size_t workspace_bytes, void* stream) {
   const EpPeers none{};
   const RowSplit rs{topk_idx, topk_w, shared_gate, rank, world};
   return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
-                      w_sh_down, w_sh_gvec, 0, E, 0, T, flags, y, workspace, workspace_bytes,
-                      stream, nullptr, 0, none, nullptr, &rs);
+                      w_sh_down, w_sh_gvec, expert_lo, expert_hi, 0, T, flags, y, workspace,
+                      workspace_bytes, stream, nullptr, 0, none, nullptr, &rs);
 }
 
 int pmoe_rows_buffer_bytes(int T_max, int H, size_t* bytes) {

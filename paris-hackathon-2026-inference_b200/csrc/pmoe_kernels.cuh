@@ -7,9 +7,14 @@ namespace pmoe {
 cudaError_t route_init();
 cudaError_t stream_init(int num_sms);
 
+// epoch_bump (may be null): a device counter the routing kernel increments
+// once (the expert-parallel exchange's epoch); false when it could not, i.e.
+// the caller must bump it separately (only the T <= kFusedRouteMaxT path does).
 cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                          const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
-                         int with_routed, const Workspace& ws, cudaStream_t st);
+                         int with_routed, const Workspace& ws, cudaStream_t st,
+                         int* epoch_bump = nullptr);
+bool route_bumps_epoch(const Dims& d);
 
 cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,

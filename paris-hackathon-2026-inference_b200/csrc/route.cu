@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     const __nv_bfloat16* __restrict__ w_gvec, int T, int H, int E, int K, int Rpad, int KS,
     int lo, int hi, int with_shared, int with_routed, float* __restrict__ logit_part,
     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
-    DispatchOut o, int32_t* __restrict__ sync) {
+    DispatchOut o, int32_t* __restrict__ sync, int* __restrict__ epoch_bump) {
   __shared__ float s_part[kFusedRouteWarps][32][17];
   __shared__ int s_cnt[256], s_off[256], s_cur[256], s_wsum[32], s_tot[2], s_last;
   extern __shared__ float s_dyn[];
@@ -334,6 +334,7 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   int* s_wcnt = reinterpret_cast<int*>(s_sg + T);             // [warps][E]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int RG = Rpad / 16, TT = (T + 31) / 32;
+  if (epoch_bump && blockIdx.x == 0 && threadIdx.x == 0) *epoch_bump += 1;
   const int kg = blockIdx.x % KS, rest = blockIdx.x / KS;
   const int rg = rest % RG, tt = rest / RG;
   // This CTA's K range [kb, kb + Hk), split over the warps in whole 32-column
@@ -485,7 +486,8 @@ size_t dispatch_smem_bytes(int E) {
 
 cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                          const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
-                         int with_routed, const Workspace& ws, cudaStream_t st) {
+                         int with_routed, const Workspace& ws, cudaStream_t st,
+                         int* epoch_bump) {
   DispatchOut o{ws.offsets, ws.active, ws.n_active, ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
                 ws.pair_w, d.sh_lo, d.sh_hi};
   const int RG = d.Rpad / 16, TT = (d.T + 31) / 32;
@@ -495,7 +497,8 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
     route_fused_kernel<<<RG * TT * d.KS, kFusedRouteThreads,
                          fused_route_smem_bytes(d.T, d.E, d.K, d.Rpad), st>>>(
         x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, d.KS, lo, hi, with_shared,
-        with_routed, ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status);
+        with_routed, ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status,
+        epoch_bump);
     return cudaGetLastError();
   }
   const long items = long(RG) * TT;
@@ -508,6 +511,8 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
       with_routed, o);
   return cudaGetLastError();
 }
+
+bool route_bumps_epoch(const Dims& d) { return d.T <= kFusedRouteMaxT; }
 
 cudaError_t route_init() {
   cudaError_t e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

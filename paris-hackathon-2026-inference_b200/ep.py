@@ -63,6 +63,27 @@ def token_range(num_tokens: int, rank: int, world_size: int):
     return rank * num_tokens // world_size, (rank + 1) * num_tokens // world_size
 
 
+def expert_owner(idx: torch.Tensor, num_experts: int, world_size: int) -> torch.Tensor:
+    """Rank owning each expert id under the contiguous ranges of expert_range."""
+    bounds = torch.tensor([r * num_experts // world_size for r in range(world_size)],
+                          dtype=torch.long, device=idx.device)
+    return torch.searchsorted(bounds, idx.long(), right=True) - 1
+
+
+def a2a_plan(idx: torch.Tensor, num_experts: int, world_size: int):
+    """Token-dispatch send plan for local tokens routed as ``idx`` [Tl, K]: each
+    token goes once to every rank owning at least one of its experts.  Returns
+    (send_tok [S] local token ids grouped by destination rank ascending,
+    counts [world] tokens per destination rank)."""
+    owners = expert_owner(idx, num_experts, world_size)            # [Tl, K]
+    hit = torch.zeros((idx.shape[0], world_size), dtype=torch.bool, device=idx.device)
+    hit.scatter_(1, owners, True)
+    toks = [torch.nonzero(hit[:, r], as_tuple=False).flatten() for r in range(world_size)]
+    counts = torch.tensor([t.numel() for t in toks], dtype=torch.long)
+    send = torch.cat(toks) if toks else torch.empty(0, dtype=torch.long, device=idx.device)
+    return send, counts
+
+
 def exchange_handles(local: bytes, group=None) -> list[bytes]:
     """All ranks' 64-byte IPC handles, indexed by rank (host collective)."""
     out: list = [None] * dist.get_world_size(group)
@@ -74,9 +95,10 @@ class EPGroup:
     """One rank's state for expert-parallel MoE calls.
 
     ``mode`` is "fused" (T <= t_max: NVLink exchange inside the kernels;
-    beyond: sliced routing + row-split expert GEMMs + NVLink all-reduce) or
+    beyond: row-split expert GEMMs + NVLink all-reduce) or
     "nccl" (contiguous expert ranges, replicated routing, partials summed with
-    all_reduce: the reference's ep_forward, the comparator)."""
+    all_reduce: the reference's ep_forward, the comparator) or "a2a" (token
+    dispatch with all_to_all_single: the second comparator)."""
 
     def __init__(self, num_experts: int, hidden: int, top_k: int, mode: str = "fused",
                  t_max: int = FUSED_MAX_T, group=None):
@@ -148,6 +170,8 @@ class EPGroup:
             return y
         if self.mode == "fused" and self.world > 1:
             return self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st)
+        if self.mode == "a2a" and self.world > 1:
+            return self._forward_a2a(x, w, I, Is, y)
         s = self.lib.pmoe_block_forward_ep(
             x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
             None, 0, self.rank, self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)
@@ -157,43 +181,73 @@ class EPGroup:
         return y
 
     def _forward_rows(self, x, wp, I, Is, flags, y, ws, nbytes, st):
-        """Prefill-sized batches: each rank routes its slice of the tokens into
-        its record of one packed buffer ([idx chunk*K | w chunk*K | gate chunk]
-        per rank, 4-byte words), one NCCL all_gather shares the records, every
-        rank computes its share of the dispatched rows
+        """Prefill-sized batches: every rank routes all tokens (the same kernel,
+        identical results; routing a slice per rank and all-gathering it was
+        slower: the tensor-core router is latency-bound per 128-token CTA),
+        computes its row-balanced share of the dispatched rows
         (pmoe_block_forward_rows) into its NVLink exchange buffer, and
         pmoe_rows_allreduce sums the partials (deterministic, fp32) into y."""
         T, H = x.shape
-        K, world, rank = self.K, self.world, self.rank
-        chunk = (T + world - 1) // world
-        rec = chunk * (2 * K + 1)
-        buf = torch.empty((world, rec), dtype=torch.int32, device=x.device)
-        mine = buf[rank]
-        t0 = min(rank * chunk, T)
-        t1 = min(t0 + chunk, T)
-        # the slice writes rows t0..t1 of arrays addressed from token 0, so
-        # hand it base pointers shifted back by t0 rows into this record
-        base = mine.data_ptr()
-        _lib.check("pmoe_route_slice", self.lib.pmoe_route_slice(
-            x.data_ptr(), T, H, self.E, K, I, Is, t0, t1, wp[0], wp[6],
-            base - t0 * K * 4, base + (chunk * K - t0 * K) * 4,
-            base + (2 * chunk * K - t0) * 4, ws.data_ptr(), nbytes, st))
-        dist.all_gather_into_tensor(buf, mine, group=self.group)
-        idx = buf[:, :chunk * K].reshape(world * chunk, K)[:T].contiguous()
-        wts = buf[:, chunk * K:2 * chunk * K].reshape(world * chunk, K)[:T].contiguous()
-        gate = buf[:, 2 * chunk * K:].reshape(world * chunk)[:T].contiguous()
-        # this rank's partial goes straight into its exchange buffer, then the
-        # NVLink all-reduce (pmoe_rows_allreduce) writes the sum into y
         self._rows_buffers(T)
         self.rx_epoch += 1
         part = ctypes.c_void_p()
         _lib.check("pmoe_rows_partial", self.lib.pmoe_rows_partial(
             self.rx_local, self.rx_tmax, H, self.rx_epoch, ctypes.byref(part)))
         _lib.check("pmoe_block_forward_rows", self.lib.pmoe_block_forward_rows(
-            x.data_ptr(), T, H, self.E, K, I, Is, *wp, idx.data_ptr(), wts.data_ptr(),
-            gate.data_ptr(), rank, world, flags, part.value, ws.data_ptr(), nbytes, st))
+            x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, None, None, None, 0, self.E,
+            self.rank, self.world, flags, part.value, ws.data_ptr(), nbytes, st))
         _lib.check("pmoe_rows_allreduce", self.lib.pmoe_rows_allreduce(
-            self.rx_arr, self.rx_tmax, T, H, rank, world, self.rx_epoch, y.data_ptr(), st))
+            self.rx_arr, self.rx_tmax, T, H, self.rank, self.world, self.rx_epoch, y.data_ptr(),
+            st))
+        return y
+
+    def _forward_a2a(self, x, w, I, Is, y):
+        """Token-dispatch comparator (all_to_all_single, the variant ep.py does not
+        have): each rank routes its own tokens, sends every token once to each
+        rank owning one of its experts, receivers compute their expert range on
+        the received tokens with the sender's routing (pmoe_block_forward_rows,
+        world 1), partial rows come back through a second all-to-all and are
+        added to the shared expert's output at home; an all_gather replicates y."""
+        from . import ops
+        T, H = x.shape
+        K, world, rank = self.K, self.world, self.rank
+        dev = x.device
+        t0, t1 = token_range(T, rank, world)
+        xl = x[t0:t1]
+        idx, wts, *_ = ops.moe_route(xl, w[0], w[6], K)
+        send, counts = a2a_plan(idx, self.E, world)
+        rc = torch.empty(world, dtype=torch.long, device=dev)
+        dist.all_to_all_single(rc, counts.to(dev), group=self.group)
+        sc, rc = counts.tolist(), rc.cpu().tolist()
+        M = sum(rc)
+        rx = torch.empty((M, H), dtype=_BF16, device=dev)
+        ri = torch.empty((M, K), dtype=torch.int32, device=dev)
+        rw = torch.empty((M, K), dtype=torch.float32, device=dev)
+        dist.all_to_all_single(rx, xl[send].contiguous(), rc, sc, group=self.group)
+        dist.all_to_all_single(ri, idx[send].contiguous(), rc, sc, group=self.group)
+        dist.all_to_all_single(rw, wts[send].contiguous(), rc, sc, group=self.group)
+        yr = torch.zeros((M, H), dtype=_BF16, device=dev)
+        if M > 0:
+            nb = _lib.workspace_size(M, H, self.E, K, I, Is)
+            ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+            gate = torch.zeros(M, dtype=torch.float32, device=dev)
+            st = torch.cuda.current_stream(dev).cuda_stream
+            _lib.check("pmoe_block_forward_rows", self.lib.pmoe_block_forward_rows(
+                rx.data_ptr(), M, H, self.E, K, I, Is, *[t.data_ptr() for t in w],
+                ri.data_ptr(), rw.data_ptr(), gate.data_ptr(), self.lo, self.hi, 0, 1, 2,
+                yr.data_ptr(), ws.data_ptr(), nb, st))
+        back = torch.empty((sum(sc), H), dtype=_BF16, device=dev)
+        dist.all_to_all_single(back, yr, sc, rc, group=self.group)
+        yl = ops.moe_block(xl, *w, K, 0, 0, 1).float()          # shared expert only
+        yl.index_add_(0, send, back.float())
+        chunk = (T + world - 1) // world
+        slab = torch.zeros((world * chunk, H), dtype=_BF16, device=dev)
+        slab[rank * chunk:rank * chunk + (t1 - t0)] = yl.to(_BF16)
+        dist.all_gather_into_tensor(slab, slab[rank * chunk:(rank + 1) * chunk].clone(),
+                                    group=self.group)
+        for r in range(world):
+            a, b = token_range(T, r, world)
+            y[a:b] = slab[r * chunk:r * chunk + (b - a)]
         return y
 
     def _rows_buffers(self, T: int):

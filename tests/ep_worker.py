@@ -28,11 +28,12 @@ def main():
     tensors = wts.tensors()
     fused = ep.EPGroup(S.E, S.H, S.K, mode="fused")
     nccl = ep.EPGroup(S.E, S.H, S.K, mode="nccl")
+    a2a = ep.EPGroup(S.E, S.H, S.K, mode="a2a")
     ok = True
     for T in (1, 5, 64, 64, 64, 200, 1024):
         x = W.make_hidden(T, S, seed=100 + T, device=dev)
         ref = ops.moe_block(x, *tensors, S.K, 0, S.E, 3).float().cpu().numpy()
-        for name, g in (("fused", fused), ("nccl", nccl)):
+        for name, g in (("fused", fused), ("nccl", nccl), ("a2a", a2a)):
             y = g.forward(x, tensors).float().cpu().numpy()
             r, m = O.rel_l2(y, ref), O.max_abs(y, ref)
             good = r <= 5e-3 and m <= 3e-2

@@ -34,3 +34,19 @@ def _worker(rank, world, port):
 
 def test_handle_exchange_gloo():
     mp.spawn(_worker, args=(2, 29611), nprocs=2, join=True)
+
+
+def test_a2a_plan_sends_each_token_once_per_owning_rank():
+    """Token-dispatch plan: a token goes to every rank owning one of its
+    experts, once, grouped by destination rank."""
+    import torch
+    from paris_moe_b200.ep import a2a_plan, expert_owner, expert_range
+    E, world = 16, 4
+    idx = torch.tensor([[0, 1, 4, 5], [15, 14, 13, 12], [3, 7, 11, 15], [2, 2, 2, 2]])
+    owner = expert_owner(idx, E, world)
+    for r in range(world):
+        lo, hi = expert_range(E, r, world)
+        assert torch.equal((owner == r), (idx >= lo) & (idx < hi))
+    send, counts = a2a_plan(idx, E, world)
+    assert counts.tolist() == [3, 2, 1, 2]
+    assert send.tolist() == [0, 2, 3, 0, 2, 2, 1, 2]

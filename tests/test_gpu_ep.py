@@ -128,7 +128,17 @@ def test_row_split_partials_sum_to_full(world):
     for r in range(world):
         y = torch.empty((T, S.H), dtype=torch.bfloat16, device="cuda")
         assert lib.pmoe_block_forward_rows(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *wp,
-                                           idx.data_ptr(), w.data_ptr(), gate.data_ptr(), r,
-                                           world, 3, y.data_ptr(), ws.data_ptr(), n, st) == 0
+                                           idx.data_ptr(), w.data_ptr(), gate.data_ptr(), 0,
+                                           S.E, r, world, 3, y.data_ptr(), ws.data_ptr(), n,
+                                           st) == 0
         total += y.float()
     assert O.rel_l2(total.cpu().numpy(), full.cpu().numpy()) < 5e-3
+    # the same split with each rank routing all tokens itself (null routing)
+    total2 = torch.zeros_like(full)
+    for r in range(world):
+        y = torch.empty((T, S.H), dtype=torch.bfloat16, device="cuda")
+        assert lib.pmoe_block_forward_rows(x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *wp,
+                                           None, None, None, 0, S.E, r, world, 3, y.data_ptr(),
+                                           ws.data_ptr(), n, st) == 0
+        total2 += y.float()
+    assert torch.equal(total2, total)
