@@ -27,6 +27,8 @@
 // The shared expert is expert index E: rows P.. of the dispatch, one per
 // token of its range, weight = its sigmoid gate.
 
+#include <algorithm>
+
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tc.cuh"
@@ -601,6 +603,113 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(
   reinterpret_cast<uint4*>(y + size_t(t) * H)[c8] = o;
 }
 
+// The same combine for K <= kCombineMaxK and H/8 <= 1024, as a persistent
+// grid: a block takes one token at a time (thread = 8 columns), issues that
+// token's row loads and meanwhile fetches the next token's selection (expert
+// ids, weights, row positions), so the two dependent round trips overlap.
+__device__ __forceinline__ void combine_select(
+    int t, int T, int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
+    const float* __restrict__ shared_gate, const int32_t* __restrict__ pair_pos, int p_lo,
+    int p_hi, unsigned& mask, float (&w)[kCombineMaxK + 1]) {
+  mask = 0u;
+#pragma unroll
+  for (int k = 0; k <= kCombineMaxK; ++k) w[k] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kCombineMaxK; ++k) {
+    if (k < K && with_routed) {
+      const size_t q = size_t(t) * K + k;
+      const int e = topk_idx[q];
+      bool sel = e >= lo && e < hi;
+      if (sel && pair_pos) {
+        const int p = pair_pos[q];
+        sel = p >= p_lo && p < p_hi;
+      }
+      if (sel) {
+        mask |= 1u << k;
+        w[k] = topk_w[q];
+      }
+    }
+  }
+  if (with_shared && t >= sh_lo && t < sh_hi) {
+    bool sel = true;
+    if (pair_pos) {
+      const int p = pair_pos[size_t(T) * K + t];
+      sel = p >= p_lo && p < p_hi;
+    }
+    if (sel) {
+      mask |= 1u << kCombineMaxK;
+      w[kCombineMaxK] = shared_gate[t];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) combine_rows_tok_kernel(
+    const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ topk_idx,
+    const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
+    int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
+    const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ row_range,
+    const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
+  const int cols8 = H / 8, c8 = threadIdx.x;
+  const bool act = c8 < cols8;
+  const int p_lo = pair_pos ? row_range[0] : 0, p_hi = pair_pos ? row_range[1] : 0;
+  unsigned mask = 0u;
+  float w[kCombineMaxK + 1];
+  int t = blockIdx.x;
+  if (t < T)
+    combine_select(t, T, K, lo, hi, with_shared, with_routed, sh_lo, sh_hi, topk_idx, topk_w,
+                   shared_gate, pair_pos, p_lo, p_hi, mask, w);
+  for (; t < T; t += gridDim.x) {
+    uint4 v[kCombineMaxK + 1];
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxK; ++k) {
+      const size_t q = k < kCombineMaxK ? size_t(t) * K + k : size_t(T) * K + t;
+      if (act && (mask >> k & 1u)) v[k] = __ldg(reinterpret_cast<const uint4*>(rows + q * H) + c8);
+    }
+    const int tn = t + gridDim.x;  // next token's selection while the rows are in flight
+    unsigned mask_n = 0u;
+    float wn[kCombineMaxK + 1];
+    if (tn < T)
+      combine_select(tn, T, K, lo, hi, with_shared, with_routed, sh_lo, sh_hi, topk_idx, topk_w,
+                     shared_gate, pair_pos, p_lo, p_hi, mask_n, wn);
+    if (act) {
+      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k <= kCombineMaxK; ++k) {
+        if (!(mask >> k & 1u)) continue;
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(b2[j]);
+          s[2 * j] = fmaf(w[k], f.x, s[2 * j]);
+          s[2 * j + 1] = fmaf(w[k], f.y, s[2 * j + 1]);
+        }
+      }
+      if (resid) {  // decoder layer: y = bf16(resid + bf16(sum))
+        const uint4 rv = reinterpret_cast<const uint4*>(resid + size_t(t) * H)[c8];
+        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(r2[j]);
+          s[2 * j] = f.x + bf16_round(s[2 * j]);
+          s[2 * j + 1] = f.y + bf16_round(s[2 * j + 1]);
+        }
+      }
+      uint4 o;
+      uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
+        op[j] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      reinterpret_cast<uint4*>(y + size_t(t) * H)[c8] = o;
+    }
+    mask = mask_n;
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxK; ++k) w[k] = wn[k];
+  }
+}
+
 namespace {
 int g_pairs = 74;  // co-resident CTA pairs of the GEMM kernels
 
@@ -703,6 +812,15 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   err = mark(2);
   if (err != cudaSuccess) return err;
   const long n8 = long(T) * d.H / 8;
+  const int* pp = world > 1 ? ws.pair_pos : nullptr;
+  if (d.K <= kCombineMaxK && d.H / 8 <= 256) {
+    const unsigned threads = unsigned((d.H / 8 + 31) / 32 * 32);
+    const unsigned blocks = unsigned(std::min<long>(T, long(2 * g_pairs) * 4));  // one wave
+    combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(
+        ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
+        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y);
+    return cudaGetLastError();
+  }
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
       ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
       with_routed, d.sh_lo, d.sh_hi, world > 1 ? ws.pair_pos : nullptr, ws.tile_counts + 4,
