@@ -99,16 +99,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* map, int c0,
-                                            int c1, int c2, int c3, int c4, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
-      "r"(smem_u32(bar))
-      : "memory");
-}
-
 // CTA-pair forms: the copy lands in this CTA's shared memory and its bytes
 // complete on the mbarrier at shared::cluster address `bar_cluster` (the
 // even CTA's, which the pair MMA waits on).  No multicast.
@@ -129,21 +119,6 @@ __device__ __forceinline__ void tma_load_5d_pair(void* smem_dst, const CUtensorM
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
       "r"(bar_cluster)
       : "memory");
-}
-
-// L2 prefetch of a tile (no shared-memory destination, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
-               : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_5d(const CUtensorMap* map, int c0, int c1, int c2,
-                                                int c3, int c4) {
-  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-               : "memory");
 }
 
 // Same, with an L2 eviction-priority hint (weights are read once per call).
