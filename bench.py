@@ -201,7 +201,8 @@ class Runner:
     def step(self, profiled=False):
         c = self.ctx
         if c.world > 1:
-            c.group.forward(self.x, self.tensors, out=self.y, workspace=self.ws)
+            c.group.forward(self.x, self.tensors, out=self.y, workspace=self.ws,
+                            events=c.ev_arr if profiled else None)
             return
         S = c.S
         args = (self.x.data_ptr(), self.T, S.H, S.E, S.K, S.I, S.Is, *self.wp, 0, S.E, 3,
@@ -236,8 +237,8 @@ class Runner:
         combine) from events around the kernels of a synchronised call."""
         import torch
         c = self.ctx
-        if c.world > 1:
-            return None
+        if c.world > 1 and c.group.uses_exchange(self.T):
+            return None      # decode exchange: no phase events across its kernels
         acc = [0.0] * 4
         for _ in range(n):
             self.step(profiled=True)
@@ -325,8 +326,13 @@ def comparators(c, x, tensors, T, steps, warmup):
     import torch
     from paris_moe_b200 import ep
     out = {}
-    for mode, label in (("nccl", "nccl_all_reduce"), ("a2a", "all_to_all")):
+    runs = [("nccl", "nccl_all_reduce"), ("a2a", "all_to_all")]
+    if T > ep.FUSED_MAX_T:
+        runs.append(("fused", "nvlink_partial_sum"))   # the earlier prefill exchange
+    for mode, label in runs:
         g = ep.EPGroup(c.S.E, c.S.H, c.S.K, mode=mode)
+        if label == "nvlink_partial_sum":
+            g.prefill = "partial"
         y = torch.empty_like(x)
         for _ in range(warmup):
             g.forward(x, tensors, out=y)
@@ -524,10 +530,14 @@ def main():
               "ms_per_step": pms, "algorithmic_flops": flops,
               "layer_tflops": flops / (pms * 1e-3) / 1e12,
               "layer_frac": flops / (pms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-              # router_tc, scan, scatter, plan, row copy, gate_up, down, combine per step
-              "gpu_launches": 8 * psteps, "clocks": pclk,
+              # router_tc, scan, scatter, plan, row copy, gate_up, down, combine per step;
+              # N > 1 adds publish, wait, publish, gather around the slice combine
+              "gpu_launches": (8 if c.world == 1 else 12) * psteps, "clocks": pclk,
               "e2e": pre.e2e(max(5, min(a.steps, 50)))}
-        if pphase is not None:
+        if pphase is not None and c.world > 1:   # rank 0's phases
+            pl["phase_ms_rank0"] = dict(zip(("route_plan_copy", "gate_up", "down_peer_stores",
+                                             "exchange_combine_gather"), pphase))
+        elif pphase is not None:
             pl["phase_ms"] = dict(zip(("route_plan_copy", "gate_up", "down", "combine"), pphase))
             P = a.prefill_T * S.K
             gu_flops = 2 * (P + a.prefill_T) * S.H * 2 * S.I

@@ -177,6 +177,15 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
                             const float* topk_w, const float* shared_gate, int expert_lo,
                             int expert_hi, int rank, int world, int flags, uint16_t* y,
                             void* workspace, size_t workspace_bytes, void* stream);
+/* pmoe_block_forward_rows with the phase events of
+ * pmoe_block_forward_profiled (events[0..4], same meaning and NULL rule). */
+int pmoe_block_forward_rows_profiled(
+    const uint16_t* x, int T, int H, int E, int K, int I, int Is, const uint16_t* w_router,
+    const uint16_t* w_gate_up, const uint16_t* w_down, const uint16_t* w_sh_gate,
+    const uint16_t* w_sh_up, const uint16_t* w_sh_down, const uint16_t* w_sh_gvec,
+    const int32_t* topk_idx, const float* topk_w, const float* shared_gate, int expert_lo,
+    int expert_hi, int rank, int world, int flags, uint16_t* y, void* workspace,
+    size_t workspace_bytes, void* stream, void* const* events, int n_events);
 
 /* Sum of the row-split partials over NVLink, in place of the caller's NCCL
  * all_reduce (ep.py:140): each rank owns a buffer of pmoe_rows_buffer_bytes
@@ -194,6 +203,29 @@ int pmoe_rows_partial(void* own_buf, int T_max, int H, int epoch, void** partial
 int pmoe_rows_allreduce(void* const* bufs, int T_max, int T, int H, int rank, int world,
                         int epoch, uint16_t* y, void* stream);
 int pmoe_rows_status(const void* own_buf, int* status);
+
+/* Row-split prefill with the exchange fused into the expert GEMMs, replacing
+ * the pmoe_block_forward_rows + all_reduce pair of ep.py:97-143/140 for
+ * prefill-sized batches.  Every rank routes all T tokens (identically) and
+ * computes its row-balanced share of the dispatched rows, as in
+ * pmoe_block_forward_rows; the down GEMM stores each unweighted output row
+ * straight into the buffer of the rank that owns its token (token slice
+ * [r*T/world, (r+1)*T/world)) with NVLink peer stores; each rank then combines
+ * its slice locally, in the single-GPU order, and every rank gathers the
+ * slices.  y is the full output on every rank, bit-identical to the
+ * single-GPU pmoe_block_forward.  bufs[q]: rank q's buffer of
+ * pmoe_rows_fused_buffer_bytes(T_max, H, K) (pmoe_ipc_alloc'ed, zeroed,
+ * mapped on every rank); epoch > 0, +1 per call, the same on every rank.
+ * flags must include PMOE_F_SHARED | PMOE_F_ROUTED; K <= 8, H <= 2048.
+ * events: as pmoe_block_forward_profiled ([4] after the gather; may be NULL).
+ * Waits are bounded (status 4 via pmoe_rows_status). */
+int pmoe_rows_fused_buffer_bytes(int T_max, int H, int K, size_t* bytes);
+int pmoe_block_forward_rows_fused(
+    const uint16_t* x, int T, int H, int E, int K, int I, int Is, const uint16_t* w_router,
+    const uint16_t* w_gate_up, const uint16_t* w_down, const uint16_t* w_sh_gate,
+    const uint16_t* w_sh_up, const uint16_t* w_sh_down, const uint16_t* w_sh_gvec, int rank,
+    int world, void* const* bufs, int T_max, int epoch, int flags, uint16_t* y,
+    void* workspace, size_t workspace_bytes, void* stream, void* const* events, int n_events);
 
 /* One decoder layer of the MoE-only stack: y = x + block(RMSNorm(x)), with
  * RMSNorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w_norm)) in fp32 and the

@@ -46,6 +46,14 @@ SIGNATURES = {
                               _P]),
     "pmoe_block_forward_rows": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
                                      _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
+    "pmoe_rows_fused_buffer_bytes": (_I, [_I, _I, _I, ctypes.POINTER(_SZ)]),
+    "pmoe_block_forward_rows_fused": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
+                                           _P, _I, _I, ctypes.POINTER(_P), _I, _I, _I, _P, _P,
+                                           _SZ, _P,
+                                           ctypes.POINTER(_P), _I]),
+    "pmoe_block_forward_rows_profiled": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P,
+                                              _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
+                                              _SZ, _P, ctypes.POINTER(_P), _I]),
     "pmoe_read_status": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
     "pmoe_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
     "pmoe_ipc_free": (_I, [_P]),

@@ -125,6 +125,10 @@ struct RowSplit {
   const float* topk_w;
   const float* shared_gate;
   int rank, world;
+  // Fused exchange (bufs non-null): the down GEMM stores rows at their token
+  // owner's buffer and the call ends with the full y on every rank.
+  void* const* bufs = nullptr;
+  int T_max = 0, epoch = 0;
 };
 
 // Shared implementation of the forward entry points.  `ep` (world > 0)
@@ -180,6 +184,7 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
         (flags & PMOE_F_FORCE_STREAM))
       return PMOE_ERR_ARG;
     if (!tc_supported(d) || !route_tc_supported(d)) return PMOE_ERR_UNSUPPORTED;
+    if (rs->bufs && (K > 8 || H > 2048 || given)) return PMOE_ERR_UNSUPPORTED;
     use_tc = true;
   }
   if (ep.world > 0 && (flags & PMOE_F_FORCE_TC)) return PMOE_ERR_UNSUPPORTED;
@@ -224,11 +229,29 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
     for (int i = 0; i < 3; ++i)
       if (events && i + 1 < n_events) ev[i] = events[i + 1];
+    RowsOut ro{};
+    const bool fused = rs && rs->bufs;
+    if (fused) {
+      ro.world = rs->world;
+      for (int q = 0; q < rs->world; ++q)
+        ro.base[q] = reinterpret_cast<__nv_bfloat16*>(
+            static_cast<char*>(rs->bufs[q]) + rx_fused_rows_offset(rs->T_max, H, K, rs->epoch));
+    }
     if (launch_tc_experts(d, xin, bf(w_gate_up), bf(w_down), bf(w_sh_gate), bf(w_sh_up),
                           bf(w_sh_down), ws, resid, reinterpret_cast<__nv_bfloat16*>(y),
                           expert_lo, expert_hi, with_shared, with_routed, rs ? rs->rank : 0,
-                          rs ? rs->world : 1, st, ev) != cudaSuccess)
+                          rs ? rs->world : 1, st, ev, fused ? &ro : nullptr) != cudaSuccess)
       return PMOE_ERR_CUDA;
+    if (fused) {
+      int sms = 148;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (launch_rows_fused_tail(rs->bufs, rs->T_max, rs->world, rs->rank, rs->epoch, T, H, E, K,
+                                 ws.topk_idx, ws.topk_w, ws.shared_gate,
+                                 reinterpret_cast<__nv_bfloat16*>(y), sms, st) != cudaSuccess)
+        return PMOE_ERR_CUDA;
+    }
     if (mark(4) != cudaSuccess) return PMOE_ERR_CUDA;
     return PMOE_OK;
   }
@@ -395,6 +418,47 @@ int pmoe_block_forward_rows(const uint16_t* x, int T, int H, int E, int K, int I
   return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
                       w_sh_down, w_sh_gvec, expert_lo, expert_hi, 0, T, flags, y, workspace,
                       workspace_bytes, stream, nullptr, 0, none, nullptr, &rs);
+}
+
+int pmoe_block_forward_rows_profiled(
+    const uint16_t* x, int T, int H, int E, int K, int I, int Is, const uint16_t* w_router,
+    const uint16_t* w_gate_up, const uint16_t* w_down, const uint16_t* w_sh_gate,
+    const uint16_t* w_sh_up, const uint16_t* w_sh_down, const uint16_t* w_sh_gvec,
+    const int32_t* topk_idx, const float* topk_w, const float* shared_gate, int expert_lo,
+    int expert_hi, int rank, int world, int flags, uint16_t* y, void* workspace,
+    size_t workspace_bytes, void* stream, void* const* events, int n_events) {
+  const EpPeers none{};
+  const RowSplit rs{topk_idx, topk_w, shared_gate, rank, world};
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, expert_lo, expert_hi, 0, T, flags, y, workspace,
+                      workspace_bytes, stream, events, n_events, none, nullptr, &rs);
+}
+
+int pmoe_rows_fused_buffer_bytes(int T_max, int H, int K, size_t* bytes) {
+  if (!bytes || T_max <= 0 || H <= 0 || H % 8 != 0 || K <= 0) return PMOE_ERR_ARG;
+  *bytes = rx_fused_buffer_bytes(T_max, H, K);
+  return PMOE_OK;
+}
+
+int pmoe_block_forward_rows_fused(
+    const uint16_t* x, int T, int H, int E, int K, int I, int Is, const uint16_t* w_router,
+    const uint16_t* w_gate_up, const uint16_t* w_down, const uint16_t* w_sh_gate,
+    const uint16_t* w_sh_up, const uint16_t* w_sh_down, const uint16_t* w_sh_gvec, int rank,
+    int world, void* const* bufs, int T_max, int epoch, int flags, uint16_t* y,
+    void* workspace, size_t workspace_bytes, void* stream, void* const* events, int n_events) {
+  if (!bufs || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || epoch <= 0 ||
+      T > T_max || (flags & (PMOE_F_SHARED | PMOE_F_ROUTED)) != (PMOE_F_SHARED | PMOE_F_ROUTED))
+    return PMOE_ERR_ARG;
+  for (int q = 0; q < world; ++q)
+    if (!bufs[q] || !aligned16(bufs[q])) return PMOE_ERR_ARG;
+  const EpPeers none{};
+  RowSplit rs{nullptr, nullptr, nullptr, rank, world};
+  rs.bufs = bufs;
+  rs.T_max = T_max;
+  rs.epoch = epoch;
+  return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
+                      w_sh_down, w_sh_gvec, 0, E, 0, T, flags, y, workspace, workspace_bytes,
+                      stream, events, n_events, none, nullptr, &rs);
 }
 
 int pmoe_rows_buffer_bytes(int T_max, int H, size_t* bytes) {

@@ -77,6 +77,23 @@ struct EpPeers {
   int epoch;               // host epoch (> 0) when epoch_dev is null
 };
 
+// Destination of the down GEMM's unweighted rows in row-split prefill with a
+// fused exchange: row q (token-major, q = t*K + k, shared row T*K + t) goes to
+// base[owner(t)] + q*H, owner(t) = the rank r with r*T/world <= t < (r+1)*T/world
+// (peer stores over NVLink).  world == 0: this rank's workspace rows.
+struct RowsOut {
+  __nv_bfloat16* base[kMaxRanks];
+  int world;
+};
+
+// The rank whose token slice [r*T/world, (r+1)*T/world) holds token t.
+__host__ __device__ __forceinline__ int slice_owner(int t, int T, int world) {
+  int r = int(long(t) * world / T);
+  while (r > 0 && long(r) * T / world > t) --r;
+  while (r + 1 < world && long(r + 1) * T / world <= t) ++r;
+  return r;
+}
+
 __device__ __forceinline__ int ep_epoch(const EpPeers& ep) {
   return ep.epoch_dev ? *ep.epoch_dev : ep.epoch;
 }

@@ -30,7 +30,12 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
                               int with_shared, int with_routed, int rank, int world,
-                              cudaStream_t st, void* const events[3]);
+                              cudaStream_t st, void* const events[3],
+                              const RowsOut* rows_out = nullptr);
+cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
+                                 const float* topk_w, const float* shared_gate, int T, int H,
+                                 int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
+                                 cudaStream_t st);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch).
@@ -61,6 +66,14 @@ size_t rx_region_offset(int T_max, int H, int epoch);
 size_t rx_status_offset();
 cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int rank, int epoch,
                                   int T, int H, __nv_bfloat16* y, int num_sms, cudaStream_t st);
+// Fused row exchange: the down GEMM stores rows at their token owner, which
+// combines its slice locally; then the gather (rows_exchange.cu).
+size_t rx_fused_buffer_bytes(int T_max, int H, int K);
+size_t rx_fused_rows_offset(int T_max, int H, int K, int epoch);
+cudaError_t launch_rows_fused_tail(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                   int T, int H, int E, int K, const int32_t* topk_idx,
+                                   const float* topk_w, const float* shared_gate,
+                                   __nv_bfloat16* y, int num_sms, cudaStream_t st);
 
 // out = Qwen3_5MoeRMSNorm(x; w, eps), bf16 [T][H].
 cudaError_t launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int T,

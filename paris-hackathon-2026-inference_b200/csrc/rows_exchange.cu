@@ -56,10 +56,16 @@ __device__ bool rx_wait(const RxPeers& p, int off) {
   return true;
 }
 
-__global__ void rx_publish_kernel(RxPeers p) {
+// Raise flags[rank] = epoch (flag set at `off`) on every rank, after all of
+// this rank's earlier work on the stream.
+__global__ void rx_publish_kernel(RxPeers p, int off) {
   __threadfence_system();
-  for (int q = 0; q < p.world; ++q) st_release_sys(rx_flags(p, q, kRxFlagsA) + p.rank, p.epoch);
+  for (int q = 0; q < p.world; ++q) st_release_sys(rx_flags(p, q, off) + p.rank, p.epoch);
 }
+
+// Bounded wait for every rank's flag at `off` (the kernels after it on the
+// stream run once it returns; a timeout leaves status 4).
+__global__ void rx_wait_kernel(RxPeers p, int off) { rx_wait(p, off); }
 
 __global__ void __launch_bounds__(kRxThreads) rx_reduce_kernel(RxPeers p, int T, int H) {
   __shared__ int s_ok;
@@ -163,8 +169,60 @@ cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int r
   p.rank = rank;
   p.epoch = epoch;
   p.region = (size_t(T_max) * H * 2 + 255) / 256 * 256;
-  rx_publish_kernel<<<1, 1, 0, st>>>(p);
+  rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
   rx_reduce_kernel<<<num_sms * 2, kRxThreads, 0, st>>>(p, T, H);
+  rx_gather_kernel<<<num_sms * 4, kRxThreads, 0, st>>>(p, T, H, y);
+  return cudaGetLastError();
+}
+
+// ---- fused row exchange ------------------------------------------------------
+// Buffer: the layout above, then two parity regions of T_max*(K+1) rows x H
+// bf16 that receive, from every rank's down GEMM (peer stores), the
+// unweighted rows of the tokens this rank owns (token-major, row q at q*H).
+// Per call, after the down GEMM on this rank's stream:
+//   publish  flagsA[rank] = e on every rank (this rank's rows are delivered)
+//   wait     (bounded) for every rank's flagsA
+//   combine  this rank's token slice from its own rows region, in the
+//            single-GPU order (routed k = 0..K-1, then shared), into its
+//            reduced region
+//   publish  flagsB[rank] = e on every rank
+//   gather   as above.
+// Parity safety is the argument above: a rank writes rows of call e+2 into
+// the region of call e only after its gather of e+1, which follows every
+// rank's combine of e+1 and so of e.
+static size_t rx_rows_region(int T_max, int H, int K) {
+  return (size_t(T_max) * (K + 1) * H * 2 + 255) / 256 * 256;
+}
+
+size_t rx_fused_buffer_bytes(int T_max, int H, int K) {
+  return rx_buffer_bytes(T_max, H) + 2 * rx_rows_region(T_max, H, K);
+}
+
+size_t rx_fused_rows_offset(int T_max, int H, int K, int epoch) {
+  return rx_buffer_bytes(T_max, H) + size_t(epoch & 1) * rx_rows_region(T_max, H, K);
+}
+
+cudaError_t launch_rows_fused_tail(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                   int T, int H, int E, int K, const int32_t* topk_idx,
+                                   const float* topk_w, const float* shared_gate,
+                                   __nv_bfloat16* y, int num_sms, cudaStream_t st) {
+  RxPeers p{};
+  for (int q = 0; q < world; ++q) p.base[q] = static_cast<char*>(bufs[q]);
+  p.world = world;
+  p.rank = rank;
+  p.epoch = epoch;
+  p.region = (size_t(T_max) * H * 2 + 255) / 256 * 256;
+  char* own = static_cast<char*>(bufs[rank]);
+  const auto* rows = reinterpret_cast<const __nv_bfloat16*>(
+      own + rx_fused_rows_offset(T_max, H, K, epoch));
+  auto* reduced = reinterpret_cast<__nv_bfloat16*>(own + rx_region_offset(T_max, H, epoch));
+  const int t0 = int(long(rank) * T / world), t1 = int(long(rank + 1) * T / world);
+  rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
+  rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
+  cudaError_t e = launch_combine_slice(rows, topk_idx, topk_w, shared_gate, T, H, E, K, t0, t1,
+                                       reduced, st);
+  if (e != cudaSuccess) return e;
+  rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsB);
   rx_gather_kernel<<<num_sms * 4, kRxThreads, 0, st>>>(p, T, H, y);
   return cudaGetLastError();
 }

@@ -28,6 +28,7 @@
 // token of its range, weight = its sigmoid gate.
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
@@ -52,6 +53,8 @@ constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kTmemCols = 512;       // two 256-column fp32 accumulators
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
+// barrier area: 16 mbarriers (128 B), the TMEM slot at 128, four abort flags at 192
+static_assert(192 + 4 * 4 <= kBarBytes, "barrier area");
 
 enum TcMode { kGateUp = 0, kDown = 1 };
 
@@ -60,6 +63,10 @@ struct TileTables {
   const int32_t* count;  // number of tiles
   const int32_t* pair_dst;  // token-major output row of each dispatched row
   const float* pair_w;
+  RowsOut out;              // down: peer destinations (out.world > 0) of the rows
+  int T, K;                 // for the token of a token-major row
+  int sh5;                  // gate_up: shared gate|up in one 5-D map (tm_b_sh0)
+  int sh_swap;              // ... whose first half is the up rows (w_sh_up < w_sh_gate)
 };
 
 __device__ __forceinline__ uint8_t* tc_align1024(uint8_t* p) {
@@ -97,7 +104,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b_sh0,
     const __grid_constant__ CUtensorMap tm_b_sh1, const __grid_constant__ CUtensorMap tm_a,
-    const __grid_constant__ CUtensorMap tm_a32, TileTables tt, int H, int E, int I, int Is,
+    const __grid_constant__ CUtensorMap tm_a32, const __grid_constant__ TileTables tt, int H, int E, int I, int Is,
     int ldh, __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ out_rows,
     int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
@@ -107,6 +114,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
   uint64_t* tfull = empty + kTcStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  // down epilogue: per column quarter, set when one of its warps gave up
+  // waiting for an accumulator, so that its four warps leave together
+  volatile int* quarter_abort = reinterpret_cast<volatile int*>(tmem_slot + 16);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
@@ -120,6 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 2 * kEpiWarps);
     }
+    for (int i = 0; i < 4; ++i) quarter_abort[i] = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -166,7 +177,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
           const uint32_t fb = full0 + s * 8;
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * tx);
           if (MODE == kGateUp) {
-            if (sh) {
+            if (sh && tt.sh5) {
+              tma_load_5d_pair(st, &tm_b_sh0, kc * kBK, 0, 0, f0 / 16, 0, fb);
+            } else if (sh) {
               for (int g = 0; g < 4; ++g) {
                 tma_load_2d_pair(st + g * 4096, &tm_b_sh0, kc * kBK, f0 + 16 * g, fb);
                 tma_load_2d_pair(st + g * 4096 + 2048, &tm_b_sh1, kc * kBK, f0 + 16 * g, fb);
@@ -248,15 +261,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
       const uint32_t b = lt & 1, use = lt >> 1;
       // down: this lane's output rows of the two 32-row chunks, loaded
       // before the accumulator wait so their latency overlaps it.
-      int ldst[2] = {0, 0};
+      int ldst[2] = {0, 0}, lown[2] = {0, 0};
       if (MODE == kDown) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           const int r = cw + 32 * k + lane;
           if (r < nrows) ldst[k] = tt.pair_dst[row0 + r];
+          if (tt.out.world > 0) {
+            const int tk = tt.T * tt.K;
+            lown[k] = slice_owner(ldst[k] < tk ? ldst[k] / tt.K : ldst[k] - tk, tt.T,
+                                  tt.out.world);
+          }
         }
       }
-      if (!mbar_wait(&tfull[b], use & 1)) {
+      const bool got = mbar_wait(&tfull[b], use & 1);
+      if (MODE == kDown) {
+        // the quarter's warps meet at named barriers below: decide together
+        if (!got && lane == 0) quarter_abort[quarter] = 1;
+        named_bar_sync(1 + quarter, 128);
+        if (quarter_abort[quarter]) {
+          tc_status(status, kStatusTimeoutTmem);
+          break;
+        }
+      } else if (!got) {
         tc_status(status, kStatusTimeoutTmem);
         break;
       }
@@ -270,6 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
         // 32 bytes of h to one lane.
         const int f0 = tl.w * 128 + 64 * int(rank) + q * 16;
         const int fl = lane & 15, hi = lane >> 4;
+        const bool swap_gu = tt.sh_swap && tl.x == E;
         __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(stg_raw);  // [32 rows][16]
         if (cw < nrows) {
           uint32_t v[2][32];  // 64 columns: two loads, one wait
@@ -284,8 +312,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
             for (int i = 0; i < 16; ++i) {
               const float mine = __uint_as_float(hi ? v[sub][i] : v[sub][16 + i]);
               const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-              const float g = hi ? other : __uint_as_float(v[sub][i]);
-              const float u = hi ? __uint_as_float(v[sub][16 + i]) : other;
+              float g = hi ? other : __uint_as_float(v[sub][i]);
+              float u = hi ? __uint_as_float(v[sub][16 + i]) : other;
+              if (swap_gu) {  // lanes 0-15 hold the up rows
+                const float tmp = g;
+                g = u;
+                u = tmp;
+              }
               stg[(hi * 16 + i) * 16 + fl] = __float2bfloat16_rn(silu_f(g) * u);
             }
             __syncwarp();
@@ -299,22 +332,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
           }
         }
       } else {
-        // Lane = output feature f0 + lane; per column (dispatched row) the
-        // warp stores 64 contiguous bytes of that row (the routing weight is
-        // applied by the combine).
-        const int f0 = tl.w * 256 + 128 * int(rank) + q * 32;
+        // Lane = output feature f0 + lane of each TMEM column (dispatched
+        // row).  The four warps of a column quarter (one per lane quadrant)
+        // stage 16 columns x their 128 features in shared memory, then each
+        // warp stores whole 256-byte row segments (16 lanes x 16 bytes per
+        // row): to this rank's rows, or to the token owner's buffer over
+        // NVLink.  The routing weight is applied by the combine.
+        const int fq = tl.w * 256 + 128 * int(rank);  // the quarter's first feature
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(
+            smem + kTcStages * kTcStageBytes + kBarBytes + quarter * 4 * kEpiWarpBytes);
+        const int bar_id = 1 + quarter;
 #pragma unroll
         for (int sub = 0; sub < 2; ++sub) {
           const int c = cw + 32 * sub;
-          if (c >= nrows) break;
+          if (c >= nrows) break;  // uniform over the quarter's four warps
           uint32_t v[32];
           tmem_ld32(taddr + c, v);
           tmem_ld_wait();
-          __nv_bfloat16* col = out_rows + f0 + lane;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int dst = __shfl_sync(0xffffffffu, ldst[sub], i);
-            if (c + i < nrows) col[size_t(dst) * H] = __float2bfloat16_rn(__uint_as_float(v[i]));
+          for (int hh = 0; hh < 2; ++hh) {
+            const int cc = c + 16 * hh;
+            if (cc >= nrows) break;
+            named_bar_sync(bar_id, 128);  // the previous segment's reads are done
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              stg[i * 128 + q * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[16 * hh + i]));
+            named_bar_sync(bar_id, 128);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int ci = 4 * q + 2 * j + (lane >> 4);  // column within the 16
+              const int dst = __shfl_sync(0xffffffffu, ldst[sub], 16 * hh + ci);
+              const int own = __shfl_sync(0xffffffffu, lown[sub], 16 * hh + ci);
+              if (cc + ci < nrows) {
+                const uint4 val = reinterpret_cast<const uint4*>(stg + ci * 128)[lane & 15];
+                __nv_bfloat16* base = tt.out.world > 0 ? tt.out.base[own] : out_rows;
+                reinterpret_cast<uint4*>(base + size_t(dst) * H + fq)[lane & 15] = val;
+              }
+            }
           }
         }
       }
@@ -325,6 +379,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
   }
 
   __syncwarp();  // reconverge warps whose work ran on one elected lane
+  if (MODE == kDown && tt.out.world > 0) __threadfence_system();  // peer rows visible
   tc_fence_before();
   cluster_sync_all();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
@@ -430,7 +485,7 @@ __device__ __forceinline__ void plan_scan(int (&v)[NV], int (&ex)[NV], int (*s_w
 __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
     const int32_t* __restrict__ n_active, int E, int H, int I, int Is, int rank, int world,
-    int4* __restrict__ gu_tiles, int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles,
+    int c0, int4* __restrict__ gu_tiles, int4* __restrict__ dn_tiles, int4* __restrict__ m_tiles,
     int32_t* __restrict__ counts) {
   __shared__ int s_wsum[3][32];
   __shared__ int s_tot[3];
@@ -446,19 +501,27 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
   }
   __syncthreads();
   // Row split across `world` ranks: the 256-row blocks of every expert, in
-  // dispatch order, go to the rank whose share of the R dispatched rows holds
-  // the block's middle row, so each rank owns one contiguous row range.
-  const long R = offsets[E + 1];
-  int e = -1, r0 = 0, nrow = 0, nbg = 0;
+  // dispatch order, each costing c0 + its rows, go to the rank whose share of
+  // the total cost holds the block's middle, so each rank owns one contiguous
+  // row range (c0 = 0: an even split of the rows; larger c0 evens out the
+  // number of blocks, hence of GEMM tiles, per rank).
+  int e = -1, r0 = 0, nrow = 0, nbg = 0, p0 = 0, n = 0, mt = 0;
   if (tid < na) {
     e = active[tid];
-    const int p0 = offsets[e], n = offsets[e + 1] - p0;
+    p0 = offsets[e];
+    n = offsets[e + 1] - p0;
     nbg = (e == E ? Is : I) / 128;
-    const int mt = (n + kTok - 1) / kTok;
+    mt = (n + kTok - 1) / kTok;
+  }
+  int cv[1] = {mt * c0 + n}, cx[1];
+  plan_scan<1>(cv, cx, s_wsum, s_tot);
+  const long total = s_tot[0];
+  __syncthreads();
+  if (tid < na) {
     int ma = mt, mb = mt;
     for (int m = 0; m < mt; ++m) {
-      const long mid = p0 + m * kTok + min(kTok, n - m * kTok) / 2;
-      const bool own = mid * world >= long(rank) * R && mid * world < long(rank + 1) * R;
+      const long mid = cx[0] + long(m) * (c0 + kTok) + (c0 + min(kTok, n - m * kTok)) / 2;
+      const bool own = mid * world >= long(rank) * total && mid * world < long(rank + 1) * total;
       if (own && ma == mt) ma = m;
       if (own) mb = m + 1;
     }
@@ -469,8 +532,8 @@ __global__ void __launch_bounds__(kPlanThreads) plan_tiles_kernel(
       atomicMax(&s_hi, r0 + nrow);
     }
   }
-  const int mt = (nrow + kTok - 1) / kTok;
-  int v[3] = {mt * nbg, mt * nb_dn, (nrow + kGatherRows - 1) / kGatherRows};
+  const int mto = (nrow + kTok - 1) / kTok;
+  int v[3] = {mto * nbg, mto * nb_dn, (nrow + kGatherRows - 1) / kGatherRows};
   int ex[3];
   plan_scan<3>(v, ex, s_wsum, s_tot);
   s_ex[tid] = make_int4(e, r0, nrow, nbg);
@@ -649,17 +712,18 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
     const float* __restrict__ topk_w, const float* __restrict__ shared_gate, int T, int H,
     int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
     const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ row_range,
-    const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
+    const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y, int t_lo,
+    int t_hi) {
   const int cols8 = H / 8, c8 = threadIdx.x;
   const bool act = c8 < cols8;
   const int p_lo = pair_pos ? row_range[0] : 0, p_hi = pair_pos ? row_range[1] : 0;
   unsigned mask = 0u;
   float w[kCombineMaxK + 1];
-  int t = blockIdx.x;
-  if (t < T)
+  int t = t_lo + blockIdx.x;
+  if (t < t_hi)
     combine_select(t, T, K, lo, hi, with_shared, with_routed, sh_lo, sh_hi, topk_idx, topk_w,
                    shared_gate, pair_pos, p_lo, p_hi, mask, w);
-  for (; t < T; t += gridDim.x) {
+  for (; t < t_hi; t += gridDim.x) {
     uint4 v[kCombineMaxK + 1];
 #pragma unroll
     for (int k = 0; k <= kCombineMaxK; ++k) {
@@ -669,7 +733,7 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
     const int tn = t + gridDim.x;  // next token's selection while the rows are in flight
     unsigned mask_n = 0u;
     float wn[kCombineMaxK + 1];
-    if (tn < T)
+    if (tn < t_hi)
       combine_select(tn, T, K, lo, hi, with_shared, with_routed, sh_lo, sh_hi, topk_idx, topk_w,
                      shared_gate, pair_pos, p_lo, p_hi, mask_n, wn);
     if (act) {
@@ -712,6 +776,19 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
 
 namespace {
 int g_pairs = 74;  // co-resident CTA pairs of the GEMM kernels
+
+// Per-block cost constant of the row split, in rows: 512 (two full blocks'
+// rows) evens out the GEMM tile count per rank where few tiles per rank make
+// the last round of the persistent grid decide the time, and keeps rows even
+// where there are many (PMOE_SPLIT_C0 overrides).
+int split_c0() {
+  static const int c0 = [] {
+    const char* v = std::getenv("PMOE_SPLIT_C0");
+    const int n = v ? std::atoi(v) : 512;
+    return n >= 0 && n <= 1 << 16 ? n : 512;
+  }();
+  return c0;
+}
 
 template <int MODE, typename... Args>
 cudaError_t launch_pairs(cudaStream_t st, Args... args) {
@@ -768,7 +845,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                               const __nv_bfloat16* w_sh_down, const Workspace& ws,
                               const __nv_bfloat16* resid, __nv_bfloat16* y, int lo, int hi,
                               int with_shared, int with_routed, int rank, int world,
-                              cudaStream_t st, void* const events[3]) {
+                              cudaStream_t st, void* const events[3],
+                              const RowsOut* rows_out) {
   // events (each may be null): before gate_up, after gate_up, after down
   auto mark = [&](int i) {
     return events[i] ? cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st) : cudaSuccess;
@@ -792,15 +870,37 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
       !make_tmap_bf16_2d(&tm_xp32, ws.x_perm, H, R, H * 2, kBK, kRowChunk))
     return cudaErrorInvalidValue;
   plan_tiles_kernel<<<1, kPlanThreads, 0, st>>>(ws.offsets, ws.active, ws.n_active, d.E, d.H,
-                                                d.I, d.Is, rank, world, ws.gu_tiles,
+                                                d.I, d.Is, rank, world, split_c0(),
+                                                ws.gu_tiles,
                                                 ws.dn_tiles, ws.m_tiles, ws.tile_counts);
   gather_rows_kernel<<<2 * g_pairs * 16, kGatherThreads, 0, st>>>(
       x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, ws.x_perm);
   cudaError_t err = mark(0);
   if (err != cudaSuccess) return err;
   int* status = ws.status + 1;
-  TileTables gu{ws.gu_tiles, ws.tile_counts, ws.pair_dst, ws.pair_w};
-  TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w};
+  // Shared gate and up rows as one 5-D map like the routed experts' (one
+  // 16 KiB box per stage instead of eight 2 KiB ones) when the two tensors'
+  // distance is a legal stride; the half at the lower address comes first.
+  int sh5 = 0, sh_swap = 0;
+  {
+    const char* g = reinterpret_cast<const char*>(w_sh_gate);
+    const char* u = reinterpret_cast<const char*>(w_sh_up);
+    const uint64_t dist = uint64_t(u > g ? u - g : g - u);
+    if (dist != 0 && dist % 16 == 0 && dist < (uint64_t(1) << 40) && Is % 64 == 0) {
+      const uint64_t sh_dims[5] = {H, 16, 2, Is / 16, 1};
+      const uint64_t sh_strides[4] = {H * 2, dist, 16 * H * 2, Is * H * 2};
+      CUtensorMap m;
+      if (make_tmap_bf16_nd(&m, u > g ? g : u, 5, sh_dims, sh_strides, gu_box)) {
+        tm_sg = m;
+        sh5 = 1;
+        sh_swap = u < g ? 1 : 0;
+      }
+    }
+  }
+  TileTables gu{ws.gu_tiles, ws.tile_counts, ws.pair_dst, ws.pair_w, RowsOut{}, d.T, d.K,
+                sh5, sh_swap};
+  TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w,
+                rows_out ? *rows_out : RowsOut{}, d.T, d.K, 0, 0};
   err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, gu, d.H, d.E, d.I, d.Is,
                               d.ldh, ws.h, ws.rows_bf16, status);
   if (err != cudaSuccess) return err;
@@ -811,6 +911,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   if (err != cudaSuccess) return err;
   err = mark(2);
   if (err != cudaSuccess) return err;
+  if (rows_out && rows_out->world > 0) return cudaSuccess;  // the token owners combine
   const long n8 = long(T) * d.H / 8;
   const int* pp = world > 1 ? ws.pair_pos : nullptr;
   if (d.K <= kCombineMaxK && d.H / 8 <= 256) {
@@ -818,13 +919,29 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
     const unsigned blocks = unsigned(std::min<long>(T, long(2 * g_pairs) * 4));  // one wave
     combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(
         ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
-        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y);
+        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y, 0, d.T);
     return cudaGetLastError();
   }
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
       ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
       with_routed, d.sh_lo, d.sh_hi, world > 1 ? ws.pair_pos : nullptr, ws.tile_counts + 4,
       resid, y);
+  return cudaGetLastError();
+}
+
+// Combine of tokens [t_lo, t_hi) from a complete token-major rows buffer
+// (every routed expert and the shared expert), y indexed by token.
+cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
+                                 const float* topk_w, const float* shared_gate, int T, int H,
+                                 int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
+                                 cudaStream_t st) {
+  if (K > kCombineMaxK || H / 8 > 256) return cudaErrorInvalidValue;
+  if (t_hi <= t_lo) return cudaSuccess;
+  const unsigned threads = unsigned((H / 8 + 31) / 32 * 32);
+  const unsigned blocks = unsigned(std::min<long>(t_hi - t_lo, long(2 * g_pairs) * 4));
+  combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(rows, topk_idx, topk_w, shared_gate, T, H,
+                                                      K, 0, E, 1, 1, 0, T, nullptr, nullptr,
+                                                      nullptr, y, t_lo, t_hi);
   return cudaGetLastError();
 }
 

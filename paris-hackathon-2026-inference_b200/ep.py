@@ -112,9 +112,13 @@ class EPGroup:
         self.lib = _lib.load()
         self.local_buf = None
         self.peer_ptrs = None
-        self.rx_local = None    # row-split partial buffers (prefill), allocated on first use
+        self.rx_local = None    # row-split exchange buffers (prefill), allocated on first use
         self.rx_tmax = 0
         self.rx_epoch = 0
+        # prefill exchange: "rows" (the down GEMM stores rows at their token
+        # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
+        # outputs summed by pmoe_rows_allreduce)
+        self.prefill = "rows"
         if mode == "fused" and self.world > 1:
             nbytes = ctypes.c_size_t(0)
             _lib.check("pmoe_ep_buffer_bytes",
@@ -144,8 +148,11 @@ class EPGroup:
         return self.peer_ptrs is not None and T <= min(self.t_max, FUSED_MAX_T)
 
     def forward(self, x: torch.Tensor, weights, flags: int = 3,
-                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
-        """y[T,H] (full output on every rank) for replicated x[T,H]."""
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                events=None):
+        """y[T,H] (full output on every rank) for replicated x[T,H].  `events`
+        (5 CUDA event handles, as pmoe_block_forward_profiled takes) are recorded
+        between the phases of a fused prefill call and ignored otherwise."""
         T, H = x.shape
         w = list(weights)
         I, Is = w[1].shape[1] // 2, w[4].shape[0]
@@ -169,7 +176,7 @@ class EPGroup:
             _lib.check("pmoe_block_forward_ep", s)
             return y
         if self.mode == "fused" and self.world > 1:
-            return self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st)
+            return self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st, events)
         if self.mode == "a2a" and self.world > 1:
             return self._forward_a2a(x, w, I, Is, y)
         s = self.lib.pmoe_block_forward_ep(
@@ -180,16 +187,27 @@ class EPGroup:
             dist.all_reduce(y, group=self.group)
         return y
 
-    def _forward_rows(self, x, wp, I, Is, flags, y, ws, nbytes, st):
+    def _forward_rows(self, x, wp, I, Is, flags, y, ws, nbytes, st, events=None):
         """Prefill-sized batches: every rank routes all tokens (the same kernel,
         identical results; routing a slice per rank and all-gathering it was
         slower: the tensor-core router is latency-bound per 128-token CTA),
-        computes its row-balanced share of the dispatched rows
-        (pmoe_block_forward_rows) into its NVLink exchange buffer, and
-        pmoe_rows_allreduce sums the partials (deterministic, fp32) into y."""
+        computes its row-balanced share of the dispatched rows.  prefill "rows":
+        the down GEMM stores each row at the rank owning its token, which
+        combines its token slice locally and all ranks gather the slices
+        (pmoe_block_forward_rows_fused; y bit-identical to one GPU).  prefill
+        "partial": each rank's partial output (pmoe_block_forward_rows) goes to
+        its exchange buffer and pmoe_rows_allreduce sums the partials
+        (deterministic, fp32) into y."""
         T, H = x.shape
         self._rows_buffers(T)
         self.rx_epoch += 1
+        if self.prefill == "rows" and (flags & 3) == 3:
+            ev, nev = (events, 5) if events is not None else (None, 0)
+            _lib.check("pmoe_block_forward_rows_fused", self.lib.pmoe_block_forward_rows_fused(
+                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.rank, self.world,
+                self.rx_arr, self.rx_tmax, self.rx_epoch, flags, y.data_ptr(), ws.data_ptr(),
+                nbytes, st, ev, nev))
+            return y
         part = ctypes.c_void_p()
         _lib.check("pmoe_rows_partial", self.lib.pmoe_rows_partial(
             self.rx_local, self.rx_tmax, H, self.rx_epoch, ctypes.byref(part)))
@@ -257,8 +275,8 @@ class EPGroup:
             return
         self._close_rows()
         nb = ctypes.c_size_t(0)
-        _lib.check("pmoe_rows_buffer_bytes",
-                   self.lib.pmoe_rows_buffer_bytes(T, self.H, ctypes.byref(nb)))
+        _lib.check("pmoe_rows_fused_buffer_bytes",
+                   self.lib.pmoe_rows_fused_buffer_bytes(T, self.H, self.K, ctypes.byref(nb)))
         ptr = ctypes.c_void_p()
         _lib.check("pmoe_ipc_alloc", self.lib.pmoe_ipc_alloc(nb.value, ctypes.byref(ptr)))
         self.rx_local, self.rx_tmax, self.rx_epoch = ptr.value, T, 0

@@ -185,3 +185,42 @@ def test_block_prefill_zipf_tc():
     rows.sort()
     assert_close(y.float().cpu().numpy()[rows], oracle_y(x, wts, route=route, rows=rows),
                  "tc T=8192 sample")
+
+
+@pytest.mark.parametrize("up_first", [False, True])
+def test_block_prefill_shared_weights_adjacent(up_first):
+    """Shared gate and up weights that lie in one buffer (either one first) take
+    the single 5-D tensor-map load of the shared expert; the result equals the
+    one with separately allocated tensors bit for bit."""
+    from paris_moe_b200 import ops, workload as W
+    S = W.MoEShape()
+    g = W.make_weights(S, seed=3).to("cuda")
+    x = W.make_hidden(1024, S, seed=3).cuda()
+    ref = block(x, g)
+    pair = torch.empty((2, S.Is, S.H), dtype=torch.bfloat16, device="cuda")
+    gate, up = (pair[1], pair[0]) if up_first else (pair[0], pair[1])
+    gate.copy_(g.w_sh_gate)
+    up.copy_(g.w_sh_up)
+    t = list(g.tensors())
+    t[3], t[4] = gate, up
+    y = ops.moe_block(x, *t, S.K, 0, S.E, F_SH | F_RT)
+    assert torch.equal(y, ref)
+    wc = W.make_weights(S, seed=3)
+    rows = np.arange(0, 1024, 16)
+    assert_close(y.float().cpu().numpy()[rows],
+                 oracle_y(x.cpu(), wc, route=route_of(x, g), rows=rows), "shared adjacent")
+
+
+def test_block_prefill_shared_gate_is_up():
+    """Shared gate and up passed as one tensor (distance 0, no 5-D map): the
+    eight 2-D loads per stage give the same bits as two separate copies."""
+    from paris_moe_b200 import ops, workload as W
+    S = W.MoEShape()
+    g = W.make_weights(S, seed=4).to("cuda")
+    x = W.make_hidden(512, S, seed=4).cuda()
+    t = list(g.tensors())
+    t[4] = t[3]
+    same = ops.moe_block(x, *t, S.K, 0, S.E, F_SH | F_RT)
+    t[4] = t[3].clone()
+    apart = ops.moe_block(x, *t, S.K, 0, S.E, F_SH | F_RT)
+    assert torch.equal(same, apart)

@@ -142,3 +142,35 @@ def test_row_split_partials_sum_to_full(world):
                                            ws.data_ptr(), n, st) == 0
         total2 += y.float()
     assert torch.equal(total2, total)
+
+
+def test_rows_fused_missing_peer_times_out():
+    """The fused row exchange for 2 ranks where rank 1 never runs: rank 0's
+    waits for rank 1's flags give up after their bounded budget and leave
+    status 4 (peer timeout) in its buffer; the GPU context stays usable."""
+    from paris_moe_b200 import _lib, ops, workload as W
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=128, Is=128)
+    wts = W.make_weights(S, seed=2, device="cuda")
+    T = 200
+    x = W.make_hidden(T, S, seed=2, device="cuda")
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_rows_fused_buffer_bytes(T, S.H, S.K, ctypes.byref(nb)) == 0
+    bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    arr = (ctypes.c_void_p * 2)(*[b.data_ptr() for b in bufs])
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    ws = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    y = torch.empty_like(x)
+    t0 = time.time()
+    assert lib.pmoe_block_forward_rows_fused(
+        x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *[t.data_ptr() for t in wts.tensors()], 0, 2,
+        arr, T, 1, 3, y.data_ptr(), ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream,
+        None, 0) == 0
+    torch.cuda.synchronize()
+    status = ctypes.c_int(-1)
+    assert lib.pmoe_rows_status(bufs[0].data_ptr(), ctypes.byref(status)) == 0
+    assert status.value == 4
+    assert time.time() - t0 < 60
+    z = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
+    torch.cuda.synchronize()
+    assert torch.isfinite(z.float()).all()
