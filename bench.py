@@ -531,7 +531,7 @@ def main():
               "layer_tflops": flops / (pms * 1e-3) / 1e12,
               "layer_frac": flops / (pms * 1e-3) / 1e12 / peaks["bf16_tflops"],
               # router_tc, scan, scatter, plan, row copy, gate_up, down, combine per step;
-              # N > 1 adds publish, wait, publish, gather around the slice combine
+              # N > 1: publish, wait, publish, wait around the slice combine (+ a copy)
               "gpu_launches": (8 if c.world == 1 else 12) * psteps, "clocks": pclk,
               "e2e": pre.e2e(max(5, min(a.steps, 50)))}
         if pphase is not None and c.world > 1:   # rank 0's phases

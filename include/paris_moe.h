@@ -211,8 +211,8 @@ int pmoe_rows_status(const void* own_buf, int* status);
  * pmoe_block_forward_rows; the down GEMM stores each unweighted output row
  * straight into the buffer of the rank that owns its token (token slice
  * [r*T/world, (r+1)*T/world)) with NVLink peer stores; each rank then combines
- * its slice locally, in the single-GPU order, and every rank gathers the
- * slices.  y is the full output on every rank, bit-identical to the
+ * its slice locally, in the single-GPU order, storing the result into every
+ * rank's buffer, and copies the completed output into y.  y is the full output on every rank, bit-identical to the
  * single-GPU pmoe_block_forward.  bufs[q]: rank q's buffer of
  * pmoe_rows_fused_buffer_bytes(T_max, H, K) (pmoe_ipc_alloc'ed, zeroed,
  * mapped on every rank); epoch > 0, +1 per call, the same on every rank.

@@ -35,7 +35,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
 cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
                                  const float* topk_w, const float* shared_gate, int T, int H,
                                  int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
-                                 cudaStream_t st);
+                                 const RowsOut* ydst, cudaStream_t st);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch).

@@ -183,13 +183,14 @@ cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int r
 //   publish  flagsA[rank] = e on every rank (this rank's rows are delivered)
 //   wait     (bounded) for every rank's flagsA
 //   combine  this rank's token slice from its own rows region, in the
-//            single-GPU order (routed k = 0..K-1, then shared), into its
-//            reduced region
+//            single-GPU order (routed k = 0..K-1, then shared), stored into
+//            the slice region of every rank (peer stores)
 //   publish  flagsB[rank] = e on every rank
-//   gather   as above.
-// Parity safety is the argument above: a rank writes rows of call e+2 into
-// the region of call e only after its gather of e+1, which follows every
-// rank's combine of e+1 and so of e.
+//   wait     (bounded) for every rank's flagsB
+//   copy     this rank's slice region (now all T rows) into y.
+// Parity safety: a rank writes rows or slices of call e+2 into a region of
+// call e only after its wait for flagsA of e+2, which every rank raises after
+// its copy of e+1, which follows its own reads of call e.
 static size_t rx_rows_region(int T_max, int H, int K) {
   return (size_t(T_max) * (K + 1) * H * 2 + 255) / 256 * 256;
 }
@@ -217,13 +218,21 @@ cudaError_t launch_rows_fused_tail(void* const* bufs, int T_max, int world, int 
       own + rx_fused_rows_offset(T_max, H, K, epoch));
   auto* reduced = reinterpret_cast<__nv_bfloat16*>(own + rx_region_offset(T_max, H, epoch));
   const int t0 = int(long(rank) * T / world), t1 = int(long(rank + 1) * T / world);
+  RowsOut ydst{};
+  ydst.world = world;
+  for (int q = 0; q < world; ++q)
+    ydst.base[q] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(bufs[q]) +
+                                                     rx_region_offset(T_max, H, epoch));
+  (void)num_sms;
   rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
   rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
   cudaError_t e = launch_combine_slice(rows, topk_idx, topk_w, shared_gate, T, H, E, K, t0, t1,
-                                       reduced, st);
+                                       reduced, &ydst, st);
   if (e != cudaSuccess) return e;
   rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsB);
-  rx_gather_kernel<<<num_sms * 4, kRxThreads, 0, st>>>(p, T, H, y);
+  rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsB);
+  e = cudaMemcpyAsync(y, reduced, size_t(T) * H * 2, cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -713,7 +713,9 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
     int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
     const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ row_range,
     const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y, int t_lo,
-    int t_hi) {
+    int t_hi, const __grid_constant__ RowsOut ydst) {
+  // ydst.world > 0: each output row goes to row t of every rank's buffer
+  // ydst.base[0..world) (peer stores) instead of y.
   const int cols8 = H / 8, c8 = threadIdx.x;
   const bool act = c8 < cols8;
   const int p_lo = pair_pos ? row_range[0] : 0, p_hi = pair_pos ? row_range[1] : 0;
@@ -766,7 +768,12 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
         __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
         op[j] = *reinterpret_cast<uint32_t*>(&b2);
       }
-      reinterpret_cast<uint4*>(y + size_t(t) * H)[c8] = o;
+      if (ydst.world > 0) {
+        for (int q = 0; q < ydst.world; ++q)
+          reinterpret_cast<uint4*>(ydst.base[q] + size_t(t) * H)[c8] = o;
+      } else {
+        reinterpret_cast<uint4*>(y + size_t(t) * H)[c8] = o;
+      }
     }
     mask = mask_n;
 #pragma unroll
@@ -919,7 +926,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
     const unsigned blocks = unsigned(std::min<long>(T, long(2 * g_pairs) * 4));  // one wave
     combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(
         ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
-        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y, 0, d.T);
+        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y, 0, d.T, RowsOut{});
     return cudaGetLastError();
   }
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
@@ -934,14 +941,15 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
 cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
                                  const float* topk_w, const float* shared_gate, int T, int H,
                                  int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
-                                 cudaStream_t st) {
+                                 const RowsOut* ydst, cudaStream_t st) {
   if (K > kCombineMaxK || H / 8 > 256) return cudaErrorInvalidValue;
   if (t_hi <= t_lo) return cudaSuccess;
   const unsigned threads = unsigned((H / 8 + 31) / 32 * 32);
   const unsigned blocks = unsigned(std::min<long>(t_hi - t_lo, long(2 * g_pairs) * 4));
   combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(rows, topk_idx, topk_w, shared_gate, T, H,
                                                       K, 0, E, 1, 1, 0, T, nullptr, nullptr,
-                                                      nullptr, y, t_lo, t_hi);
+                                                      nullptr, y, t_lo, t_hi,
+                                                      ydst ? *ydst : RowsOut{});
   return cudaGetLastError();
 }
 
