@@ -1,14 +1,18 @@
 // Prefill routing (large T): tcgen05 router GEMM with top-k in the epilogue,
 // then a parallel stable CSR dispatch.
 //
-//   router_tc_kernel   one CTA per 128-token tile: logits = x . W_r^T on the
-//                      tensor cores (M=128 tokens, N=256 experts) plus the
-//                      shared-expert gate as a second N=16 MMA whose B tile
-//                      is w_sh_gvec with TMA zero-filling rows 1..15.  The
-//                      epilogue (one token per thread) rounds each logit to
-//                      bf16, keeps the top K keys in registers (ties -> lower
-//                      expert), renormalises, and writes the tile's
-//                      per-expert histogram.
+//   router_tc_kernel   a cluster of two CTAs per 128-token tile, CTA h on
+//                      experts [128h, 128h+128): logits = x . W_r^T on the
+//                      tensor cores (M=128 tokens, N=128 experts; CTA 0 also
+//                      the shared-expert gate as an N=16 MMA whose B tile is
+//                      w_sh_gvec with TMA zero-filling rows 1..15).  Each
+//                      epilogue thread (one token) rounds its logits to bf16
+//                      and keeps its top K keys in registers (ties -> lower
+//                      expert); CTA 0 merges the peer's keys through
+//                      distributed shared memory, renormalises, and writes the
+//                      tile's per-expert histogram.  (One CTA per tile on all
+//                      256 experts left 84 SMs idle at T=8192 and ran 64 %
+//                      tensor-busy on the rest.)
 //   route_scan_kernel  one CTA: per-expert counts, CSR offsets, active list
 //                      and, per (tile, expert), the first output slot.
 //   route_scatter_kernel  one CTA per tile: stable ranks of the tile's pairs
@@ -23,12 +27,14 @@
 namespace pmoe {
 
 constexpr int kRtM = 128, kRtN = 256, kRtN2 = 16, kRtK = 64;
-constexpr int kRtStages = 4;
-constexpr int kRtA = kRtM * kRtK * 2;     // 16 KiB
-constexpr int kRtB = kRtN * kRtK * 2;     // 32 KiB
-constexpr int kRtB2 = kRtN2 * kRtK * 2;   // 2 KiB
+constexpr int kRtNH = kRtN / 2;            // experts per CTA of the pair
+constexpr int kRtStages = 6;
+constexpr int kRtA = kRtM * kRtK * 2;      // 16 KiB
+constexpr int kRtB = kRtNH * kRtK * 2;     // 16 KiB
+constexpr int kRtB2 = kRtN2 * kRtK * 2;    // 2 KiB
 constexpr int kRtStageBytes = kRtA + kRtB + kRtB2;
 constexpr int kRtSmem = kRtStages * kRtStageBytes + 1024 + 256;
+static_assert(kRtSmem <= 227 * 1024, "router shared memory");
 constexpr int kRtThreads = 6 * 32;
 constexpr int kRtMaxK = 8;
 static_assert(kRtStageBytes % 1024 == 0, "stage alignment");
@@ -45,6 +51,15 @@ __device__ __forceinline__ float rt_value(uint32_t key) {
   return __uint_as_float(b << 16);
 }
 
+__device__ __forceinline__ uint4 ld_shared_cluster_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
     const __grid_constant__ CUtensorMap tm_g, int T, int H, int E, int K,
@@ -58,8 +73,11 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   uint64_t* tfull = empty + kRtStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
   __shared__ int s_hist[256];
+  __shared__ __align__(16) uint32_t s_top[kRtM][kRtMaxK];  // this CTA's keys per token
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * kRtM;
+  const uint32_t h = cluster_ctarank();  // expert half
+  const int t0 = (blockIdx.x >> 1) * kRtM;
+  const int e0 = int(h) * kRtNH;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
       mbar_init(&full[s], 1);
@@ -70,7 +88,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   }
   for (int i = threadIdx.x; i < 256; i += kRtThreads) s_hist[i] = 0;
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -81,6 +99,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
 
   if (warp == 0) {
     if (lane == 0) {
+      const uint32_t tx = h == 0 ? kRtStageBytes : kRtA + kRtB;
       for (int kc = 0; kc < nk; ++kc) {
         const int s = kc % kRtStages;
         if (kc >= kRtStages && !mbar_wait(&empty[s], ((kc / kRtStages) & 1) ^ 1)) {
@@ -88,15 +107,15 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
           break;
         }
         uint8_t* sa = smem + s * kRtStageBytes;
-        mbar_arrive_expect_tx(&full[s], kRtStageBytes);
+        mbar_arrive_expect_tx(&full[s], tx);
         tma_load_2d(sa, &tm_x, kc * kRtK, t0, &full[s]);
-        tma_load_2d(sa + kRtA, &tm_w, kc * kRtK, 0, &full[s]);
-        tma_load_2d(sa + kRtA + kRtB, &tm_g, kc * kRtK, 0, &full[s]);
+        tma_load_2d(sa + kRtA, &tm_w, kc * kRtK, e0, &full[s]);  // rows >= E read as zero
+        if (h == 0) tma_load_2d(sa + kRtA + kRtB, &tm_g, kc * kRtK, 0, &full[s]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t id1 = idesc_bf16_f32(kRtM, kRtN), id2 = idesc_bf16_f32(kRtM, kRtN2);
+      const uint32_t id1 = idesc_bf16_f32(kRtM, kRtNH), id2 = idesc_bf16_f32(kRtM, kRtN2);
       const uint32_t sb0 = smem_u32(smem);
       bool ok = true;
       for (int kc = 0; kc < nk; ++kc) {
@@ -114,31 +133,34 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
         for (int kk = 0; kk < kRtK / 16; ++kk) {
           const uint32_t acc = (kc | kk) != 0 ? 1u : 0u;
           umma_bf16(tmem_base, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), id1, acc);
-          umma_bf16(tmem_base + kRtN, ad + uint64_t(kk * 2), gd + uint64_t(kk * 2), id2, acc);
+          if (h == 0)
+            umma_bf16(tmem_base + kRtNH, ad + uint64_t(kk * 2), gd + uint64_t(kk * 2), id2, acc);
         }
         umma_commit(&empty[s]);
       }
       if (ok) umma_commit(tfull);
     }
-  } else {
-    // epilogue: warps 2..5, one token row per thread
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const int t = t0 + r;
+  }
+  // epilogue warps 2..5: one token row per thread, the top keys of this half
+  const int q = warp & 3;
+  const int r = q * 32 + lane;
+  const int t = t0 + r;
+  float gate_logit = 0.f;
+  if (warp >= 2) {
+    uint32_t top[kRtMaxK];
+#pragma unroll
+    for (int k = 0; k < kRtMaxK; ++k) top[k] = 0u;
     if (mbar_wait(tfull, 0)) {
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16);
-      uint32_t top[kRtMaxK];
-#pragma unroll
-      for (int k = 0; k < kRtMaxK; ++k) top[k] = 0u;
 #pragma unroll 1
-      for (int cc = 0; cc < kRtN / 32; ++cc) {
+      for (int cc = 0; cc < kRtNH / 32; ++cc) {
         uint32_t v[32];
         tmem_ld32(taddr + cc * 32, v);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int e = cc * 32 + i;
+          const int e = e0 + cc * 32 + i;
           if (e < E) {
             const uint32_t key = rt_key(bf16_round(__uint_as_float(v[i])), e);
             if (key > top[kRtMaxK - 1]) {
@@ -155,40 +177,74 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
           }
         }
       }
-      uint32_t gv[32];
-      tmem_ld32(taddr + kRtN, gv);
-      tmem_ld_wait();
-      if (t < T) {
-        const float l0 = rt_value(top[0]);
-        float ex[kRtMaxK], den = 0.f;
-#pragma unroll
-        for (int k = 0; k < kRtMaxK; ++k) {
-          ex[k] = k < K ? __expf(rt_value(top[k]) - l0) : 0.f;
-          den += ex[k];
-        }
-        const float inv = 1.0f / den;
-#pragma unroll
-        for (int k = 0; k < kRtMaxK; ++k) {
-          if (k < K) {
-            const int e = 0xFFFF - int(top[k] & 0xFFFFu);
-            topk_idx[size_t(t) * K + k] = e;
-            topk_w[size_t(t) * K + k] = ex[k] * inv;
-            atomicAdd(&s_hist[e], 1);
-          }
-        }
-        shared_gate[t] = 1.0f / (1.0f + __expf(-__uint_as_float(gv[0])));
+      if (h == 0) {
+        uint32_t gv[32];
+        tmem_ld32(taddr + kRtNH, gv);
+        tmem_ld_wait();
+        gate_logit = __uint_as_float(gv[0]);
       }
     } else {
       atomicCAS(status, 0, kStatusTimeoutTmem);
     }
+#pragma unroll
+    for (int k = 0; k < kRtMaxK; ++k) s_top[r][k] = top[k];
   }
   __syncwarp();
   tc_fence_before();
+  cluster_sync_all();  // both halves' keys are in shared memory
+  if (h == 0 && warp >= 2) {
+    // merge: the peer's keys inserted into this half's descending list (keys
+    // are unique: they hold the expert index)
+    uint32_t b[kRtMaxK], top[kRtMaxK];
+    const uint32_t peer = mapa_shared(smem_u32(&s_top[r][0]), 1);
+    const uint4 b0 = ld_shared_cluster_v4(peer), b1 = ld_shared_cluster_v4(peer + 16);
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+    b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+#pragma unroll
+    for (int k = 0; k < kRtMaxK; ++k) top[k] = s_top[r][k];
+#pragma unroll
+    for (int j = 0; j < kRtMaxK; ++j) {
+      if (b[j] > top[kRtMaxK - 1]) {
+        top[kRtMaxK - 1] = b[j];
+#pragma unroll
+        for (int k = kRtMaxK - 1; k > 0; --k) {
+          if (top[k] > top[k - 1]) {
+            const uint32_t tmp = top[k];
+            top[k] = top[k - 1];
+            top[k - 1] = tmp;
+          }
+        }
+      }
+    }
+    if (t < T) {
+      const float l0 = rt_value(top[0]);
+      float ex[kRtMaxK], den = 0.f;
+#pragma unroll
+      for (int k = 0; k < kRtMaxK; ++k) {
+        ex[k] = k < K ? __expf(rt_value(top[k]) - l0) : 0.f;
+        den += ex[k];
+      }
+      const float inv = 1.0f / den;
+#pragma unroll
+      for (int k = 0; k < kRtMaxK; ++k) {
+        if (k < K) {
+          const int e = 0xFFFF - int(top[k] & 0xFFFFu);
+          topk_idx[size_t(t) * K + k] = e;
+          topk_w[size_t(t) * K + k] = ex[k] * inv;
+          atomicAdd(&s_hist[e], 1);
+        }
+      }
+      shared_gate[t] = 1.0f / (1.0f + __expf(-gate_logit));
+    }
+  }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += kRtThreads) hist[size_t(blockIdx.x) * E + e] = s_hist[e];
+  if (h == 0)
+    for (int e = threadIdx.x; e < E; e += kRtThreads)
+      hist[size_t(blockIdx.x >> 1) * E + e] = s_hist[e];
+  cluster_sync_all();  // the peer has read this CTA's keys
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, 256);
   }
 }
 
@@ -345,13 +401,24 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
   CUtensorMap tm_x, tm_w, tm_g;
   const uint64_t H = d.H;
   if (!make_tmap_bf16_2d(&tm_x, x, H, d.T, H * 2, kRtK, kRtM) ||
-      !make_tmap_bf16_2d(&tm_w, w_router, H, d.E, H * 2, kRtK, kRtN) ||
+      !make_tmap_bf16_2d(&tm_w, w_router, H, d.E, H * 2, kRtK, kRtNH) ||
       !make_tmap_bf16_2d(&tm_g, w_gvec, H, 1, H * 2, kRtK, kRtN2))
     return cudaErrorInvalidValue;
   const int nb = (d.T + kRtM - 1) / kRtM;
-  router_tc_kernel<<<nb, kRtThreads, kRtSmem, st>>>(tm_x, tm_w, tm_g, d.T, d.H, d.E, d.K,
-                                                    topk_idx, topk_w, shared_gate, hist, status);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * nb);
+  cfg.blockDim = dim3(kRtThreads);
+  cfg.dynamicSmemBytes = kRtSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, router_tc_kernel, tm_x, tm_w, tm_g, int(d.T), int(d.H),
+                            int(d.E), int(d.K), topk_idx, topk_w, shared_gate, hist, status);
 }
 
 // Scan + scatter from the routing in ws.topk_idx / topk_w / shared_gate and
