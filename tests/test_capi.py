@@ -75,3 +75,37 @@ def test_forward_rejects_bad_args_before_touching_gpu(lib):
     st = lib.pmoe_block_forward(null, 4, 2048, 256, 8, 512, 512, *([null] * 7), 0, 256, 64,
                                 null, null, 0, null)
     assert st == -1       # unknown flag
+
+
+def test_rows_fused_buffer_layout(lib):
+    """The fused row-exchange buffer is the partial-sum buffer (header + two
+    T_max x H bf16 slice regions) followed by two regions of T_max*(K+1) rows."""
+    def r256(n):
+        return (n + 255) // 256 * 256
+    T, H, K = 8192, 2048, 8
+    a, b = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert lib.pmoe_rows_buffer_bytes(T, H, ctypes.byref(a)) == 0
+    assert lib.pmoe_rows_fused_buffer_bytes(T, H, K, ctypes.byref(b)) == 0
+    assert a.value == 1024 + 2 * r256(T * H * 2)
+    assert b.value == a.value + 2 * r256(T * (K + 1) * H * 2)
+    assert lib.pmoe_rows_fused_buffer_bytes(T, H, 0, ctypes.byref(b)) == -1
+    assert lib.pmoe_rows_fused_buffer_bytes(T, 2047, K, ctypes.byref(b)) == -1
+    assert lib.pmoe_rows_fused_buffer_bytes(0, H, K, ctypes.byref(b)) == -1
+
+
+def test_rows_fused_rejects_bad_args_before_touching_gpu(lib):
+    null = None
+    fake = (ctypes.c_void_p * 2)(0x10000, 0x20000)   # never dereferenced: checks fail first
+
+    def call(bufs=fake, rank=0, world=2, T=4, T_max=4, epoch=1, flags=3, x=null):
+        return lib.pmoe_block_forward_rows_fused(
+            x, T, 2048, 256, 8, 512, 512, *([null] * 7), rank, world, bufs, T_max, epoch, flags,
+            null, null, 0, null, null, 0)
+    assert call(bufs=None) == -1
+    assert call(rank=2) == -1
+    assert call(world=9) == -1
+    assert call(epoch=0) == -1
+    assert call(T=8, T_max=4) == -1
+    assert call(flags=2) == -1          # the slice combine needs routed and shared rows
+    assert call() == -1                 # null x / weights / y / workspace
+    assert call(T=0) == 0               # empty batch: no-op
