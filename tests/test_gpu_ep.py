@@ -174,3 +174,34 @@ def test_rows_fused_missing_peer_times_out():
     z = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
     torch.cuda.synchronize()
     assert torch.isfinite(z.float()).all()
+
+
+@pytest.mark.parametrize("T", [200, 1000])
+def test_rows_fused_single_rank_matches_block(T):
+    """The fused row exchange with world = 1 runs all of its kernels on one GPU
+    (down-GEMM stores to the owner's buffer, both flag rounds, the slice
+    combine's push, the final copy): y equals pmoe_block_forward bit for bit,
+    for two calls (both buffer parities)."""
+    from paris_moe_b200 import _lib, ops, workload as W
+    lib = _lib.load()
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=6, device="cuda", zipf_s=1.1)
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_rows_fused_buffer_bytes(T, S.H, S.K, ctypes.byref(nb)) == 0
+    buf = torch.zeros(nb.value, dtype=torch.uint8, device="cuda")
+    arr = (ctypes.c_void_p * 1)(buf.data_ptr())
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for epoch in (1, 2):
+        x = W.make_hidden(T, S, seed=30 + epoch, device="cuda", zipf=True)
+        ref = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
+        y = torch.empty_like(x)
+        assert lib.pmoe_block_forward_rows_fused(
+            x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *[t.data_ptr() for t in wts.tensors()],
+            0, 1, arr, T, epoch, 3, y.data_ptr(), ws.data_ptr(), n, st, None, 0) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+    status = ctypes.c_int(-1)
+    assert lib.pmoe_rows_status(buf.data_ptr(), ctypes.byref(status)) == 0
+    assert status.value == 0
