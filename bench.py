@@ -31,10 +31,12 @@ Multi-GPU (N>1, one process per GPU under torch.distributed.run): expert
 parallel, strong scaling over the same tokens.  Decode: contiguous expert
 ranges by rank (engine/runtime/ep.py:78-86), the weighted expert rows cross
 NVLink from the down-projection epilogue (no collective kernel).  Prefill:
-sliced routing + one all_gather, a row-balanced share of the dispatched rows
-per rank, partials summed over NVLink.  ``comparators`` (decode and prefill)
-times the same call with the reference's NCCL all_reduce exchange and with a
-token-dispatch all_to_all_single exchange.
+every rank routes all tokens, computes a cost-balanced run of the dispatched
+rows, and its down GEMM stores each row at the rank owning the row's token
+over NVLink; each rank combines its token slice and pushes it to every rank.
+``comparators`` (decode and prefill) times the same call with the
+reference's NCCL all_reduce exchange and with a token-dispatch
+all_to_all_single exchange.
 """
 from __future__ import annotations
 
@@ -42,7 +44,6 @@ import argparse
 import importlib.util
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -70,16 +71,6 @@ def measured_peaks():
     if os.path.exists(p):
         return json.load(open(p)), "measured"
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
-
-
-def profiled_traffic(name: str):
-    """DRAM bytes per launch of a kernel from its committed ncu summary
-    (a line `traffic_bytes_per_launch: N` in profiles/<name>.md), or None."""
-    p = os.path.join(ROOT, "profiles", f"{name}.md")
-    if not os.path.exists(p):
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(p).read())
-    return int(m.group(1)) if m else None
 
 
 # ------------------------------------------------------------------ clocks --
@@ -142,16 +133,26 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU baseline --
 
-def cpu_reference(weights_cpu, x_cpu, budget_s: float, max_steps: int | None = None):
-    """Time HF's Qwen3_5MoeSparseMoeBlock (grouped_mm, the HF default) on CPU."""
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def hf_cpu_block(weights_cpu, impl: str = "grouped_mm"):
+    """HF's Qwen3_5MoeSparseMoeBlock on the host, holding ``weights_cpu``."""
     import torch
     from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
     from transformers.models.qwen3_5_moe import modeling_qwen3_5_moe as M
     S = weights_cpu.shape
-    torch.set_num_threads(os.cpu_count())
     cfg = Qwen3_5MoeTextConfig(hidden_size=S.H, num_experts=S.E, num_experts_per_tok=S.K,
                                moe_intermediate_size=S.I, shared_expert_intermediate_size=S.Is)
-    cfg._experts_implementation = "grouped_mm"
+    cfg._experts_implementation = impl
     with torch.device("meta"):
         blk = M.Qwen3_5MoeSparseMoeBlock(cfg)
     blk = blk.to_empty(device="cpu").to(torch.bfloat16).eval()
@@ -163,24 +164,52 @@ def cpu_reference(weights_cpu, x_cpu, budget_s: float, max_steps: int | None = N
         blk.shared_expert.up_proj.weight.copy_(weights_cpu.w_sh_up)
         blk.shared_expert.down_proj.weight.copy_(weights_cpu.w_sh_down)
         blk.shared_expert_gate.weight.copy_(weights_cpu.w_sh_gvec)
+    return blk
+
+
+def cpu_reference(weights_cpu, x_cpu, budget_s: float, max_steps: int | None = None,
+                  impl: str = "grouped_mm", warmup: int = 2, min_steps: int = 10):
+    """Time HF's Qwen3_5MoeSparseMoeBlock (``impl``: grouped_mm, the HF default,
+    or eager) on all host cores: ``warmup`` untimed calls, then timed calls
+    until ``budget_s`` has passed and at least ``min_steps`` ran (or
+    ``max_steps``); the median call time gives tokens/s."""
+    import torch
+    torch.set_num_threads(os.cpu_count())
+    blk = hf_cpu_block(weights_cpu, impl)
     T = x_cpu.shape[0]
-    x3 = x_cpu.view(1, T, S.H)
+    x3 = x_cpu.view(1, T, weights_cpu.shape.H)
     times = []
     with torch.inference_mode():
-        for _ in range(2):
+        for _ in range(warmup):
             blk(x3)
         t_end = time.perf_counter() + budget_s
-        while time.perf_counter() < t_end and (max_steps is None or len(times) < max_steps):
+        while (max_steps is None or len(times) < max_steps) and \
+                (time.perf_counter() < t_end or len(times) < min_steps):
             t0 = time.perf_counter()
             blk(x3)
             times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": T / med, "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "reference",
+            "kind": "reference", "cpu_model": cpu_model(),
             "sample": f"HF transformers {__import__('transformers').__version__} "
-                      f"Qwen3_5MoeSparseMoeBlock grouped_mm on CPU, T={T}, "
-                      f"median of {len(times)} calls after 2 warm-ups",
-            "ms_per_call": med * 1e3, "calls": len(times)}
+                      f"Qwen3_5MoeSparseMoeBlock {impl} on CPU, T={T}, "
+                      f"median of {len(times)} calls after {warmup} warm-ups",
+            "ms_per_call": med * 1e3, "calls": len(times), "T": T, "impl": impl}
+
+
+def cpu_baseline_rows(wts_cpu, a):
+    """BASELINE's CPU plan: primary T=16 (config 1), extra rows T=64 (the GPU
+    headline's batch) and T=16 with HF's eager experts.  Bounded: each row
+    about ``a.cpu_budget`` seconds."""
+    from paris_moe_b200 import workload as W
+    x = W.make_hidden(64, wts_cpu.shape, seed=0)
+    prim = cpu_reference(wts_cpu, x[:16].clone(), a.cpu_budget)
+    rows = [cpu_reference(wts_cpu, x, a.cpu_budget),
+            cpu_reference(wts_cpu, x[:16].clone(), a.cpu_budget / 2, impl="eager", min_steps=5)]
+    out = {k: prim[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")}
+    out["rows"] = [{k: r[k] for k in ("T", "impl", "value", "ms_per_call", "calls")}
+                   for r in rows]
+    return out
 
 
 # ----------------------------------------------------------- GPU measuring --
@@ -505,7 +534,10 @@ def main():
         line["roofline"] = {"kernel": "gate_up_tma_kernel", "bound": "hbm", "achieved": ach,
                             "peak": peaks["hbm_gbs"], "unit": "GB/s",
                             "frac": ach / peaks["hbm_gbs"],
-                            "traffic": profiled_traffic("gate_up_tma_decode_T64"),
+                            # DRAM bytes come from ncu, which this run does not use;
+                            # the capture of this kernel is summarised in the file named
+                            "traffic": None,
+                            "traffic_profile": "profiles/gate_up_tma_decode_T64.md",
                             "algorithmic_bytes": gu_bytes, "avg_launch_ms": phase[1],
                             "peak_source": f"{peak_kind} (hbm_gbs)"}
     else:
@@ -544,8 +576,8 @@ def main():
             ach = gu_flops / (pphase[1] * 1e-3) / 1e12
             pl["roofline"] = {"kernel": "tc_pair_kernel<gate_up>", "bound": "tensor",
                               "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                              "frac": ach / peaks["bf16_tflops"], "traffic": profiled_traffic(
-                                  "tc_pair_gate_up_prefill_T8192"),
+                              "frac": ach / peaks["bf16_tflops"], "traffic": None,
+                              "traffic_profile": "profiles/tc_pair_gate_up_prefill_T8192.md",
                               "algorithmic_flops": gu_flops, "avg_launch_ms": pphase[1],
                               "peak_source": f"{peak_kind} (bf16_tflops, burst)"}
         if c.world > 1:
@@ -558,8 +590,17 @@ def main():
         line["stack"] = stack_bench(c, a, peaks, peak_kind)
 
     if world == 1 and rank == 0 and not a.no_cpu_baseline:
-        ref = cpu_reference(c.wts.to("cpu"), x.cpu(), budget_s=a.cpu_budget)
-        line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        wcpu = c.wts.to("cpu")
+        line["cpu_baseline"] = cpu_baseline_rows(wcpu, a)
+        if "prefill" in line:
+            # config 3 on the host: the T=8192 Zipf workload, a bounded sample
+            # of calls (each call is the whole layer)
+            wz = W.make_weights(S, seed=0, zipf_s=a.zipf)
+            xz = W.make_hidden(a.prefill_T, S, seed=0, zipf=True)
+            pr = cpu_reference(wz, xz, a.cpu_budget, warmup=1, min_steps=2, max_steps=5)
+            line["prefill"]["cpu_baseline"] = {
+                k: pr[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model",
+                                   "ms_per_call")}
     if rank == 0:
         print(json.dumps(line))
     if c.group is not None:

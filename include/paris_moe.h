@@ -64,7 +64,11 @@ int pmoe_workspace_size(int T, int H, int E, int K, int I, int Is, size_t* bytes
 
 /* Router + top-k + dispatch only.
  * Replaces Qwen3_5MoeTopKRouter.forward (modeling_qwen3_5_moe.py:762-770)
- * followed by moe_dispatch_indices (engine/kernels/moe_dispatch.py:178-209):
+ * followed by moe_dispatch_indices (engine/kernels/moe_dispatch.py:178-209).
+ * The bf16 logit of (token, expert) is the bf16 value nearest (ties to even)
+ * to the exact dot product of the bf16 operands; the selection is exact on
+ * those values (approximate tensor-core logits with a stated error bound,
+ * exact re-evaluation of the experts whose rounding the bound leaves open):
  *   topk_idx    [T, K] int32  experts by descending bf16 logit, ties -> lower index
  *   topk_w      [T, K] fp32   renormalised softmax weights
  *   offsets     [E+1]  int32  CSR offsets of the (token, slot) pairs by expert
@@ -77,6 +81,20 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K,
                int32_t* topk_idx, float* topk_w, int32_t* offsets,
                int32_t* sorted_tok, int32_t* sorted_slot, float* shared_gate,
                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostics of the exact top-k (testing): runs the routing of pmoe_route
+ * and returns, besides topk_idx / topk_w, the router GEMM's fp32
+ * approximate logits logits[T][Rpad] (Rpad = E + 1 rounded up to 16; column
+ * E is the shared-expert gate sum), the bound factor *gamma of that path (the
+ * top-k treats |approx - exact| <= gamma * ||x_t|| * ||w_e|| as given) and
+ * stats[0] = experts evaluated exactly, stats[1] = of which outside the
+ * exactness condition of the double-double sum (expected 0).  stats is host
+ * memory; the call synchronises the stream.  No counterpart in the reference
+ * (test infrastructure for the exact selection). */
+int pmoe_route_diag(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_router,
+                    const uint16_t* w_sh_gvec, int32_t* topk_idx, float* topk_w, float* logits,
+                    float* gamma, int32_t* stats, void* workspace, size_t workspace_bytes,
+                    void* stream);
 
 /* The whole MoE block, y[T,H] (bf16) =
  *     sum_k w_tk * down_e(SiLU(gate_e x) * up_e x)          (PMOE_F_ROUTED, e in [lo,hi))
@@ -203,6 +221,17 @@ int pmoe_rows_partial(void* own_buf, int T_max, int H, int epoch, void** partial
 int pmoe_rows_allreduce(void* const* bufs, int T_max, int T, int H, int rank, int world,
                         int epoch, uint16_t* y, void* stream);
 int pmoe_rows_status(const void* own_buf, int* status);
+
+/* Asynchronous reads of the sticky status words of the exchange buffers, for
+ * an engine that checks a peer loss at its next call instead of blocking: the
+ * word (0 ok, 4 a wait on a peer gave up in some earlier call; only a fresh,
+ * zeroed buffer clears it) is copied to dst (pinned host or device memory) in
+ * stream order.  own_buf: this rank's buffer of pmoe_block_forward_ep /
+ * pmoe_layer_forward (pmoe_ep_status_async) or of the row exchanges
+ * (pmoe_rows_status_async).  Replace nothing in the reference, whose
+ * ep_forward (engine/runtime/ep.py:120-143) relies on NCCL's own error path. */
+int pmoe_ep_status_async(const void* own_buf, int* dst, void* stream);
+int pmoe_rows_status_async(const void* own_buf, int* dst, void* stream);
 
 /* Row-split prefill with the exchange fused into the expert GEMMs, replacing
  * the pmoe_block_forward_rows + all_reduce pair of ep.py:97-143/140 for

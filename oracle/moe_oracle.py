@@ -20,10 +20,11 @@ checked out, runs them on seeded inputs, and stores their outputs; the
 ``-m "not gpu"`` tests check this oracle against those fixtures.
 
 Numerics.  bf16 tensors are carried as ``uint16`` bit patterns and widened
-exactly to fp32.  Router logits are accumulated in float64 and rounded once
-to bf16 (round-to-nearest-even), which is the exact value a
-"fp32-accumulate, round once" GEMM approximates; top-k ties are broken to
-the lower expert index.  Everything after routing is fp32 ("the
+exactly to fp32.  Router logits are the bf16 values nearest (ties to even)
+to the exact dot products -- the value a "fp32-accumulate, round once" GEMM
+approximates -- computed in float64 with a rigorous error bound and, where
+the bound leaves the rounding open, in integer arithmetic; top-k ties are
+broken to the lower expert index.  Everything after routing is fp32 ("the
 fp32-accumulate reference" the output tolerance is stated against).
 """
 from __future__ import annotations
@@ -57,16 +58,79 @@ def torch_bf16_bits(t) -> np.ndarray:
 
 # ----------------------------------------------------------------- routing --
 
+def _rn_bf16_f64(v: np.ndarray) -> np.ndarray:
+    """Nearest bf16 value (ties to even) of float64 values, as float64.
+
+    |v| in [2^(e-1), 2^e) has bf16 spacing 2^(e-8); subnormal bf16 spacing is
+    2^-133.  Scaling by a power of two is exact, so one ``rint`` (half to
+    even) rounds correctly."""
+    v = np.asarray(v, dtype=np.float64)
+    _, e = np.frexp(v)
+    q = np.maximum(e - 8, -133)
+    return np.ldexp(np.rint(np.ldexp(v, -q)), q)
+
+
+def _bf16_int(b: int):
+    """bf16 bit pattern -> (signed integer significand M, exponent k): value = M * 2^k."""
+    sign = -1 if b & 0x8000 else 1
+    E = (b >> 7) & 0xFF
+    frac = b & 0x7F
+    if E == 0:
+        return sign * frac, -133
+    return sign * (128 + frac), E - 134
+
+
+def exact_logit_bf16(x_row_bits: np.ndarray, w_row_bits: np.ndarray) -> float:
+    """bf16 nearest (ties to even) to the exact dot product of two bf16 rows,
+    in Python integer arithmetic (no rounding before the final one)."""
+    terms = []
+    for xb, wb in zip(x_row_bits.tolist(), w_row_bits.tolist()):
+        mx, kx = _bf16_int(xb)
+        mw, kw = _bf16_int(wb)
+        if mx and mw:
+            terms.append((mx * mw, kx + kw))
+    if not terms:
+        return 0.0
+    base = min(k for _, k in terms)
+    n = sum(m << (k - base) for m, k in terms)
+    if n == 0:
+        return 0.0
+    sign, n = (-1 if n < 0 else 1), abs(n)
+    shift = max(n.bit_length() - 8, -133 - base)
+    if shift > 0:
+        qv, rem = n >> shift, n & ((1 << shift) - 1)
+        half = 1 << (shift - 1)
+        if rem > half or (rem == half and (qv & 1)):
+            qv += 1
+        n, base = qv, base + shift
+    import math
+    return float(sign * math.ldexp(n, base))
+
+
 def router_logits(x_bits: np.ndarray, w_router_bits: np.ndarray) -> np.ndarray:
     """bf16 router logits as fp32 values.
 
     Follows ``Qwen3_5MoeTopKRouter.forward`` (modeling_qwen3_5_moe.py:762-764):
-    ``F.linear(hidden_states, self.weight)`` in bf16, i.e. a dot product
-    accumulated at high precision and rounded once to bf16.
+    ``F.linear(hidden_states, self.weight)`` in bf16.  The value taken is the
+    bf16 nearest (ties to even) to the EXACT dot product -- the one rounding
+    every fp32-accumulating bf16 GEMM approximates, and the definition the CUDA
+    kernels implement.  Products of bf16 values are exact in float64; the
+    float64 sum has |error| <= n * 2^-52 * sum|x_i w_i| (twice the textbook
+    bound for any summation order); where that interval still straddles a bf16
+    rounding boundary the logit is recomputed in integer arithmetic
+    (``exact_logit_bf16``).
     """
     x = bf16_to_f32(x_bits).astype(np.float64)
     w = bf16_to_f32(w_router_bits).astype(np.float64)
-    return round_bf16((x @ w.T).astype(np.float32))
+    a = x @ w.T
+    bound = (np.abs(x) @ np.abs(w).T) * (x.shape[1] * 2.0 ** -52)
+    r = _rn_bf16_f64(a)
+    amb = _rn_bf16_f64(a - bound) != _rn_bf16_f64(a + bound)
+    xb = np.asarray(x_bits, dtype=np.uint16)
+    wb = np.asarray(w_router_bits, dtype=np.uint16)
+    for t, e in zip(*np.nonzero(amb)):
+        r[t, e] = exact_logit_bf16(xb[t], wb[e])
+    return r.astype(np.float32)
 
 
 def topk_route(logits: np.ndarray, k: int):
@@ -160,7 +224,7 @@ def moe_block(x_bits, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up, w_sh_down
         wgu = bf16_to_f32(w_gate_up[e])
         wd = bf16_to_f32(w_down[e])
         out = swiglu(x[tok], wgu[:I], wgu[I:], wd, round_h=round_h)
-        np.add.at(y, tok, out * wts[tok, slot][:, None])
+        y[tok] += out * wts[tok, slot][:, None]      # tokens are distinct within an expert
     if with_shared:
         sh = swiglu(x, bf16_to_f32(w_sh_gate), bf16_to_f32(w_sh_up),
                     bf16_to_f32(w_sh_down), round_h=round_h)
@@ -200,20 +264,3 @@ def rel_l2(a, b) -> float:
 
 def max_abs(a, b) -> float:
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
-
-
-def explain_topk_mismatch(idx_a, idx_b, logits_exact_f64, k):
-    """For tokens whose top-k sets differ, report whether the disagreement is a
-    rounding near-tie: the k-th and (k+1)-th exact (float64) logits lie within
-    one bf16 ulp of each other, so two correct fp32-accumulate-then-round
-    implementations may legitimately order them differently.
-    Returns (n_mismatch_tokens, n_explained)."""
-    bad = np.nonzero(np.any(np.sort(idx_a, -1) != np.sort(idx_b, -1), axis=-1))[0]
-    explained = 0
-    for t in bad:
-        row = np.sort(logits_exact_f64[t])[::-1]
-        kth, nxt = row[k - 1], row[k]
-        ulp = 2.0 ** (np.floor(np.log2(max(abs(kth), 1e-30))) - 7)
-        if abs(kth - nxt) <= ulp:
-            explained += 1
-    return len(bad), explained

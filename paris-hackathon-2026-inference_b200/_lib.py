@@ -22,6 +22,8 @@ SIGNATURES = {
     "pmoe_version": (ctypes.c_char_p, []),
     "pmoe_workspace_size": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_SZ)]),
     "pmoe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "pmoe_route_diag": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_float),
+                             ctypes.POINTER(_I), _P, _SZ, _P]),
     "pmoe_block_forward": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
                                 _I, _I, _I, _P, _P, _SZ, _P]),
     "pmoe_block_forward_profiled": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
@@ -42,6 +44,8 @@ SIGNATURES = {
     "pmoe_rows_partial": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
     "pmoe_rows_allreduce": (_I, [ctypes.POINTER(_P), _I, _I, _I, _I, _I, _I, _P, _P]),
     "pmoe_rows_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "pmoe_ep_status_async": (_I, [_P, _P, _P]),
+    "pmoe_rows_status_async": (_I, [_P, _P, _P]),
     "pmoe_route_slice": (_I, [_P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _SZ,
                               _P]),
     "pmoe_block_forward_rows": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
@@ -61,6 +65,8 @@ SIGNATURES = {
     "pmoe_ipc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "pmoe_ipc_close": (_I, [_P]),
 }
+
+PMOE_ERR_PEER_TIMEOUT = -6
 
 PMOE_F_SHARED = 1
 PMOE_F_ROUTED = 2

@@ -112,6 +112,38 @@ int pmoe_route(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_
   return PMOE_OK;
 }
 
+int pmoe_route_diag(const uint16_t* x, int T, int H, int E, int K, const uint16_t* w_router,
+                    const uint16_t* w_sh_gvec, int32_t* topk_idx, float* topk_w, float* logits,
+                    float* gamma, int32_t* stats, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int s = check_shape(T, H, E, K, 64, 64);
+  if (s != PMOE_OK) return s;
+  if (!x || !w_router || !w_sh_gvec || !workspace || !topk_idx || !topk_w || !logits || !gamma ||
+      !stats || T == 0)
+    return PMOE_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_router) || !aligned16(w_sh_gvec)) return PMOE_ERR_ALIGN;
+  if ((s = ensure_device()) != PMOE_OK) return s;
+  Dims d = make_dims(T, H, E, K, 64, 64);
+  Workspace ws = carve(workspace, d);
+  if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
+  ws.diag = logits;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool route_tc = T > kFusedRouteMaxT && route_tc_supported(d);
+  const cudaError_t rerr =
+      route_tc ? launch_route_tc(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st)
+               : launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), 0, E, 1, 1, ws, st);
+  if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
+  *gamma = route_tc ? route_tc_gamma(d) : route_gamma(d);
+  const size_t P = size_t(T) * K;
+  if (cudaMemcpyAsync(topk_idx, ws.topk_idx, P * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(topk_w, ws.topk_w, P * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(stats, ws.status + 8, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return PMOE_ERR_CUDA;
+  return PMOE_OK;
+}
+
 // Decoder-layer extras: y = x + block(RMSNorm(x; w_norm, eps)).
 struct LayerArgs {
   const uint16_t* w_norm;
@@ -302,10 +334,13 @@ int pmoe_block_forward(const uint16_t* x, int T, int H, int E, int K, int I, int
 
 // ---- expert parallelism ------------------------------------------------------
 
-// Exchange buffer header: flags [0,256), CTA ticket at 256, device epoch at 384.
+// Exchange buffer header: flags [0,256), CTA ticket at 256, device epoch at 384,
+// sticky status word at 448 (set by a combine whose peer wait gave up; only
+// a fresh, zeroed buffer clears it).
 static const size_t kEpHeader = 512;
 static const size_t kEpTicket = 256;
 static const size_t kEpEpoch = 384;
+static const size_t kEpSticky = 448;
 
 int pmoe_ep_buffer_bytes(int T_max, int H, int K, size_t* bytes) {
   if (!bytes || T_max <= 0 || H <= 0 || K <= 0) return PMOE_ERR_ARG;
@@ -336,6 +371,7 @@ static int setup_ep(int T, int H, int K, int flags, void* const* peer_bufs,
   ep.par_stride = (half / 256 * 256) / sizeof(float);
   char* own = static_cast<char*>(peer_bufs[rank]);
   ep.ticket = reinterpret_cast<int*>(own + kEpTicket);
+  ep.sticky = reinterpret_cast<int*>(own + kEpSticky);
   ep.epoch_dev = epoch == 0 ? reinterpret_cast<const int*>(own + kEpEpoch) : nullptr;
   ep.world = world;
   ep.rank = rank;
@@ -397,10 +433,11 @@ int pmoe_route_slice(const uint16_t* x, int T, int H, int E, int K, int I, int I
   if (ws.bytes > workspace_bytes) return PMOE_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Dims ds = make_dims(t1 - t0, H, E, K, I, Is);
-  if (cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st) != cudaSuccess ||
+  if (cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st) != cudaSuccess ||
       launch_router_tc(ds, bf(x) + size_t(t0) * H, bf(w_router), bf(w_sh_gvec),
                        topk_idx + size_t(t0) * K, topk_w + size_t(t0) * K, shared_gate + t0,
-                       ws.hist, ws.status + 1, st) != cudaSuccess)
+                       ws.hist, ws.status, ws.logit_part, ws.xnorm, ws.wnorm, nullptr,
+                       st) != cudaSuccess)
     return PMOE_ERR_CUDA;
   return PMOE_OK;
 }
@@ -497,6 +534,23 @@ int pmoe_rows_status(const void* own_buf, int* status) {
   if (!own_buf || !status) return PMOE_ERR_ARG;
   return cudaMemcpy(status, static_cast<const char*>(own_buf) + rx_status_offset(), sizeof(int),
                     cudaMemcpyDeviceToHost) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
+int pmoe_ep_status_async(const void* own_buf, int* dst, void* stream) {
+  if (!own_buf || !dst) return PMOE_ERR_ARG;
+  return cudaMemcpyAsync(dst, static_cast<const char*>(own_buf) + kEpSticky, sizeof(int),
+                         cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
+int pmoe_rows_status_async(const void* own_buf, int* dst, void* stream) {
+  if (!own_buf || !dst) return PMOE_ERR_ARG;
+  return cudaMemcpyAsync(dst, static_cast<const char*>(own_buf) + rx_status_offset(),
+                         sizeof(int), cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
              ? PMOE_OK
              : PMOE_ERR_CUDA;
 }

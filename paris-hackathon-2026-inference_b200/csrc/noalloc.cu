@@ -40,8 +40,17 @@ int scratch_address(void** out) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PMOE_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_scratch_ptr[dev]) {
+    // The library holds sm_100a code only: on another device the symbol has no
+    // device copy, so report the device, not the failed lookup.
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return PMOE_ERR_CUDA;
+    if (major != 10) return PMOE_ERR_DEVICE;
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return PMOE_ERR_CUDA;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();  // do not leave the failure for a later error check
+      return PMOE_ERR_CUDA;
+    }
     g_scratch_ptr[dev] = p;
   }
   *out = g_scratch_ptr[dev];

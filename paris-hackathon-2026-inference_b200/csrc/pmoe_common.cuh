@@ -25,8 +25,16 @@ struct Workspace {
   int32_t* pair_dst;    // [T*K+T]    destination row in `rows` (t*K+s, or T*K+t)
   int32_t* pair_pos;    // [T*K+T]    inverse: dispatched row of destination row q (prefill path)
   float* pair_w;        // [T*K+T]    routing weight (or shared gate) of each row
-  float* logit_part;    // [T][Rpad]   router logits (bf16-rounded) + raw shared-gate sum
-  int32_t* status;      // [8]        [0] route ticket, [1] error code (kStatus*), cleared per call
+  float* logit_part;    // [KS][T][Rpad] fp32 router logits (decode: KS split-K partials) + raw
+                        //            shared-gate sum in column E
+  float* xnorm;         // [KS][T]    token norms (decode: partial sums of squares per k range)
+  float* wnorm;         // [TT][KS][Rpad] router-row norms (decode: partial sums of squares per
+                        //            token group and k range; other paths: [E] norms)
+  float* diag;          // not carved: when set, the routing copies its fp32 logits [T][Rpad] here
+  int32_t* status;      // [kStatusWords] [0] route ticket, [1] error code (kStatus*), [2]/[3]
+                        //            stream queues, [4..7] decode group tickets, [8] exact logit
+                        //            evaluations, [9] of which outside the exactness condition;
+                        //            cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
   __nv_bfloat16* xn;    // [T][H]     RMSNorm(x) (decoder-layer entry points)
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
@@ -39,10 +47,14 @@ struct Workspace {
   int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
   int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M blocks; [4]/[5] the dispatched
                         //     rows [lo, hi) this call computes (row-split expert parallelism)
+  int32_t* comb_cnt;    // [T][H/128] stored row segments per token and 128-feature chunk
+                        //            (tensor-core path, combine fused into the down GEMM)
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
 };
+
+constexpr int kStatusWords = 16;
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -71,6 +83,7 @@ struct EpPeers {
   size_t par_stride;       // floats from the parity-0 to the parity-1 copy
   int* flags[kMaxRanks];   // each rank's flag array, indexed by the writing rank
   int* ticket;             // this rank's CTA-completion counter (starts and ends at 0)
+  int* sticky;             // this rank's sticky status word: a peer timeout of any call
   const int* epoch_dev;    // device epoch counter, or null: use `epoch`
   int world;               // 0: no exchange
   int rank;
@@ -140,7 +153,9 @@ inline Workspace carve(void* base, const Dims& d) {
   w.pair_pos = (int32_t*)take(sizeof(int32_t) * R);
   w.pair_w = (float*)take(sizeof(float) * R);
   w.logit_part = (float*)take(sizeof(float) * size_t(d.KS) * d.T * d.Rpad);
-  w.status = (int32_t*)take(sizeof(int32_t) * 8);
+  w.xnorm = (float*)take(sizeof(float) * size_t(d.KS) * d.T);
+  w.wnorm = (float*)take(sizeof(float) * size_t((d.T + 31) / 32) * d.KS * d.Rpad);
+  w.status = (int32_t*)take(sizeof(int32_t) * kStatusWords);
   w.h = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * R * d.ldh);
   w.xn = (__nv_bfloat16*)take(sizeof(__nv_bfloat16) * size_t(d.T) * d.H);
   w.rows = (float*)take(sizeof(float) * R * d.H);
@@ -152,6 +167,7 @@ inline Workspace carve(void* base, const Dims& d) {
   w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 128 + 1));
   w.m_tiles = (int4*)take(sizeof(int4) * mt_max);
   w.tile_counts = (int32_t*)take(sizeof(int32_t) * 8);
+  w.comb_cnt = (int32_t*)take(sizeof(int32_t) * size_t(d.T) * (size_t(d.H) / 128 + 1));
   const size_t ntile = (size_t(d.T) + 127) / 128;
   w.hist = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
   w.hist_base = (int32_t*)take(sizeof(int32_t) * ntile * d.E);

@@ -15,6 +15,10 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
                          int with_routed, const Workspace& ws, cudaStream_t st,
                          int* epoch_bump = nullptr);
 bool route_bumps_epoch(const Dims& d);
+// Accumulation-bound factor gamma of the exact top-k for the routing path
+// that launch_route / launch_route_tc take for d (pmoe_exact.cuh).
+float route_gamma(const Dims& d);
+float route_tc_gamma(const Dims& d);
 
 cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
                                   const __nv_bfloat16* w_gate_up, const __nv_bfloat16* w_down,
@@ -35,7 +39,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
 cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
                                  const float* topk_w, const float* shared_gate, int T, int H,
                                  int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
-                                 const RowsOut* ydst, cudaStream_t st);
+                                 const RowsOut* ydst, const int* abort_if, cudaStream_t st);
 
 // Prefill routing on the tensor cores (router GEMM + top-k epilogue, parallel
 // stable dispatch).
@@ -44,11 +48,17 @@ bool route_tc_supported(const Dims& d);
 cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                             const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                             int with_routed, const Workspace& ws, cudaStream_t st);
-// The router GEMM + top-k alone, for d.T tokens starting at x, into the given
-// arrays (hist: per-128-token-tile expert counts, status: error word).
+// The router GEMM + exact top-k alone, for d.T tokens starting at x, into the
+// given arrays (hist: per-128-token-tile expert counts; status: the status
+// words, error at [1], exact-evaluation counts at [8]/[9]; logits [d.T][Rpad],
+// xnorm [d.T], wnorm [E]: scratch; diag: optional copy of the fp32 logits).
 cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                              const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
-                             float* shared_gate, int32_t* hist, int* status, cudaStream_t st);
+                             float* shared_gate, int32_t* hist, int* status, float* logits,
+                             float* xnorm, float* wnorm, float* diag, cudaStream_t st);
+// Router-row norms for the exact top-k (one warp per row).
+cudaError_t launch_row_norms(const __nv_bfloat16* a, int rows, int H, float* out,
+                             cudaStream_t st);
 // Dispatch (histogram, scan, scatter) from routing computed elsewhere.
 cudaError_t launch_dispatch_given(const Dims& d, const int32_t* topk_idx, const float* topk_w,
                                   const float* shared_gate, int lo, int hi, int with_shared,

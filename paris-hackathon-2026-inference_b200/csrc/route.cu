@@ -15,8 +15,22 @@
 //  * larger T: router GEMM tiles -> warp-per-token top-k -> one-CTA dispatch.
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
+#include "pmoe_exact.cuh"
 
 namespace pmoe {
+
+// Sum of squares of 8 packed bf16 (squares are exact in fp32).
+__device__ __forceinline__ float sumsq8(const uint4& v) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float lo = __uint_as_float(u[j] << 16), hi = __uint_as_float(u[j] & 0xFFFF0000u);
+    s = fmaf(lo, lo, s);
+    s = fmaf(hi, hi, s);
+  }
+  return s;
+}
 
 // ---------------------------------------------------------------------------
 // Router tile: 16 router rows (row E = shared gate vector, rows > E zero) x
@@ -28,7 +42,7 @@ __device__ __forceinline__ void router_tile(const __nv_bfloat16* __restrict__ x,
                                            const __nv_bfloat16* __restrict__ w_router,
                                            const __nv_bfloat16* __restrict__ w_gvec, int T,
                                            int H, int E, int rg, int tt, int k_begin, int k_len,
-                                           float (&acc)[4][4]) {
+                                           float (&acc)[4][4], float (&wss)[2], float (&xss)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int r0 = rg * 16 + g, r1 = r0 + 8;
   auto row_ptr = [&](int r) -> const __nv_bfloat16* {
@@ -45,146 +59,46 @@ __device__ __forceinline__ void router_tile(const __nv_bfloat16* __restrict__ x,
     xp[q] = t < T ? x + size_t(t) * H : nullptr;
   }
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < 4; ++q) {
+    xss[q] = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[q][i] = 0.f;
+  }
+  wss[0] = wss[1] = 0.f;
   const uint4 zero = make_uint4(0, 0, 0, 0);
 #pragma unroll 4
   for (int k0 = k_begin; k0 < k_begin + k_len; k0 += 32) {
     const int kk = k0 + 8 * c;
     const uint4 wa = wa_p ? ldg_stream(wa_p + kk) : zero;
     const uint4 wb = wb_p ? ldg_stream(wb_p + kk) : zero;
+    wss[0] += sumsq8(wa);
+    wss[1] += sumsq8(wb);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       if (tt * 32 + q * 8 < T) {  // warp-uniform
         const uint4 xv = xp[q] ? ldg_keep(xp[q] + kk) : zero;
         mma_k32(acc[q], wa, wb, xv);
+        xss[q] += sumsq8(xv);
       }
     }
   }
 }
 
-// ---------------------------------------------------------------------------
-// Warp-per-token top-k on bf16 logits.
-//
-// Each logit is exactly a bf16 value, so (order-preserving 16-bit key of the
-// logit, 0xFFFF - expert) packed into 32 bits is a unique key whose maximum
-// is the largest logit with ties going to the lower expert.  K rounds of a
-// lane-local max plus one redux.sync max select the top K.  Weights follow
-// softmax -> topk -> divide-by-sum (router :765-768), computed as
-//   w_k = exp(l_k - l_0) / sum_j exp(l_j - l_0)   over the K selected.
-// `row` points at the token's Rpad logits (entry E = raw shared-gate sum).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t bf16_key(float v) {
-  uint32_t b = __float_as_uint(v) >> 16;  // v is already bf16-exact
-  if (b == 0x8000u) b = 0;                // -0 == +0
-  return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+// Row norms (sqrt of the fp32 sum of squares, rounded up) of a bf16 matrix
+// [rows][H], one warp per row.
+__global__ void __launch_bounds__(256) row_norms_kernel(const __nv_bfloat16* __restrict__ a,
+                                                        int rows, int H, float* __restrict__ out) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float ss = warp_row_sumsq(a + size_t(r) * H, H);
+  if ((threadIdx.x & 31) == 0) out[r] = norm_from_sumsq(ss);
 }
 
-__device__ __forceinline__ float key_value(uint32_t key) {
-  uint32_t s = key >> 16;
-  uint32_t b = (s & 0x8000u) ? (s & 0x7FFFu) : (~s & 0xFFFFu);
-  return __uint_as_float(b << 16);
-}
-
-__device__ __forceinline__ void warp_topk(const float* row, bool round_logits, int t, int E,
-                                          int K, int32_t* __restrict__ topk_idx,
-                                          float* __restrict__ topk_w,
-                                          float* __restrict__ shared_gate, int* cnt) {
-  const int lane = threadIdx.x & 31;
-  uint32_t key[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int e = j * 32 + lane;
-    if (e < E) {
-      float v = row[e];
-      if (round_logits) v = bf16_round(v);
-      key[j] = (bf16_key(v) << 16) | uint32_t(0xFFFF - e);
-    } else {
-      key[j] = 0u;
-    }
-  }
-  uint32_t mine = 0;  // lane k keeps the k-th selected key
-  for (int k = 0; k < K; ++k) {
-    uint32_t m = key[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) m = max(m, key[j]);
-    const uint32_t wmax = __reduce_max_sync(0xffffffffu, m);
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (key[j] == wmax) key[j] = 0u;
-    if (lane == k) mine = wmax;
-  }
-  const float l0 = key_value(__shfl_sync(0xffffffffu, mine, 0));
-  const float ex = lane < K ? __expf(key_value(mine) - l0) : 0.f;
-  float den = ex;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  if (lane < K) {
-    const int e = 0xFFFF - int(mine & 0xFFFFu);
-    topk_idx[size_t(t) * K + lane] = e;
-    topk_w[size_t(t) * K + lane] = ex / den;
-    atomicAdd(&cnt[e], 1);
-  }
-  if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-row[E]));
-}
-
-// The same selection for NT tokens per warp (t_first + i * t_stride), their
-// K rounds interleaved so the warp reductions of different tokens overlap.
-template <int NT>
-__device__ __forceinline__ void warp_topk_multi(const float* lg, int Rpad, int t_first,
-                                                int t_stride, int T, int E, int K,
-                                                int32_t* __restrict__ topk_idx,
-                                                float* __restrict__ topk_w,
-                                                float* __restrict__ shared_gate, int* cnt) {
-  const int lane = threadIdx.x & 31;
-  uint32_t key[NT][8], mine[NT];
-#pragma unroll
-  for (int i = 0; i < NT; ++i) {
-    const int t = t_first + i * t_stride;
-    mine[i] = 0u;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int e = j * 32 + lane;
-      key[i][j] = (t < T && e < E)
-                      ? (bf16_key(lg[size_t(t) * Rpad + e]) << 16) | uint32_t(0xFFFF - e)
-                      : 0u;
-    }
-  }
-  for (int k = 0; k < K; ++k) {
-    uint32_t wm[NT];
-#pragma unroll
-    for (int i = 0; i < NT; ++i) {
-      uint32_t m = key[i][0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) m = max(m, key[i][j]);
-      wm[i] = __reduce_max_sync(0xffffffffu, m);
-    }
-#pragma unroll
-    for (int i = 0; i < NT; ++i) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (key[i][j] == wm[i]) key[i][j] = 0u;
-      if (lane == k) mine[i] = wm[i];
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < NT; ++i) {
-    const int t = t_first + i * t_stride;
-    if (t >= T) continue;  // warp-uniform
-    const float l0 = key_value(__shfl_sync(0xffffffffu, mine[i], 0));
-    const float ex = lane < K ? __expf(key_value(mine[i]) - l0) : 0.f;
-    float den = ex;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (lane < K) {
-      const int e = 0xFFFF - int(mine[i] & 0xFFFFu);
-      topk_idx[size_t(t) * K + lane] = e;
-      topk_w[size_t(t) * K + lane] = ex / den;
-      atomicAdd(&cnt[e], 1);
-    }
-    if (lane == 0) shared_gate[t] = 1.0f / (1.0f + __expf(-lg[size_t(t) * Rpad + E]));
-  }
+cudaError_t launch_row_norms(const __nv_bfloat16* a, int rows, int H, float* out,
+                             cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  row_norms_kernel<<<(rows + 7) / 8, 256, 0, st>>>(a, rows, H, out);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -322,9 +236,12 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_router,
     const __nv_bfloat16* __restrict__ w_gvec, int T, int H, int E, int K, int Rpad, int KS,
     int lo, int hi, int with_shared, int with_routed, float* __restrict__ logit_part,
+    float* __restrict__ xn_part, float* __restrict__ wn_part, float* __restrict__ diag,
     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
     DispatchOut o, int32_t* __restrict__ sync, int* __restrict__ epoch_bump) {
   __shared__ float s_part[kFusedRouteWarps][32][17];
+  __shared__ float s_wss[kFusedRouteWarps][16], s_xss[kFusedRouteWarps][32];
+  __shared__ float s_wn[256], s_xn[32];
   __shared__ int s_cnt[256], s_off[256], s_cur[256], s_wsum[32], s_tot[2], s_last;
   extern __shared__ float s_dyn[];
   float* s_lg = s_dyn;                                       // [32][Rpad] (one token group)
@@ -342,14 +259,30 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   const int Hk = H / KS, kb = kg * Hk;
   const int slice = (Hk / kFusedRouteWarps + 31) / 32 * 32;
   const int k_off = min(Hk, warp * slice);
-  float acc[4][4];
-  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, kb + k_off, min(slice, Hk - k_off), acc);
+  float acc[4][4], wss[2], xss[4];
+  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, kb + k_off, min(slice, Hk - k_off), acc, wss,
+              xss);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     s_part[warp][q * 8 + 2 * c][g] = acc[q][0];
     s_part[warp][q * 8 + 2 * c + 1][g] = acc[q][1];
     s_part[warp][q * 8 + 2 * c][g + 8] = acc[q][2];
     s_part[warp][q * 8 + 2 * c + 1][g + 8] = acc[q][3];
+  }
+  // sums of squares of this warp's k slice: the 4 lanes of a row group hold
+  // disjoint k ranges
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) {
+    wss[0] += __shfl_xor_sync(0xffffffffu, wss[0], o);
+    wss[1] += __shfl_xor_sync(0xffffffffu, wss[1], o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xss[q] += __shfl_xor_sync(0xffffffffu, xss[q], o);
+  }
+  if (c == 0) {
+    s_wss[warp][g] = wss[0];
+    s_wss[warp][g + 8] = wss[1];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s_xss[warp][q * 8 + g] = xss[q];
   }
   __syncthreads();
   float* part = logit_part + size_t(kg) * T * Rpad;
@@ -363,10 +296,22 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
       part[size_t(t) * Rpad + r] = s;
     }
   }
+  if (tid < 16) {  // this CTA's k range of its 16 router rows (every group keeps its own copy)
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFusedRouteWarps; ++w) s += s_wss[w][tid];
+    wn_part[(size_t(tt) * KS + kg) * Rpad + rg * 16 + tid] = s;
+  } else if (tid < 48 && rg == 0) {  // and of the group's tokens
+    const int tl = tid - 16, t = tt * 32 + tl;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFusedRouteWarps; ++w) s += s_xss[w][tl];
+    if (t < T) xn_part[size_t(kg) * T + t] = s;
+  }
   __threadfence();
   __syncthreads();
   // Level 1: the last CTA of this 32-token group sums the KS partials in a
-  // fixed order, rounds the logits to bf16 and selects the group's top-k.
+  // fixed order and selects the group's top-k on exactly rounded logits.
   if (tid == 0) s_last = (atomicAdd(&sync[4 + tt], 1) == RG * KS - 1);
   __syncthreads();
   if (!s_last) return;
@@ -386,18 +331,28 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
       if (k < KS) {
         sum.x += v[k].x; sum.y += v[k].y; sum.z += v[k].z; sum.w += v[k].w;
       }
-    const int r = (4 * i) % Rpad;  // the 4 logits are experts r .. r+3 of one token
-    sum.x = r < E ? bf16_round(sum.x) : sum.x;
-    sum.y = r + 1 < E ? bf16_round(sum.y) : sum.y;
-    sum.z = r + 2 < E ? bf16_round(sum.z) : sum.z;
-    sum.w = r + 3 < E ? bf16_round(sum.w) : sum.w;
     reinterpret_cast<float4*>(s_lg)[i] = sum;
+    if (diag) reinterpret_cast<float4*>(diag)[gi] = sum;
+  }
+  for (int r = tid; r < E; r += kFusedRouteThreads) {
+    float s = 0.f;
+    for (int k = 0; k < KS; ++k) s += __ldcg(wn_part + (size_t(tt) * KS + k) * Rpad + r);
+    s_wn[r] = norm_from_sumsq(s);
+  }
+  if (tid < nt) {
+    float s = 0.f;
+    for (int k = 0; k < KS; ++k) s += __ldcg(xn_part + size_t(k) * T + t0 + tid);
+    s_xn[tid] = norm_from_sumsq(s);
   }
   for (int e = tid; e < 256; e += kFusedRouteThreads) s_cnt[e] = 0;
   __syncthreads();
-  static_assert(32 <= 2 * kFusedRouteWarps, "2 tokens per warp");
-  warp_topk_multi<2>(s_lg, Rpad, warp, kFusedRouteWarps, nt, E, K, topk_idx + size_t(t0) * K,
-                     topk_w + size_t(t0) * K, shared_gate + t0, s_cnt);
+  // accumulation depth: the MMA steps of one warp's slice, the sum over the
+  // CTA's warps and the sum over the KS partials
+  const float gamma = float(2 * (slice / 32) + kFusedRouteWarps + KS) * kAccStepErr;
+  const ExactStats stats{sync + 8, sync + 9};
+  for (int tl = warp; tl < nt; tl += kFusedRouteWarps)
+    warp_topk_token(s_lg + size_t(tl) * Rpad, s_xn[tl], s_wn, gamma, t0 + tl, E, K, x, w_router,
+                    H, stats, topk_idx, topk_w, shared_gate, s_cnt);
   __threadfence();
   __syncthreads();
   // Level 2: the last group to finish builds the dispatch for all tokens.
@@ -437,8 +392,8 @@ __global__ void __launch_bounds__(128) router_logits_kernel(
   const long item = long(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (item >= long(RG) * TT) return;
   const int rg = int(item % RG), tt = int(item / RG);
-  float acc[4][4];
-  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, 0, H, acc);
+  float acc[4][4], wss[2], xss[4];
+  router_tile(x, w_router, w_gvec, T, H, E, rg, tt, 0, H, acc, wss, xss);
   const int r0 = rg * 16 + g, r1 = r0 + 8;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -454,14 +409,19 @@ __global__ void __launch_bounds__(128) router_logits_kernel(
   }
 }
 
-__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int T, int E,
-                                                   int K, int Rpad, int32_t* __restrict__ topk_idx,
-                                                   float* __restrict__ topk_w,
-                                                   float* __restrict__ shared_gate,
-                                                   int32_t* __restrict__ counts) {
+// Warp per token over the logits of router_logits_kernel (one MMA chain of
+// H/16 steps per logit); wn: the router rows' norms (row_norms_kernel).
+__global__ void __launch_bounds__(256) topk_kernel(
+    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ x,
+    const __nv_bfloat16* __restrict__ w_router, const float* __restrict__ wn, int T, int H,
+    int E, int K, int Rpad, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+    float* __restrict__ shared_gate, int32_t* __restrict__ counts, ExactStats stats) {
   const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
-  warp_topk(logits + size_t(t) * Rpad, true, t, E, K, topk_idx, topk_w, shared_gate, counts);
+  const float nx = norm_from_sumsq(warp_row_sumsq(x + size_t(t) * H, H));
+  const float gamma = float(H / 16 + 1) * kAccStepErr;
+  warp_topk_token(logits + size_t(t) * Rpad, nx, wn, gamma, t, E, K, x, w_router, H, stats,
+                  topk_idx, topk_w, shared_gate, counts);
 }
 
 constexpr int kDispatchThreads = 1024;
@@ -491,21 +451,27 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
   DispatchOut o{ws.offsets, ws.active, ws.n_active, ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
                 ws.pair_w, d.sh_lo, d.sh_hi};
   const int RG = d.Rpad / 16, TT = (d.T + 31) / 32;
-  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
   if (d.T <= kFusedRouteMaxT) {
     route_fused_kernel<<<RG * TT * d.KS, kFusedRouteThreads,
                          fused_route_smem_bytes(d.T, d.E, d.K, d.Rpad), st>>>(
         x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, d.KS, lo, hi, with_shared,
-        with_routed, ws.logit_part, ws.topk_idx, ws.topk_w, ws.shared_gate, o, ws.status,
-        epoch_bump);
+        with_routed, ws.logit_part, ws.xnorm, ws.wnorm, ws.diag, ws.topk_idx, ws.topk_w,
+        ws.shared_gate, o, ws.status, epoch_bump);
     return cudaGetLastError();
   }
   const long items = long(RG) * TT;
   router_logits_kernel<<<unsigned((items + 3) / 4), 128, 0, st>>>(
       x, w_router, w_gvec, d.T, d.H, d.E, d.Rpad, ws.logit_part, ws.counts);
-  topk_kernel<<<(d.T + 7) / 8, 256, 0, st>>>(ws.logit_part, d.T, d.E, d.K, d.Rpad, ws.topk_idx,
-                                             ws.topk_w, ws.shared_gate, ws.counts);
+  err = launch_row_norms(w_router, d.E, d.H, ws.wnorm, st);
+  if (err != cudaSuccess) return err;
+  if (ws.diag)
+    cudaMemcpyAsync(ws.diag, ws.logit_part, sizeof(float) * size_t(d.T) * d.Rpad,
+                    cudaMemcpyDeviceToDevice, st);
+  topk_kernel<<<(d.T + 7) / 8, 256, 0, st>>>(ws.logit_part, x, w_router, ws.wnorm, d.T, d.H, d.E,
+                                             d.K, d.Rpad, ws.topk_idx, ws.topk_w, ws.shared_gate,
+                                             ws.counts, ExactStats{ws.status + 8, ws.status + 9});
   dispatch_kernel<<<1, kDispatchThreads, dispatch_smem_bytes(d.E), st>>>(
       ws.counts, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.E, d.K, lo, hi, with_shared,
       with_routed, o);
@@ -513,6 +479,14 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
 }
 
 bool route_bumps_epoch(const Dims& d) { return d.T <= kFusedRouteMaxT; }
+
+float route_gamma(const Dims& d) {
+  if (d.T <= kFusedRouteMaxT) {
+    const int slice = (d.H / d.KS / kFusedRouteWarps + 31) / 32 * 32;
+    return float(2 * (slice / 32) + kFusedRouteWarps + d.KS) * kAccStepErr;
+  }
+  return float(d.H / 16 + 1) * kAccStepErr;
+}
 
 cudaError_t route_init() {
   cudaError_t e = cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -23,6 +23,7 @@
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tc.cuh"
+#include "pmoe_exact.cuh"
 
 namespace pmoe {
 
@@ -37,34 +38,28 @@ constexpr int kRtSmem = kRtStages * kRtStageBytes + 1024 + 256;
 static_assert(kRtSmem <= 227 * 1024, "router shared memory");
 constexpr int kRtThreads = 6 * 32;
 constexpr int kRtMaxK = 8;
+// The expert logits accumulate in kRtChains TMEM accumulators (k chunk kc
+// goes to chain kc % kRtChains), summed in fp32 in the epilogue: shorter MMA
+// chains tighten the accumulation bound of the exact top-k (pmoe_exact.cuh).
+constexpr int kRtChains = 3;
+constexpr int kRtGateCol = kRtChains * kRtNH;  // gate accumulator (CTA 0)
+constexpr int kRtTmemCols = 512;
+static_assert(kRtGateCol + kRtN2 <= kRtTmemCols, "TMEM columns");
 static_assert(kRtStageBytes % 1024 == 0, "stage alignment");
 
-__device__ __forceinline__ uint32_t rt_key(float v, int e) {
-  uint32_t b = __float_as_uint(v) >> 16;  // v is bf16-exact
-  if (b == 0x8000u) b = 0;
-  b = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
-  return (b << 16) | uint32_t(0xFFFF - e);
-}
-__device__ __forceinline__ float rt_value(uint32_t key) {
-  const uint32_t s = key >> 16;
-  const uint32_t b = (s & 0x8000u) ? (s & 0x7FFFu) : (~s & 0xFFFFu);
-  return __uint_as_float(b << 16);
-}
-
-__device__ __forceinline__ uint4 ld_shared_cluster_v4(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
+// Accumulation depth of one logit: the MMA steps of the longest chain plus
+// the two fp32 additions of the chains.
+__host__ __device__ inline int router_tc_depth(int H) {
+  const int nk = H / kRtK;
+  return ((nk + kRtChains - 1) / kRtChains) * (kRtK / 16) + (kRtChains - 1);
 }
 
 __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-    const __grid_constant__ CUtensorMap tm_g, int T, int H, int E, int K,
-    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
-    int32_t* __restrict__ hist, int* __restrict__ status) {
+    const __grid_constant__ CUtensorMap tm_g, const __nv_bfloat16* __restrict__ x,
+    const __nv_bfloat16* __restrict__ w_router, int T, int H, int E, int Rpad,
+    float* __restrict__ logits, float* __restrict__ xnorm, float* __restrict__ wnorm,
+    int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -72,11 +67,10 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   uint64_t* empty = full + kRtStages;
   uint64_t* tfull = empty + kRtStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
-  __shared__ int s_hist[256];
-  __shared__ __align__(16) uint32_t s_top[kRtM][kRtMaxK];  // this CTA's keys per token
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t h = cluster_ctarank();  // expert half
-  const int t0 = (blockIdx.x >> 1) * kRtM;
+  const int tile = blockIdx.x >> 1;
+  const int t0 = tile * kRtM;
   const int e0 = int(h) * kRtNH;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
@@ -86,9 +80,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
     mbar_init(tfull, 1);
     mbar_fence_init();
   }
-  for (int i = threadIdx.x; i < 256; i += kRtThreads) s_hist[i] = 0;
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, kRtTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -129,123 +122,113 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
         const uint32_t sa = sb0 + s * kRtStageBytes;
         const uint64_t ad = sdesc_k_sw128(sa), bd = sdesc_k_sw128(sa + kRtA),
                        gd = sdesc_k_sw128(sa + kRtA + kRtB);
+        const uint32_t chain = tmem_base + uint32_t(kc % kRtChains) * kRtNH;
 #pragma unroll
         for (int kk = 0; kk < kRtK / 16; ++kk) {
-          const uint32_t acc = (kc | kk) != 0 ? 1u : 0u;
-          umma_bf16(tmem_base, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), id1, acc);
+          const uint32_t acc = (kc >= kRtChains || kk != 0) ? 1u : 0u;
+          umma_bf16(chain, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), id1, acc);
           if (h == 0)
-            umma_bf16(tmem_base + kRtNH, ad + uint64_t(kk * 2), gd + uint64_t(kk * 2), id2, acc);
+            umma_bf16(tmem_base + kRtGateCol, ad + uint64_t(kk * 2), gd + uint64_t(kk * 2), id2,
+                      (kc | kk) != 0 ? 1u : 0u);
         }
         umma_commit(&empty[s]);
       }
       if (ok) umma_commit(tfull);
     }
-  }
-  // epilogue warps 2..5: one token row per thread, the top keys of this half
-  const int q = warp & 3;
-  const int r = q * 32 + lane;
-  const int t = t0 + r;
-  float gate_logit = 0.f;
-  if (warp >= 2) {
-    uint32_t top[kRtMaxK];
-#pragma unroll
-    for (int k = 0; k < kRtMaxK; ++k) top[k] = 0u;
+  } else {
+    // Epilogue warps 2..5.  While the MMAs run: the norms the exact top-k
+    // needs -- this half's 64 tokens of the tile and, on tile 0, this half's
+    // router rows (L2-resident reads, one warp per row).
+    const int wi = warp - 2;
+    for (int i = 0; i < 16; ++i) {
+      const int t = t0 + int(h) * 64 + wi * 16 + i;
+      if (t < T) {
+        const float ss = warp_row_sumsq(x + size_t(t) * H, H);
+        if (lane == 0) xnorm[t] = norm_from_sumsq(ss);
+      }
+    }
+    if (tile == 0)
+      for (int i = 0; i < 32; ++i) {
+        const int e = e0 + wi * 32 + i;
+        if (e < E) {
+          const float ss = warp_row_sumsq(w_router + size_t(e) * H, H);
+          if (lane == 0) wnorm[e] = norm_from_sumsq(ss);
+        }
+      }
+    // One token row per thread: the chains' sum, in a fixed order, to global.
+    const int q = warp & 3;
+    const int t = t0 + q * 32 + lane;
     if (mbar_wait(tfull, 0)) {
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16);
 #pragma unroll 1
       for (int cc = 0; cc < kRtNH / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(taddr + cc * 32, v);
+        uint32_t v0[32], v1[32], v2[32];
+        tmem_ld32(taddr + cc * 32, v0);
+        tmem_ld32(taddr + kRtNH + cc * 32, v1);
+        tmem_ld32(taddr + 2 * kRtNH + cc * 32, v2);
         tmem_ld_wait();
+        if (t < T) {
+          float4* dst = reinterpret_cast<float4*>(logits + size_t(t) * Rpad + e0 + cc * 32);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int e = e0 + cc * 32 + i;
-          if (e < E) {
-            const uint32_t key = rt_key(bf16_round(__uint_as_float(v[i])), e);
-            if (key > top[kRtMaxK - 1]) {
-              top[kRtMaxK - 1] = key;
-#pragma unroll
-              for (int k = kRtMaxK - 1; k > 0; --k) {
-                if (top[k] > top[k - 1]) {
-                  const uint32_t tmp = top[k];
-                  top[k] = top[k - 1];
-                  top[k - 1] = tmp;
-                }
-              }
-            }
+          for (int i = 0; i < 32; i += 4) {
+            float4 o;
+            o.x = (__uint_as_float(v0[i]) + __uint_as_float(v1[i])) + __uint_as_float(v2[i]);
+            o.y = (__uint_as_float(v0[i + 1]) + __uint_as_float(v1[i + 1])) +
+                  __uint_as_float(v2[i + 1]);
+            o.z = (__uint_as_float(v0[i + 2]) + __uint_as_float(v1[i + 2])) +
+                  __uint_as_float(v2[i + 2]);
+            o.w = (__uint_as_float(v0[i + 3]) + __uint_as_float(v1[i + 3])) +
+                  __uint_as_float(v2[i + 3]);
+            dst[i / 4] = o;
           }
         }
       }
       if (h == 0) {
         uint32_t gv[32];
-        tmem_ld32(taddr + kRtNH, gv);
+        tmem_ld32(taddr + kRtGateCol, gv);
         tmem_ld_wait();
-        gate_logit = __uint_as_float(gv[0]);
+        if (t < T) logits[size_t(t) * Rpad + E] = __uint_as_float(gv[0]);
       }
     } else {
       atomicCAS(status, 0, kStatusTimeoutTmem);
     }
-#pragma unroll
-    for (int k = 0; k < kRtMaxK; ++k) s_top[r][k] = top[k];
   }
-  __syncwarp();
   tc_fence_before();
-  cluster_sync_all();  // both halves' keys are in shared memory
-  if (h == 0 && warp >= 2) {
-    // merge: the peer's keys inserted into this half's descending list (keys
-    // are unique: they hold the expert index)
-    uint32_t b[kRtMaxK], top[kRtMaxK];
-    const uint32_t peer = mapa_shared(smem_u32(&s_top[r][0]), 1);
-    const uint4 b0 = ld_shared_cluster_v4(peer), b1 = ld_shared_cluster_v4(peer + 16);
-    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
-    b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
-#pragma unroll
-    for (int k = 0; k < kRtMaxK; ++k) top[k] = s_top[r][k];
-#pragma unroll
-    for (int j = 0; j < kRtMaxK; ++j) {
-      if (b[j] > top[kRtMaxK - 1]) {
-        top[kRtMaxK - 1] = b[j];
-#pragma unroll
-        for (int k = kRtMaxK - 1; k > 0; --k) {
-          if (top[k] > top[k - 1]) {
-            const uint32_t tmp = top[k];
-            top[k] = top[k - 1];
-            top[k - 1] = tmp;
-          }
-        }
-      }
-    }
-    if (t < T) {
-      const float l0 = rt_value(top[0]);
-      float ex[kRtMaxK], den = 0.f;
-#pragma unroll
-      for (int k = 0; k < kRtMaxK; ++k) {
-        ex[k] = k < K ? __expf(rt_value(top[k]) - l0) : 0.f;
-        den += ex[k];
-      }
-      const float inv = 1.0f / den;
-#pragma unroll
-      for (int k = 0; k < kRtMaxK; ++k) {
-        if (k < K) {
-          const int e = 0xFFFF - int(top[k] & 0xFFFFu);
-          topk_idx[size_t(t) * K + k] = e;
-          topk_w[size_t(t) * K + k] = ex[k] * inv;
-          atomicAdd(&s_hist[e], 1);
-        }
-      }
-      shared_gate[t] = 1.0f / (1.0f + __expf(-gate_logit));
-    }
-  }
   __syncthreads();
-  if (h == 0)
-    for (int e = threadIdx.x; e < E; e += kRtThreads)
-      hist[size_t(blockIdx.x >> 1) * E + e] = s_hist[e];
-  cluster_sync_all();  // the peer has read this CTA's keys
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 256);
+    tmem_dealloc(tmem_base, kRtTmemCols);
   }
+}
+
+// Exact top-k over the router GEMM's logits: one CTA per 128-token tile
+// (16 warps, a token per warp at a time); writes the routing and the tile's
+// expert histogram.
+constexpr int kRtTopkThreads = 512;
+__global__ void __launch_bounds__(kRtTopkThreads, 1) route_topk_tc_kernel(
+    const float* __restrict__ logits, const float* __restrict__ xnorm,
+    const float* __restrict__ wnorm, const __nv_bfloat16* __restrict__ x,
+    const __nv_bfloat16* __restrict__ w_router, int T, int H, int E, int K, int Rpad,
+    float gamma, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+    float* __restrict__ shared_gate, int32_t* __restrict__ hist, ExactStats stats) {
+  __shared__ int s_hist[kRtN];
+  __shared__ float s_wn[kRtN];
+  for (int e = threadIdx.x; e < kRtN; e += blockDim.x) {
+    s_hist[e] = 0;
+    s_wn[e] = e < E ? wnorm[e] : 0.f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kRtM;
+  for (int i = warp; i < kRtM; i += kRtTopkThreads / 32) {
+    const int t = t0 + i;
+    if (t >= T) break;
+    warp_topk_token(logits + size_t(t) * Rpad, xnorm[t], s_wn, gamma, t, E, K, x, w_router, H,
+                    stats, topk_idx, topk_w, shared_gate, s_hist);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[size_t(blockIdx.x) * E + e] = s_hist[e];
 }
 
 // ---------------------------------------------------------------------------
@@ -376,6 +359,8 @@ cudaError_t route_tc_init() {
                               kRtSmem);
 }
 
+float route_tc_gamma(const Dims& d) { return float(router_tc_depth(d.H)) * kAccStepErr; }
+
 bool route_tc_supported(const Dims& d) {
   return d.E <= kRtN && d.K <= kRtMaxK && d.H % kRtK == 0;
 }
@@ -397,7 +382,8 @@ __global__ void __launch_bounds__(256) route_hist_kernel(const int32_t* __restri
 
 cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                              const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
-                             float* shared_gate, int32_t* hist, int* status, cudaStream_t st) {
+                             float* shared_gate, int32_t* hist, int* status, float* logits,
+                             float* xnorm, float* wnorm, float* diag, cudaStream_t st) {
   CUtensorMap tm_x, tm_w, tm_g;
   const uint64_t H = d.H;
   if (!make_tmap_bf16_2d(&tm_x, x, H, d.T, H * 2, kRtK, kRtM) ||
@@ -417,8 +403,20 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, router_tc_kernel, tm_x, tm_w, tm_g, int(d.T), int(d.H),
-                            int(d.E), int(d.K), topk_idx, topk_w, shared_gate, hist, status);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, router_tc_kernel, tm_x, tm_w, tm_g, x, w_router,
+                                       int(d.T), int(d.H), int(d.E), int(d.Rpad), logits, xnorm,
+                                       wnorm, status + 1);
+  if (err != cudaSuccess) return err;
+  if (diag) {
+    err = cudaMemcpyAsync(diag, logits, sizeof(float) * size_t(d.T) * d.Rpad,
+                          cudaMemcpyDeviceToDevice, st);
+    if (err != cudaSuccess) return err;
+  }
+  const float gamma = float(router_tc_depth(d.H)) * kAccStepErr;
+  route_topk_tc_kernel<<<nb, kRtTopkThreads, 0, st>>>(
+      logits, xnorm, wnorm, x, w_router, d.T, d.H, d.E, d.K, d.Rpad, gamma, topk_idx, topk_w,
+      shared_gate, hist, ExactStats{status + 8, status + 9});
+  return cudaGetLastError();
 }
 
 // Scan + scatter from the routing in ws.topk_idx / topk_w / shared_gate and
@@ -439,10 +437,10 @@ static cudaError_t launch_dispatch(const Dims& d, int lo, int hi, int with_share
 cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                             const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                             int with_routed, const Workspace& ws, cudaStream_t st) {
-  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
   err = launch_router_tc(d, x, w_router, w_gvec, ws.topk_idx, ws.topk_w, ws.shared_gate, ws.hist,
-                         ws.status + 1, st);
+                         ws.status, ws.logit_part, ws.xnorm, ws.wnorm, ws.diag, st);
   if (err != cudaSuccess) return err;
   return launch_dispatch(d, lo, hi, with_shared, with_routed, ws, st);
 }
@@ -450,7 +448,7 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
 cudaError_t launch_dispatch_given(const Dims& d, const int32_t* topk_idx, const float* topk_w,
                                   const float* shared_gate, int lo, int hi, int with_shared,
                                   int with_routed, const Workspace& ws, cudaStream_t st) {
-  cudaError_t err = cudaMemsetAsync(ws.status, 0, 8 * sizeof(int32_t), st);
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st);
   const size_t P = size_t(d.T) * d.K;
   if (err == cudaSuccess)
     err = cudaMemcpyAsync(ws.topk_idx, topk_idx, P * 4, cudaMemcpyDeviceToDevice, st);

@@ -18,6 +18,8 @@
 // A rank one call ahead writes the other parity; it cannot be two calls ahead
 // (its reduce of call e+1 waits for every rank's partial of e+1, written after
 // that rank's gather of e).
+#include <algorithm>
+
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tma.cuh"
@@ -42,11 +44,14 @@ __device__ __forceinline__ int* rx_flags(const RxPeers& p, int q, int off) {
 }
 
 // Bounded wait of one thread for flags[0..world) >= epoch; false on timeout.
+// Returns at once when an earlier wait of this rank already gave up.
 __device__ bool rx_wait(const RxPeers& p, int off) {
   const long long t0 = clock64();
   const int* f = rx_flags(p, p.rank, off);
+  const int* status = rx_flags(p, p.rank, kRxStatus);
   for (int q = 0; q < p.world; ++q) {
     while (ld_acquire_sys(f + q) < p.epoch) {
+      if (__ldcg(status) != 0) return false;
       if (clock64() - t0 > kWaitBudgetCycles) {
         atomicCAS(rx_flags(p, p.rank, kRxStatus), 0, kStatusTimeoutPeer);
         return false;
@@ -57,21 +62,57 @@ __device__ bool rx_wait(const RxPeers& p, int off) {
 }
 
 // Raise flags[rank] = epoch (flag set at `off`) on every rank, after all of
-// this rank's earlier work on the stream.
+// this rank's earlier work on the stream -- unless a wait of this rank gave
+// up (status word set): its data are then incomplete and peers must not
+// read them (they time out in turn and report it).
 __global__ void rx_publish_kernel(RxPeers p, int off) {
   __threadfence_system();
+  if (__ldcg(rx_flags(p, p.rank, kRxStatus)) != 0) return;
   for (int q = 0; q < p.world; ++q) st_release_sys(rx_flags(p, q, off) + p.rank, p.epoch);
+}
+
+// y = this rank's slice region (all T rows after the second flag round),
+// unless a wait gave up.
+__global__ void __launch_bounds__(kRxThreads) rx_copy_kernel(RxPeers p,
+                                                             const uint4* __restrict__ src,
+                                                             uint4* __restrict__ dst, long n16) {
+  if (__ldcg(rx_flags(p, p.rank, kRxStatus)) != 0) return;
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n16;
+       i += long(gridDim.x) * blockDim.x)
+    dst[i] = __ldcg(src + i);
 }
 
 // Bounded wait for every rank's flag at `off` (the kernels after it on the
 // stream run once it returns; a timeout leaves status 4).
 __global__ void rx_wait_kernel(RxPeers p, int off) { rx_wait(p, off); }
 
+// The CTA-completion ticket: the last CTA to arrive resets it and, unless a
+// wait of this call gave up (status word set), raises flagsB[rank] = epoch on
+// every rank.  Every CTA takes the ticket, the ones that timed out included,
+// so it is back at 0 for the next call.
+__device__ void rx_ticket_and_publish(const RxPeers& p) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ticket = rx_flags(p, p.rank, kRxTicket);
+    if (atomicAdd(ticket, 1) == int(gridDim.x) - 1) {
+      __threadfence_system();
+      *ticket = 0;
+      if (__ldcg(rx_flags(p, p.rank, kRxStatus)) == 0)
+        for (int q = 0; q < p.world; ++q)
+          st_release_sys(rx_flags(p, q, kRxFlagsB) + p.rank, p.epoch);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kRxThreads) rx_reduce_kernel(RxPeers p, int T, int H) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_ok = rx_wait(p, kRxFlagsA) ? 1 : 0;
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_ok) {
+    rx_ticket_and_publish(p);
+    return;
+  }
   const int t0 = int(long(p.rank) * T / p.world), t1 = int(long(p.rank + 1) * T / p.world);
   const int h8 = H / 8;
   const long n = long(t1 - t0) * h8;
@@ -104,24 +145,14 @@ __global__ void __launch_bounds__(kRxThreads) rx_reduce_kernel(RxPeers p, int T,
     }
     *reinterpret_cast<uint4*>(own + off) = o;
   }
-  // The last CTA to finish raises flagsB[rank] on every rank.
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int* ticket = rx_flags(p, p.rank, kRxTicket);
-    if (atomicAdd(ticket, 1) == int(gridDim.x) - 1) {
-      __threadfence_system();
-      *ticket = 0;
-      for (int q = 0; q < p.world; ++q)
-        st_release_sys(rx_flags(p, q, kRxFlagsB) + p.rank, p.epoch);
-    }
-  }
+  rx_ticket_and_publish(p);
 }
 
 __global__ void __launch_bounds__(kRxThreads) rx_gather_kernel(RxPeers p, int T, int H,
                                                                __nv_bfloat16* __restrict__ y) {
   __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = rx_wait(p, kRxFlagsB) ? 1 : 0;
+  if (threadIdx.x == 0)
+    s_ok = (__ldcg(rx_flags(p, p.rank, kRxStatus)) == 0 && rx_wait(p, kRxFlagsB)) ? 1 : 0;
   __syncthreads();
   if (!s_ok) return;
   const int h8 = H / 8;
@@ -223,16 +254,19 @@ cudaError_t launch_rows_fused_tail(void* const* bufs, int T_max, int world, int 
   for (int q = 0; q < world; ++q)
     ydst.base[q] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(bufs[q]) +
                                                      rx_region_offset(T_max, H, epoch));
-  (void)num_sms;
   rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
   rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsA);
+  const int* status = reinterpret_cast<const int*>(own + kRxStatus);
   cudaError_t e = launch_combine_slice(rows, topk_idx, topk_w, shared_gate, T, H, E, K, t0, t1,
-                                       reduced, &ydst, st);
+                                       reduced, &ydst, status, st);
   if (e != cudaSuccess) return e;
   rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsB);
   rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsB);
-  e = cudaMemcpyAsync(y, reduced, size_t(T) * H * 2, cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return e;
+  const long n16 = long(T) * H * 2 / 16;  // H % 8 == 0
+  const unsigned blocks = unsigned(std::min<long>((n16 + kRxThreads - 1) / kRxThreads,
+                                                  long(num_sms) * 4));
+  rx_copy_kernel<<<blocks, kRxThreads, 0, st>>>(p, reinterpret_cast<const uint4*>(reduced),
+                                                reinterpret_cast<uint4*>(y), n16);
   return cudaGetLastError();
 }
 

@@ -474,8 +474,8 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const float* __restrict__ rows, size_t par_stride, const int32_t* __restrict__ topk_idx,
     int T, int H, int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
     const int* __restrict__ wait_flags, int world, const int* __restrict__ epoch_dev,
-    int epoch_host, int* __restrict__ status, const __nv_bfloat16* __restrict__ resid,
-    __nv_bfloat16* __restrict__ y) {
+    int epoch_host, int* __restrict__ status, int* __restrict__ sticky,
+    const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
   const int epoch = epoch_dev ? *epoch_dev : epoch_host;
   if (world > 0) rows += size_t(epoch & 1) * par_stride;
   if (world > 0) {
@@ -488,6 +488,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
           if (clock64() - t0 > kWaitBudgetCycles) {
             ok = 0;
             atomicCAS(status, 0, kStatusTimeoutPeer);
+            if (sticky) atomicCAS(sticky, 0, kStatusTimeoutPeer);  // survives the next call
             break;
           }
         }
@@ -657,7 +658,7 @@ cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, i
   const int* flags = ep.world > 0 ? ep.flags[ep.rank] : nullptr;
   combine_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(
       rows, ep.par_stride, ws.topk_idx, d.T, d.H, d.K, lo, hi, with_shared, with_routed, d.sh_lo,
-      d.sh_hi, flags, ep.world, ep.epoch_dev, ep.epoch, ws.status + 1, resid, y);
+      d.sh_hi, flags, ep.world, ep.epoch_dev, ep.epoch, ws.status + 1, ep.sticky, resid, y);
   return cudaGetLastError();
 }
 

@@ -49,8 +49,14 @@ constexpr int kTcStageBytes = kWBytes + kRowBytes;  // 32 KiB
 constexpr int kEpiWarps = 16;  // four per TMEM lane quadrant, each owning 64 columns
 constexpr int kEpiWarpBytes = 32 * 16 * 2;  // per-warp gate_up staging tile (bf16 32 x 16)
 constexpr int kBarBytes = 256;            // mbarriers + TMEM slot
-constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps * kEpiWarpBytes;
+// down with the fused combine: per column quarter, the list of tokens whose
+// every row segment of this CTA's 128 features is now stored (64 + 1 ints)
+constexpr int kFuseListInts = 68;
+constexpr int kFuseBytes = 4 * kFuseListInts * 4;
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps * kEpiWarpBytes +
+                        kFuseBytes;
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
+constexpr int kCombineMaxKFused = 8;      // top-k sizes the fused down combine handles
 constexpr uint32_t kTmemCols = 512;       // two 256-column fp32 accumulators
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
 // barrier area: 16 mbarriers (128 B), the TMEM slot at 128, four abort flags at 192
@@ -67,6 +73,17 @@ struct TileTables {
   int T, K;                 // for the token of a token-major row
   int sh5;                  // gate_up: shared gate|up in one 5-D map (tm_b_sh0)
   int sh_swap;              // ... whose first half is the up rows (w_sh_up < w_sh_gate)
+  // down, fused combine (fuse != 0; every token has all K routed rows and
+  // its shared row on this GPU): cnt[t * (H/128) + c] counts the stored
+  // 128-feature segments c of token t's rows; the epilogue that stores the
+  // last of them sums the token's segments into y (see the down epilogue).
+  int fuse;
+  int* cnt;
+  const int32_t* topk_idx;
+  const float* topk_w;
+  const float* shared_gate;
+  const __nv_bfloat16* resid;  // decoder layer: y = bf16(resid + bf16(sum)); may be null
+  __nv_bfloat16* y;
 };
 
 __device__ __forceinline__ uint8_t* tc_align1024(uint8_t* p) {
@@ -79,6 +96,94 @@ __device__ __forceinline__ void tc_status(int* status, int code) { atomicCAS(sta
 // tile's descriptor one tile ahead).
 __device__ __forceinline__ int4 tile_at(const TileTables& tt, int t, int ntiles) {
   return t < ntiles ? tt.tiles[t] : make_int4(0, 0, 0, 0);
+}
+
+// Fused routing-weighted combine of the down GEMM (single GPU, every row of
+// every token computed here).  Called by the four warps of a column quarter
+// after they stored the segments [fq, fq + 128) of the tile's columns
+// cw .. cw + 63 (dispatched rows; ldst = their token-major rows, lane-indexed
+// per 32-column half, identical in the four warps).  Each stored segment
+// increments its token's counter for this 128-feature chunk; the store that
+// completes a token's K + 1 segments (counter reaches K + 1) makes this quarter
+// sum them: y[t, fq .. fq+127] = bf16(sum_k w_tk * row_k + g_t * row_shared)
+// in fp32, k = 0..K-1 then the shared row, exactly as combine_rows_tok_kernel
+// (bit-identical results).  The counter is reset for the next call.
+// Ordering: stores -> __threadfence -> atomicAdd; the last adder's
+// atomicAdd -> __threadfence -> L2 loads (ld.cg).
+__device__ __forceinline__ void down_fused_combine(const TileTables& tt, int H, int fq,
+                                                   int quarter, int q, int lane, int cw,
+                                                   int nrows, const int (&ldst)[2],
+                                                   const __nv_bfloat16* __restrict__ rows,
+                                                   int* s_list) {
+  const int bar_id = 1 + quarter;
+  const int tq = q * 32 + lane;  // 0..127 within the quarter
+  const int nch = H / 128, ch = fq / 128;
+  const int tk = tt.T * tt.K;
+  __threadfence();
+  if (tq == 0) s_list[64] = 0;
+  named_bar_sync(bar_id, 128);
+  if (q < 2) {
+    const int col = cw + tq;  // warp q < 2 holds this column's row in ldst[q]
+    const int dst = q == 0 ? ldst[0] : ldst[1];
+    if (col < nrows) {
+      const int t = dst < tk ? dst / tt.K : dst - tk;
+      int* c = tt.cnt + size_t(t) * nch + ch;
+      if (atomicAdd(c, 1) == tt.K) {  // this store completed the token's K + 1 segments
+        *c = 0;                       // ready for the next call
+        s_list[atomicAdd(&s_list[64], 1)] = t;
+      }
+    }
+  }
+  named_bar_sync(bar_id, 128);
+  const int n = s_list[64];
+  const int part = tq & 15;  // 16 threads x 8 features per token
+  for (int i = tq >> 4; i < n; i += 8) {
+    const int t = s_list[i];
+    __threadfence();
+    float w[kCombineMaxKFused + 1];
+    uint4 v[kCombineMaxKFused + 1];
+#pragma unroll
+    for (int k = 0; k < kCombineMaxKFused; ++k)
+      if (k < tt.K) w[k] = __ldcg(tt.topk_w + size_t(t) * tt.K + k);
+    w[kCombineMaxKFused] = __ldcg(tt.shared_gate + t);
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxKFused; ++k) {
+      const size_t r = k < kCombineMaxKFused ? size_t(t) * tt.K + k : size_t(tk) + t;
+      if (k < tt.K || k == kCombineMaxKFused)
+        v[k] = __ldcg(reinterpret_cast<const uint4*>(rows + r * H + fq) + part);
+    }
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k <= kCombineMaxKFused; ++k) {
+      if (!(k < tt.K || k == kCombineMaxKFused)) continue;
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        s[2 * j] = fmaf(w[k], f.x, s[2 * j]);
+        s[2 * j + 1] = fmaf(w[k], f.y, s[2 * j + 1]);
+      }
+    }
+    if (tt.resid) {  // decoder layer: y = bf16(resid + bf16(sum))
+      const uint4 rv = __ldg(reinterpret_cast<const uint4*>(tt.resid + size_t(t) * H + fq) + part);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(r2[j]);
+        s[2 * j] = f.x + bf16_round(s[2 * j]);
+        s[2 * j + 1] = f.y + bf16_round(s[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
+      op[j] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    reinterpret_cast<uint4*>(tt.y + size_t(t) * H + fq)[part] = o;
+  }
+  (void)nch;
 }
 
 // One persistent kernel per GEMM, launched as CTA pairs (clusters of 2).  A
@@ -370,6 +475,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
               }
             }
           }
+        }
+        if (tt.fuse) {
+          // The accumulator is read: release it before the combine work.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty0 + b * 8);
+          down_fused_combine(tt, H, fq, quarter, q, lane, cw, nrows, ldst, out_rows,
+                             reinterpret_cast<int*>(smem + kTcStages * kTcStageBytes +
+                                                    kBarBytes + kEpiWarps * kEpiWarpBytes) +
+                                 quarter * kFuseListInts);
+          continue;
         }
       }
       tc_fence_before();
@@ -713,9 +829,12 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
     int K, int lo, int hi, int with_shared, int with_routed, int sh_lo, int sh_hi,
     const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ row_range,
     const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y, int t_lo,
-    int t_hi, const __grid_constant__ RowsOut ydst) {
+    int t_hi, const __grid_constant__ RowsOut ydst, const int* __restrict__ abort_if) {
   // ydst.world > 0: each output row goes to row t of every rank's buffer
   // ydst.base[0..world) (peer stores) instead of y.
+  // abort_if (may be null): a status word; non-zero (an earlier wait of the
+  // exchange gave up) -> do nothing, in particular no peer stores.
+  if (abort_if && __ldcg(abort_if) != 0) return;
   const int cols8 = H / 8, c8 = threadIdx.x;
   const bool act = c8 < cols8;
   const int p_lo = pair_pos ? row_range[0] : 0, p_hi = pair_pos ? row_range[1] : 0;
@@ -783,6 +902,16 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
 
 namespace {
 int g_pairs = 74;  // co-resident CTA pairs of the GEMM kernels
+
+// PMOE_UNFUSED_COMBINE=1 runs the combine as its own kernel after the down
+// GEMM (for measuring the fusion; the results are bit-identical).
+bool fused_combine_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("PMOE_UNFUSED_COMBINE");
+    return v && v[0] == '1';
+  }();
+  return off;
+}
 
 // Per-block cost constant of the row split, in rows: 512 (two full blocks'
 // rows) evens out the GEMM tile count per rank where few tiles per rank make
@@ -908,6 +1037,22 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
                 sh5, sh_swap};
   TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w,
                 rows_out ? *rows_out : RowsOut{}, d.T, d.K, 0, 0};
+  // The routing-weighted combine runs inside the down GEMM's epilogue when
+  // this GPU computes every row of every token (no expert or row split).
+  const bool fuse = !rows_out && world == 1 && lo == 0 && hi == d.E && with_routed &&
+                    with_shared && d.sh_lo == 0 && d.sh_hi == d.T && d.K <= kCombineMaxKFused &&
+                    d.H % 128 == 0 && !fused_combine_disabled();
+  if (fuse) {
+    dn.fuse = 1;
+    dn.cnt = ws.comb_cnt;
+    dn.topk_idx = ws.topk_idx;
+    dn.topk_w = ws.topk_w;
+    dn.shared_gate = ws.shared_gate;
+    dn.resid = resid;
+    dn.y = y;
+    err = cudaMemsetAsync(ws.comb_cnt, 0, sizeof(int) * size_t(d.T) * (d.H / 128), st);
+    if (err != cudaSuccess) return err;
+  }
   err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, gu, d.H, d.E, d.I, d.Is,
                               d.ldh, ws.h, ws.rows_bf16, status);
   if (err != cudaSuccess) return err;
@@ -918,6 +1063,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   if (err != cudaSuccess) return err;
   err = mark(2);
   if (err != cudaSuccess) return err;
+  if (fuse) return cudaSuccess;                             // y is complete
   if (rows_out && rows_out->world > 0) return cudaSuccess;  // the token owners combine
   const long n8 = long(T) * d.H / 8;
   const int* pp = world > 1 ? ws.pair_pos : nullptr;
@@ -926,7 +1072,8 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
     const unsigned blocks = unsigned(std::min<long>(T, long(2 * g_pairs) * 4));  // one wave
     combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(
         ws.rows_bf16, ws.topk_idx, ws.topk_w, ws.shared_gate, d.T, d.H, d.K, lo, hi, with_shared,
-        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y, 0, d.T, RowsOut{});
+        with_routed, d.sh_lo, d.sh_hi, pp, ws.tile_counts + 4, resid, y, 0, d.T, RowsOut{},
+        nullptr);
     return cudaGetLastError();
   }
   combine_rows_kernel<<<unsigned((n8 + 255) / 256), 256, 0, st>>>(
@@ -941,7 +1088,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
 cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_idx,
                                  const float* topk_w, const float* shared_gate, int T, int H,
                                  int E, int K, int t_lo, int t_hi, __nv_bfloat16* y,
-                                 const RowsOut* ydst, cudaStream_t st) {
+                                 const RowsOut* ydst, const int* abort_if, cudaStream_t st) {
   if (K > kCombineMaxK || H / 8 > 256) return cudaErrorInvalidValue;
   if (t_hi <= t_lo) return cudaSuccess;
   const unsigned threads = unsigned((H / 8 + 31) / 32 * 32);
@@ -949,7 +1096,7 @@ cudaError_t launch_combine_slice(const __nv_bfloat16* rows, const int32_t* topk_
   combine_rows_tok_kernel<<<blocks, threads, 0, st>>>(rows, topk_idx, topk_w, shared_gate, T, H,
                                                       K, 0, E, 1, 1, 0, T, nullptr, nullptr,
                                                       nullptr, y, t_lo, t_hi,
-                                                      ydst ? *ydst : RowsOut{});
+                                                      ydst ? *ydst : RowsOut{}, abort_if);
   return cudaGetLastError();
 }
 

@@ -20,9 +20,18 @@ are summed.  Two ways to sum:
   NVLink (CUDA IPC-mapped), raises per-rank completion flags, and the
   combine waits on them (bounded) and sums locally -- every rank ends with the
   full output and no collective kernel runs;
-* ``nccl`` (the comparator, and prefill): each rank returns its partial
-  (its experts plus its share of the shared expert's tokens) and
-  ``torch.distributed.all_reduce`` sums them, as ep.py:140 does.
+  Prefill-sized batches use the row split: the down GEMM stores each row at
+  the rank owning its token over NVLink, that rank combines its token slice
+  and pushes it to every rank (``pmoe_block_forward_rows_fused``);
+* ``nccl`` (the comparator): each rank returns its partial (its experts plus
+  its share of the shared expert's tokens) and ``torch.distributed.all_reduce``
+  sums them, as ep.py:140 does; ``a2a``: token dispatch with all_to_all_single.
+
+A peer that never arrives makes the kernels' bounded waits give up (about a
+second) and set a sticky status word in this rank's exchange buffer instead
+of hanging; ``EPGroup`` reads it asynchronously after every exchange call and
+raises ``PmoeError(PMOE_ERR_PEER_TIMEOUT)`` at the next call, at ``check()``
+and at ``close()`` (the reference's ep_forward relies on NCCL's error path).
 """
 from __future__ import annotations
 
@@ -102,23 +111,9 @@ class EPGroup:
 
     def __init__(self, num_experts: int, hidden: int, top_k: int, mode: str = "fused",
                  t_max: int = FUSED_MAX_T, group=None):
-        self.group = group
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.E, self.H, self.K = num_experts, hidden, top_k
-        self.lo, self.hi = expert_range(num_experts, self.rank, self.world)
-        self.mode = mode
-        self.epoch = 0
-        self.lib = _lib.load()
-        self.local_buf = None
-        self.peer_ptrs = None
-        self.rx_local = None    # row-split exchange buffers (prefill), allocated on first use
-        self.rx_tmax = 0
-        self.rx_epoch = 0
-        # prefill exchange: "rows" (the down GEMM stores rows at their token
-        # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
-        # outputs summed by pmoe_rows_allreduce)
-        self.prefill = "rows"
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self._init_state(num_experts, hidden, top_k, mode, rank, world, group)
         if mode == "fused" and self.world > 1:
             nbytes = ctypes.c_size_t(0)
             _lib.check("pmoe_ep_buffer_bytes",
@@ -144,6 +139,94 @@ class EPGroup:
             torch.cuda.synchronize()
             dist.barrier(group)
 
+    def _init_state(self, num_experts, hidden, top_k, mode, rank, world, group):
+        self.group = group
+        self.rank, self.world = rank, world
+        self.E, self.H, self.K = num_experts, hidden, top_k
+        self.lo, self.hi = expert_range(num_experts, self.rank, self.world)
+        self.mode = mode
+        self.epoch = 0
+        self.lib = _lib.load()
+        self.local_buf = None
+        self.peer_ptrs = None
+        self.owns_buffers = True
+        self.rx_local = None    # row-split exchange buffers (prefill), allocated on first use
+        self.rx_tmax = 0
+        self.rx_epoch = 0
+        # prefill exchange: "rows" (the down GEMM stores rows at their token
+        # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
+        # outputs summed by pmoe_rows_allreduce)
+        self.prefill = "rows"
+        # sticky status words of this rank's exchange buffers ([0] decode, [1]
+        # row split), copied here asynchronously after every exchange call
+        self._st_host = torch.zeros(2, dtype=torch.int32,
+                                    pin_memory=torch.cuda.is_available())
+        self._st_event = None
+
+    @classmethod
+    def emulated(cls, num_experts: int, hidden: int, top_k: int, rank: int, world: int,
+                 peer_bufs=None, rows_bufs=None, rows_t_max: int = 0, t_max: int = FUSED_MAX_T):
+        """A rank of a peer group whose exchange buffers the caller provides
+        (device pointers, one per rank; no process group, no IPC): for running
+        the exchange paths in one process, e.g. with ranks that never arrive.
+        ``peer_bufs``: pmoe_ep_buffer_bytes(t_max) each; ``rows_bufs``:
+        pmoe_rows_fused_buffer_bytes(rows_t_max) each.  The caller frees them."""
+        g = cls.__new__(cls)
+        g._init_state(num_experts, hidden, top_k, "fused", rank, world, None)
+        g.owns_buffers = False
+        if peer_bufs is not None:
+            nb = ctypes.c_size_t(0)
+            _lib.check("pmoe_ep_buffer_bytes",
+                       g.lib.pmoe_ep_buffer_bytes(t_max, hidden, top_k, ctypes.byref(nb)))
+            g.buf_bytes, g.t_max = int(nb.value), t_max
+            g.peer_ptrs = list(peer_bufs)
+            g.local_buf = g.peer_ptrs[rank]
+            g.peer_arr = (ctypes.c_void_p * world)(*g.peer_ptrs)
+        if rows_bufs is not None:
+            g.rx_ptrs = list(rows_bufs)
+            g.rx_local = g.rx_ptrs[rank]
+            g.rx_tmax = rows_t_max
+            g.rx_arr = (ctypes.c_void_p * world)(*g.rx_ptrs)
+        return g
+
+    # ---- peer-loss detection ---------------------------------------------------
+
+    def _status_enqueue(self, stream):
+        """Copy the sticky status words to pinned host memory in stream order
+        (not while the stream is being captured into a graph)."""
+        if torch.cuda.is_current_stream_capturing():
+            return
+        hp = self._st_host.data_ptr()
+        if self.local_buf is not None:
+            _lib.check("pmoe_ep_status_async",
+                       self.lib.pmoe_ep_status_async(self.local_buf, hp, stream))
+        if self.rx_local is not None:
+            _lib.check("pmoe_rows_status_async",
+                       self.lib.pmoe_rows_status_async(self.rx_local, hp + 4, stream))
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        self._st_event = ev
+
+    def _status_check(self, block: bool):
+        ev = self._st_event
+        if ev is None:
+            return
+        if block:
+            ev.synchronize()
+        elif not ev.query():
+            return
+        codes = self._st_host.tolist()
+        if any(codes):
+            raise _lib.PmoeError(
+                "EPGroup", _lib.PMOE_ERR_PEER_TIMEOUT,
+                f"rank {self.rank}: a peer GPU did not arrive within the bounded wait "
+                f"(status words {codes}); the exchange results since then are invalid")
+
+    def check(self):
+        """Wait for the last exchange call's status and raise PmoeError
+        (PMOE_ERR_PEER_TIMEOUT) if any wait on a peer has given up."""
+        self._status_check(block=True)
+
     def uses_exchange(self, T: int) -> bool:
         return self.peer_ptrs is not None and T <= min(self.t_max, FUSED_MAX_T)
 
@@ -153,6 +236,7 @@ class EPGroup:
         """y[T,H] (full output on every rank) for replicated x[T,H].  `events`
         (5 CUDA event handles, as pmoe_block_forward_profiled takes) are recorded
         between the phases of a fused prefill call and ignored otherwise."""
+        self._status_check(block=False)
         T, H = x.shape
         w = list(weights)
         I, Is = w[1].shape[1] // 2, w[4].shape[0]
@@ -174,9 +258,12 @@ class EPGroup:
                 self.peer_arr, self.buf_bytes, self.rank, self.world, 0, y.data_ptr(),
                 ws.data_ptr(), nbytes, st)
             _lib.check("pmoe_block_forward_ep", s)
+            self._status_enqueue(st)
             return y
         if self.mode == "fused" and self.world > 1:
-            return self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st, events)
+            y = self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st, events)
+            self._status_enqueue(st)
+            return y
         if self.mode == "a2a" and self.world > 1:
             return self._forward_a2a(x, w, I, Is, y)
         s = self.lib.pmoe_block_forward_ep(
@@ -273,6 +360,8 @@ class EPGroup:
         (collective: every rank calls forward with the same T)."""
         if self.rx_local is not None and T <= self.rx_tmax:
             return
+        if not self.owns_buffers:
+            raise ValueError(f"emulated group: row buffers for {self.rx_tmax} tokens, got {T}")
         self._close_rows()
         nb = ctypes.c_size_t(0)
         _lib.check("pmoe_rows_fused_buffer_bytes",
@@ -312,6 +401,7 @@ class EPGroup:
         """One MoE-only decoder layer, x + block(RMSNorm(x)), full output on every
         rank (pmoe_layer_forward over the NVLink exchange; T <= t_max).  ``out``
         may be ``x`` (in-place residual update)."""
+        self._status_check(block=False)
         T, H = x.shape
         if not self.uses_exchange(T) and self.world > 1:
             raise ValueError("layer_forward across ranks needs the fused exchange (T <= t_max)")
@@ -332,17 +422,32 @@ class EPGroup:
             self.lo, self.hi, slo, shi, flags, peers, self.buf_bytes if peers else 0, self.rank,
             self.world, 0, y.data_ptr(), ws.data_ptr(), nbytes, st)
         _lib.check("pmoe_layer_forward", s)
+        if peers is not None:
+            self._status_enqueue(st)
         return y
 
     def close(self):
-        self._close_rows()
-        if self.peer_ptrs is not None:
-            torch.cuda.synchronize()
-            for r, p in enumerate(self.peer_ptrs):
-                if r != self.rank:
-                    self.lib.pmoe_ipc_close(p)
-            self.lib.pmoe_ipc_free(self.local_buf)
-            self.peer_ptrs = None
+        """Release the exchange buffers; raises PmoeError afterwards if a wait
+        on a peer gave up in any call since the last check."""
+        err = None
+        try:
+            self._status_check(block=True)
+        except _lib.PmoeError as e:
+            err = e
+        if self.owns_buffers:
+            self._close_rows()
+            if self.peer_ptrs is not None:
+                torch.cuda.synchronize()
+                for r, p in enumerate(self.peer_ptrs):
+                    if r != self.rank:
+                        self.lib.pmoe_ipc_close(p)
+                self.lib.pmoe_ipc_free(self.local_buf)
+        self.peer_ptrs = None
+        self.local_buf = None
+        self.rx_local = None
+        self._st_event = None
+        if err is not None:
+            raise err
 
 
 def patch_moe_for_ep(model, rank: int, world_size: int, mode: str = "fused") -> int:

@@ -105,20 +105,44 @@ def test_block_empty():
     assert block(x, g).shape == (0, 256)
 
 
-def test_block_prefill_zipf_streaming(full):
-    """T=8192 skewed routing through the streaming kernels: checked on a
-    sample of 256 tokens against the oracle (tokens are independent)."""
+@pytest.fixture(scope="module")
+def zipf8192():
+    """T=8192 Zipf workload and the oracle's output on its OWN routing (every
+    row; the GPU routing is bit-identical to it, checked here first)."""
     from paris_moe_b200 import workload as W
     wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=1.1)
-    g = wts.to("cuda")
     x = W.make_hidden(8192, W.MoEShape(), seed=0, zipf=True)
+    g = wts.to("cuda")
     xg = x.cuda()
+    y, oidx, _ = O.moe_block(bits(x), *[bits(t) for t in wts.tensors()], k=wts.shape.K)
+    idx, _ = route_of(xg, g)
+    assert np.array_equal(idx, oidx)
+    return wts, g, x, xg, y
+
+
+def test_block_prefill_zipf_streaming(zipf8192):
+    """T=8192 skewed routing through the streaming kernels, every row."""
+    wts, g, x, xg, ref = zipf8192
     y = block(xg, g, flags=F_SH | F_RT | F_STREAM)
-    route = route_of(xg, g)
-    rows = np.random.default_rng(0).choice(8192, 256, replace=False)
-    rows.sort()
-    assert_close(y.float().cpu().numpy()[rows], oracle_y(x, wts, route=route, rows=rows),
-                 "T=8192 sample")
+    assert_close(y, ref, "T=8192 streaming")
+
+
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_block_oracle_routing(full, T):
+    """End to end against the oracle's own routing (route=None): the GPU's
+    exactly rounded top-k makes the two routings identical."""
+    wts, g, x = full
+    xg = x[:T].cuda()
+    y = block(xg, g)
+    assert_close(y, oracle_y(x[:T], wts), f"T={T} oracle routing")
+
+
+@pytest.mark.parametrize("name", ["tiny_T1", "tiny_T5", "tiny_T33", "tiny_T200_zipf"])
+def test_block_tiny_golden_oracle_routing(name):
+    d, meta = load_golden(name)
+    shape, wts, x = golden_inputs(meta)
+    y = block(x.cuda(), wts.to("cuda"))
+    assert_close(y, oracle_y(x, wts), name)
 
 
 # ---- tcgen05 grouped-GEMM path (prefill) -----------------------------------
@@ -172,19 +196,11 @@ def test_block_prefill_tc_deterministic():
     assert torch.equal(a, b)
 
 
-def test_block_prefill_zipf_tc():
-    """Default path at T=8192 (tensor cores), skewed routing; 256 sampled rows."""
-    from paris_moe_b200 import workload as W
-    wts = W.make_weights(W.MoEShape(), seed=0, zipf_s=1.1)
-    g = wts.to("cuda")
-    x = W.make_hidden(8192, W.MoEShape(), seed=0, zipf=True)
-    xg = x.cuda()
+def test_block_prefill_zipf_tc(zipf8192):
+    """Default path at T=8192 (tensor cores), skewed routing, every row."""
+    wts, g, x, xg, ref = zipf8192
     y = block(xg, g)
-    route = route_of(xg, g)
-    rows = np.random.default_rng(1).choice(8192, 256, replace=False)
-    rows.sort()
-    assert_close(y.float().cpu().numpy()[rows], oracle_y(x, wts, route=route, rows=rows),
-                 "tc T=8192 sample")
+    assert_close(y, ref, "tc T=8192")
 
 
 @pytest.mark.parametrize("up_first", [False, True])

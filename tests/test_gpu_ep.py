@@ -65,6 +65,32 @@ def test_missing_peer_times_out_without_hanging():
     assert torch.isfinite(z.float()).all()
 
 
+def test_missing_peer_raises_through_epgroup():
+    """The same lost peer seen by the product path: EPGroup reads the sticky
+    status asynchronously and raises PmoeError(PMOE_ERR_PEER_TIMEOUT) at the
+    next call, at check() and at close()."""
+    from paris_moe_b200 import _lib, workload as W
+    from paris_moe_b200.ep import EPGroup
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=64, Is=64)
+    wts = W.make_weights(S, seed=1, device="cuda")
+    x = W.make_hidden(8, S, seed=1, device="cuda")
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_ep_buffer_bytes(64, S.H, S.K, ctypes.byref(nb)) == 0
+    bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    g = EPGroup.emulated(S.E, S.H, S.K, 0, 2, peer_bufs=[b.data_ptr() for b in bufs])
+    t0 = time.time()
+    g.forward(x, wts.tensors())                # rank 1 never runs: the combine gives up
+    with pytest.raises(_lib.PmoeError) as ei:
+        g.check()
+    assert ei.value.status == _lib.PMOE_ERR_PEER_TIMEOUT
+    with pytest.raises(_lib.PmoeError):        # sticky: the next call refuses
+        g.forward(x, wts.tensors())
+    with pytest.raises(_lib.PmoeError):
+        g.close()
+    assert time.time() - t0 < 60
+
+
 @pytest.mark.parametrize("T,flags", [(200, 3), (64, 3), (64, 3 | 4), (200, 2), (200, 1)])
 def test_rank_partials_sum_to_full(T, flags):
     """What each of 4 ranks returns without the exchange (its experts, its
@@ -174,6 +200,37 @@ def test_rows_fused_missing_peer_times_out():
     z = ops.moe_block(x, *wts.tensors(), S.K, 0, S.E, 3)
     torch.cuda.synchronize()
     assert torch.isfinite(z.float()).all()
+
+
+def test_rows_fused_missing_peer_raises_through_epgroup():
+    """Prefill row exchange with rank 1 absent, through EPGroup: rank 0's
+    waits give up, its combine, slice push and copy are skipped (y is left
+    as it was), and the group raises PMOE_ERR_PEER_TIMEOUT."""
+    from paris_moe_b200 import _lib, workload as W
+    from paris_moe_b200.ep import EPGroup
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=128, Is=128)
+    wts = W.make_weights(S, seed=2, device="cuda")
+    T = 200
+    x = W.make_hidden(T, S, seed=2, device="cuda")
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_rows_fused_buffer_bytes(T, S.H, S.K, ctypes.byref(nb)) == 0
+    bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    g = EPGroup.emulated(S.E, S.H, S.K, 0, 2, rows_bufs=[b.data_ptr() for b in bufs],
+                         rows_t_max=T)
+    y = torch.full_like(x, 7.0)
+    g.forward(x, wts.tensors(), out=y)
+    with pytest.raises(_lib.PmoeError) as ei:
+        g.check()
+    assert ei.value.status == _lib.PMOE_ERR_PEER_TIMEOUT
+    assert bool((y == 7.0).all())             # nothing was copied out
+    # and no slice was pushed into the absent peer's slice region (epoch 1:
+    # parity region 1 after the 1 KiB header); the down GEMM's row stores
+    # into its rows region happen before any wait and are expected
+    region = (T * S.H * 2 + 255) // 256 * 256
+    assert int(bufs[1][1024 + region:1024 + 2 * region].count_nonzero()) == 0
+    with pytest.raises(_lib.PmoeError):
+        g.close()
 
 
 @pytest.mark.parametrize("T", [200, 1000])

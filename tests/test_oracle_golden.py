@@ -115,3 +115,23 @@ def test_dispatch_empty_and_ragged():
     offs, st, ss = O.dispatch(idx, 8)
     assert offs.tolist() == [0, 1, 3, 3, 5, 5, 5, 5, 6]
     assert st.tolist() == [2, 0, 1, 0, 2, 1] and ss.tolist() == [1, 1, 0, 0, 0, 1]
+
+
+def test_router_logits_exactly_rounded():
+    """The oracle's logits equal the integer-arithmetic exact rounding, on
+    random rows and on crafted exact midpoints (ties to even) and near-midpoints."""
+    rng = np.random.default_rng(3)
+    x = O.f32_to_bf16(rng.standard_normal((6, 512)).astype(np.float32))
+    w = O.f32_to_bf16((rng.standard_normal((40, 512)) * 0.02).astype(np.float32))
+    lg = O.router_logits(x, w)
+    for t in range(6):
+        for e in range(0, 40, 3):
+            assert lg[t, e] == O.exact_logit_bf16(x[t], w[e])
+    one, eps, tiny = [O.f32_to_bf16(np.float32(v)) for v in (1.0, 2.0 ** -8, 2.0 ** -40)]
+    xx = np.zeros((3, 256), np.uint16)
+    ww = np.zeros((1, 256), np.uint16)
+    xx[:, 0], xx[:, 1] = one, eps                    # exact sum 1 + 2^-8: a midpoint
+    xx[1, 2] = tiny                                  # just above it
+    xx[2, 2] = tiny | 0x8000                         # just below it
+    ww[0, 0] = ww[0, 1] = ww[0, 2] = one
+    np.testing.assert_array_equal(O.router_logits(xx, ww)[:, 0], [1.0, 1.0 + 2 ** -7, 1.0])
