@@ -96,6 +96,17 @@ int pmoe_route_diag(const uint16_t* x, int T, int H, int E, int K, const uint16_
                     float* gamma, int32_t* stats, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* Exactly rounded router logits of all T x E (token, expert) pairs: logits[t*E + e]
+ * = the bf16 value (as fp32) nearest, ties to even, to the exact dot product
+ * of x[t] and w_router[e] (H % 256 == 0), by integer arithmetic on the
+ * GPU, one warp per pair.  *n_inexact (device int, incremented) counts pairs
+ * whose operands' exponent spread exceeds the exact window (expected 0).
+ * The top-k of pmoe_route evaluates only the few logits its error bound
+ * leaves open; this computes them all (tests, diagnostics).  No counterpart
+ * in the reference. */
+int pmoe_exact_logits(const uint16_t* x, int T, int H, int E, const uint16_t* w_router,
+                      float* logits, int32_t* n_inexact, void* stream);
+
 /* The whole MoE block, y[T,H] (bf16) =
  *     sum_k w_tk * down_e(SiLU(gate_e x) * up_e x)          (PMOE_F_ROUTED, e in [lo,hi))
  *   + sigmoid(x . w_sh_gvec) * shared_expert(x)             (PMOE_F_SHARED)

@@ -24,6 +24,7 @@ SIGNATURES = {
     "pmoe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "pmoe_route_diag": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_float),
                              ctypes.POINTER(_I), _P, _SZ, _P]),
+    "pmoe_exact_logits": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "pmoe_block_forward": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
                                 _I, _I, _I, _P, _P, _SZ, _P]),
     "pmoe_block_forward_profiled": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,

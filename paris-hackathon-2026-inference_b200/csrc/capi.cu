@@ -144,6 +144,20 @@ int pmoe_route_diag(const uint16_t* x, int T, int H, int E, int K, const uint16_
   return PMOE_OK;
 }
 
+int pmoe_exact_logits(const uint16_t* x, int T, int H, int E, const uint16_t* w_router,
+                      float* logits, int32_t* n_inexact, void* stream) {
+  if (T < 0 || H <= 0 || E <= 0 || H % 256 != 0) return PMOE_ERR_ARG;
+  if (T == 0) return PMOE_OK;
+  if (!x || !w_router || !logits || !n_inexact) return PMOE_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_router)) return PMOE_ERR_ALIGN;
+  int s = ensure_device();
+  if (s != PMOE_OK) return s;
+  return launch_exact_logits(bf(x), bf(w_router), T, H, E, logits, n_inexact,
+                             static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? PMOE_OK
+             : PMOE_ERR_CUDA;
+}
+
 // Decoder-layer extras: y = x + block(RMSNorm(x; w_norm, eps)).
 struct LayerArgs {
   const uint16_t* w_norm;

@@ -47,8 +47,6 @@ struct Workspace {
   int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
   int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M blocks; [4]/[5] the dispatched
                         //     rows [lo, hi) this call computes (row-split expert parallelism)
-  int32_t* comb_cnt;    // [T][H/128] stored row segments per token and 128-feature chunk
-                        //            (tensor-core path, combine fused into the down GEMM)
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
@@ -167,7 +165,6 @@ inline Workspace carve(void* base, const Dims& d) {
   w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 128 + 1));
   w.m_tiles = (int4*)take(sizeof(int4) * mt_max);
   w.tile_counts = (int32_t*)take(sizeof(int32_t) * 8);
-  w.comb_cnt = (int32_t*)take(sizeof(int32_t) * size_t(d.T) * (size_t(d.H) / 128 + 1));
   const size_t ntile = (size_t(d.T) + 127) / 128;
   w.hist = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
   w.hist_base = (int32_t*)take(sizeof(int32_t) * ntile * d.E);

@@ -56,6 +56,10 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
                              const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
                              float* shared_gate, int32_t* hist, int* status, float* logits,
                              float* xnorm, float* wnorm, float* diag, cudaStream_t st);
+// Exactly rounded logits of all T x E pairs (one warp each); n_inexact (a
+// device counter) counts pairs outside the exactness condition.
+cudaError_t launch_exact_logits(const __nv_bfloat16* x, const __nv_bfloat16* w, int T, int H,
+                                int E, float* out, int* n_inexact, cudaStream_t st);
 // Router-row norms for the exact top-k (one warp per row).
 cudaError_t launch_row_norms(const __nv_bfloat16* a, int rows, int H, float* out,
                              cudaStream_t st);

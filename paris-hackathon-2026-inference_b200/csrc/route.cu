@@ -94,6 +94,32 @@ __global__ void __launch_bounds__(256) row_norms_kernel(const __nv_bfloat16* __r
   if ((threadIdx.x & 31) == 0) out[r] = norm_from_sumsq(ss);
 }
 
+// Exactly rounded logits of every (token, expert) pair, one warp per pair
+// (test and diagnostic use: the full evaluation the top-k avoids).
+__global__ void __launch_bounds__(256) exact_logits_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ w,
+                                                           int T, int H, int E,
+                                                           float* __restrict__ out,
+                                                           int* __restrict__ n_inexact) {
+  const long p = long(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (p >= long(T) * E) return;
+  const int t = int(p / E), e = int(p % E);
+  bool ok = true;
+  const float r = warp_exact_dot(x + size_t(t) * H, w + size_t(e) * H, H, ok);
+  if ((threadIdx.x & 31) == 0) {
+    out[p] = r;
+    if (!ok) atomicAdd(n_inexact, 1);
+  }
+}
+
+cudaError_t launch_exact_logits(const __nv_bfloat16* x, const __nv_bfloat16* w, int T, int H,
+                                int E, float* out, int* n_inexact, cudaStream_t st) {
+  const long pairs = long(T) * E;
+  if (pairs == 0) return cudaSuccess;
+  exact_logits_kernel<<<unsigned((pairs + 7) / 8), 256, 0, st>>>(x, w, T, H, E, out, n_inexact);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_row_norms(const __nv_bfloat16* a, int rows, int H, float* out,
                              cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
@@ -226,13 +252,21 @@ constexpr int kFusedRouteThreads = 512;
 constexpr int kMaxRouteKS = 4;  // split-K factor of the decode router (Dims::KS)
 constexpr int kFusedRouteWarps = kFusedRouteThreads / 32;
 
+using FusedExact = ExactCta<kFusedRouteWarps, 32>;
+
+// Dynamic shared memory: the group's logits, the dispatch staging, and (at
+// a 16-byte aligned offset) the exact top-k queue.
+__host__ __device__ inline size_t fused_route_exact_offset(int T, int E, int K, int Rpad) {
+  const size_t b = sizeof(float) * size_t(T) * Rpad + sizeof(int) * size_t(T) * K +
+                   sizeof(float) * size_t(T) * K + sizeof(float) * T +
+                   sizeof(int) * size_t(kFusedRouteWarps) * E;
+  return (b + 15) / 16 * 16;
+}
 size_t fused_route_smem_bytes(int T, int E, int K, int Rpad) {
-  return sizeof(float) * size_t(T) * Rpad + sizeof(int) * size_t(T) * K +
-         sizeof(float) * size_t(T) * K + sizeof(float) * T +
-         sizeof(int) * size_t(kFusedRouteWarps) * E;
+  return fused_route_exact_offset(T, E, K, Rpad) + sizeof(FusedExact);
 }
 
-__global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
+__global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_router,
     const __nv_bfloat16* __restrict__ w_gvec, int T, int H, int E, int K, int Rpad, int KS,
     int lo, int hi, int with_shared, int with_routed, float* __restrict__ logit_part,
@@ -317,42 +351,81 @@ __global__ void __launch_bounds__(kFusedRouteThreads) route_fused_kernel(
   if (!s_last) return;
   __threadfence();
   const int t0 = tt * 32, nt = min(32, T - t0);
-  // Rpad is a multiple of 16: whole float4s; all KS partial loads in flight.
-  for (int i = tid; i < nt * Rpad / 4; i += kFusedRouteThreads) {
-    const size_t gi = size_t(t0) * Rpad / 4 + i;
-    float4 v[kMaxRouteKS];
+  // The norms' partial sums first (one round trip, overlapping the logits'),
+  // then the logits: Rpad is a multiple of 16, so whole float4s; two items
+  // per thread and iteration, all 2 * KS partial loads in flight.
+  float wss_r = 0.f, xss_t = 0.f;
+  {
+    float wv[kMaxRouteKS], xv[kMaxRouteKS];
 #pragma unroll
-    for (int k = 0; k < kMaxRouteKS; ++k)
-      if (k < KS)
-        v[k] = __ldcg(reinterpret_cast<const float4*>(logit_part + size_t(k) * T * Rpad) + gi);
-    float4 sum = v[0];
+    for (int k = 0; k < kMaxRouteKS; ++k) {
+      wv[k] = (k < KS && tid < E) ? __ldcg(wn_part + (size_t(tt) * KS + k) * Rpad + tid) : 0.f;
+      xv[k] = (k < KS && tid < nt) ? __ldcg(xn_part + size_t(k) * T + t0 + tid) : 0.f;
+    }
 #pragma unroll
-    for (int k = 1; k < kMaxRouteKS; ++k)
-      if (k < KS) {
-        sum.x += v[k].x; sum.y += v[k].y; sum.z += v[k].z; sum.w += v[k].w;
-      }
-    reinterpret_cast<float4*>(s_lg)[i] = sum;
-    if (diag) reinterpret_cast<float4*>(diag)[gi] = sum;
+    for (int k = 0; k < kMaxRouteKS; ++k) {
+      wss_r += wv[k];
+      xss_t += xv[k];
+    }
   }
-  for (int r = tid; r < E; r += kFusedRouteThreads) {
-    float s = 0.f;
-    for (int k = 0; k < KS; ++k) s += __ldcg(wn_part + (size_t(tt) * KS + k) * Rpad + r);
-    s_wn[r] = norm_from_sumsq(s);
+  static_assert(kFusedRouteThreads >= 256, "one thread per router row");
+  const int n4 = nt * Rpad / 4;
+  for (int i0 = tid; i0 < n4; i0 += 2 * kFusedRouteThreads) {
+    float4 v[2][kMaxRouteKS];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * kFusedRouteThreads;
+      const size_t gi = size_t(t0) * Rpad / 4 + (i < n4 ? i : 0);
+#pragma unroll
+      for (int k = 0; k < kMaxRouteKS; ++k)
+        if (k < KS)
+          v[u][k] = __ldcg(reinterpret_cast<const float4*>(logit_part + size_t(k) * T * Rpad) + gi);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * kFusedRouteThreads;
+      if (i >= n4) break;
+      float4 sum = v[u][0];
+#pragma unroll
+      for (int k = 1; k < kMaxRouteKS; ++k)
+        if (k < KS) {
+          sum.x += v[u][k].x; sum.y += v[u][k].y; sum.z += v[u][k].z; sum.w += v[u][k].w;
+        }
+      reinterpret_cast<float4*>(s_lg)[i] = sum;
+      if (diag) reinterpret_cast<float4*>(diag)[size_t(t0) * Rpad / 4 + i] = sum;
+    }
   }
-  if (tid < nt) {
-    float s = 0.f;
-    for (int k = 0; k < KS; ++k) s += __ldcg(xn_part + size_t(k) * T + t0 + tid);
-    s_xn[tid] = norm_from_sumsq(s);
-  }
+  if (tid < E) s_wn[tid] = norm_from_sumsq(wss_r);
+  if (tid < nt) s_xn[tid] = norm_from_sumsq(xss_t);
   for (int e = tid; e < 256; e += kFusedRouteThreads) s_cnt[e] = 0;
   __syncthreads();
   // accumulation depth: the MMA steps of one warp's slice, the sum over the
   // CTA's warps and the sum over the KS partials
-  const float gamma = float(2 * (slice / 32) + kFusedRouteWarps + KS) * kAccStepErr;
+  const float gamma = accumulation_gamma(2 * (slice / 32), kFusedRouteWarps + KS);
   const ExactStats stats{sync + 8, sync + 9};
-  for (int tl = warp; tl < nt; tl += kFusedRouteWarps)
-    warp_topk_token(s_lg + size_t(tl) * Rpad, s_xn[tl], s_wn, gamma, t0 + tl, E, K, x, w_router,
-                    H, stats, topk_idx, topk_w, shared_gate, s_cnt);
+  FusedExact& xq = *reinterpret_cast<FusedExact*>(
+      reinterpret_cast<char*>(s_dyn) + fused_route_exact_offset(T, E, K, Rpad));
+  if (tid == 0) {
+    xq.n_pend = 0;
+    xq.n_req = 0;
+  }
+  __syncthreads();
+  // two tokens per warp (tl, tl + 16), their fast checks interleaved
+  static_assert(2 * kFusedRouteWarps >= 32, "a 32-token group in one pass");
+  if (warp < nt) {
+    const int tl0 = warp, tl1 = warp + kFusedRouteWarps;
+    const bool v1 = tl1 < nt;
+    const float* r0 = s_lg + size_t(tl0) * Rpad;
+    const float* r1 = s_lg + size_t(v1 ? tl1 : tl0) * Rpad;
+    warp_topk_stage2(xq, [&](int i, int e) { return (i ? r1 : r0)[e]; }, s_wn, s_xn[tl0],
+                     s_xn[v1 ? tl1 : tl0], gamma, t0 + tl0, t0 + tl1, v1, E, K, x, w_router, H,
+                     stats, topk_idx, topk_w, s_cnt);
+    if (lane == 0) {
+      shared_gate[t0 + tl0] = 1.0f / (1.0f + expf(-r0[E]));
+      if (v1) shared_gate[t0 + tl1] = 1.0f / (1.0f + expf(-r1[E]));
+    }
+  }
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, s_cnt);
   __threadfence();
   __syncthreads();
   // Level 2: the last group to finish builds the dispatch for all tokens.
@@ -411,17 +484,27 @@ __global__ void __launch_bounds__(128) router_logits_kernel(
 
 // Warp per token over the logits of router_logits_kernel (one MMA chain of
 // H/16 steps per logit); wn: the router rows' norms (row_norms_kernel).
-__global__ void __launch_bounds__(256) topk_kernel(
+__global__ void __launch_bounds__(256, 2) topk_kernel(
     const float* __restrict__ logits, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w_router, const float* __restrict__ wn, int T, int H,
     int E, int K, int Rpad, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
     float* __restrict__ shared_gate, int32_t* __restrict__ counts, ExactStats stats) {
-  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (t >= T) return;
-  const float nx = norm_from_sumsq(warp_row_sumsq(x + size_t(t) * H, H));
-  const float gamma = float(H / 16 + 1) * kAccStepErr;
-  warp_topk_token(logits + size_t(t) * Rpad, nx, wn, gamma, t, E, K, x, w_router, H, stats,
-                  topk_idx, topk_w, shared_gate, counts);
+  __shared__ ExactCta<8, 8> xq;
+  if (threadIdx.x == 0) {
+    xq.n_pend = 0;
+    xq.n_req = 0;
+  }
+  __syncthreads();
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < T) {
+    const float nx = norm_from_sumsq(warp_row_sumsq(x + size_t(t) * H, H));
+    const float gamma = accumulation_gamma(H / 16, 1);
+    const float* row = logits + size_t(t) * Rpad;
+    warp_topk_stage(xq, [&](int e) { return row[e]; }, wn, nx, gamma, t, E, K, x, w_router, H,
+                    stats, topk_idx, topk_w, counts);
+    if ((threadIdx.x & 31) == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
+  }
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, counts);
 }
 
 constexpr int kDispatchThreads = 1024;
@@ -483,9 +566,9 @@ bool route_bumps_epoch(const Dims& d) { return d.T <= kFusedRouteMaxT; }
 float route_gamma(const Dims& d) {
   if (d.T <= kFusedRouteMaxT) {
     const int slice = (d.H / d.KS / kFusedRouteWarps + 31) / 32 * 32;
-    return float(2 * (slice / 32) + kFusedRouteWarps + d.KS) * kAccStepErr;
+    return accumulation_gamma(2 * (slice / 32), kFusedRouteWarps + d.KS);
   }
-  return float(d.H / 16 + 1) * kAccStepErr;
+  return accumulation_gamma(d.H / 16, 1);
 }
 
 cudaError_t route_init() {

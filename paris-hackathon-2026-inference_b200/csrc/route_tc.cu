@@ -47,11 +47,11 @@ constexpr int kRtTmemCols = 512;
 static_assert(kRtGateCol + kRtN2 <= kRtTmemCols, "TMEM columns");
 static_assert(kRtStageBytes % 1024 == 0, "stage alignment");
 
-// Accumulation depth of one logit: the MMA steps of the longest chain plus
-// the two fp32 additions of the chains.
-__host__ __device__ inline int router_tc_depth(int H) {
+// Accumulation bound of one logit: the MMA steps of the longest chain and
+// the fp32 additions of the chains.
+__host__ __device__ inline float router_tc_gamma(int H) {
   const int nk = H / kRtK;
-  return ((nk + kRtChains - 1) / kRtChains) * (kRtK / 16) + (kRtChains - 1);
+  return accumulation_gamma(((nk + kRtChains - 1) / kRtChains) * (kRtK / 16), kRtChains - 1);
 }
 
 __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRtStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 1 + 4);  // the MMA commit and the four epilogue warps
     }
     mbar_init(tfull, 1);
     mbar_fence_init();
@@ -136,28 +136,47 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
       if (ok) umma_commit(tfull);
     }
   } else {
-    // Epilogue warps 2..5.  While the MMAs run: the norms the exact top-k
-    // needs -- this half's 64 tokens of the tile and, on tile 0, this half's
-    // router rows (L2-resident reads, one warp per row).
-    const int wi = warp - 2;
-    for (int i = 0; i < 16; ++i) {
-      const int t = t0 + int(h) * 64 + wi * 16 + i;
-      if (t < T) {
-        const float ss = warp_row_sumsq(x + size_t(t) * H, H);
-        if (lane == 0) xnorm[t] = norm_from_sumsq(ss);
+    // Epilogue warps 2..5.  While the MMAs run they read every stage too and
+    // keep the sums of squares the exact top-k needs: thread r sums row r of
+    // the x tile (tokens t0 + r) and of this half's router rows (experts
+    // e0 + r); a stage is released once the MMAs and these four warps are
+    // done with it.  Within a swizzled 128-byte row the 16-byte chunks are
+    // permuted, which a sum over the whole row does not see.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    float ssx = 0.f, ssw = 0.f;
+    const uint32_t sb0 = smem_u32(smem);
+    bool fed = true;
+    for (int kc = 0; kc < nk; ++kc) {
+      const int s = kc % kRtStages;
+      if (!mbar_wait(&full[s], (kc / kRtStages) & 1)) {
+        atomicCAS(status, 0, kStatusTimeoutFull);
+        fed = false;
+        break;
       }
-    }
-    if (tile == 0)
-      for (int i = 0; i < 32; ++i) {
-        const int e = e0 + wi * 32 + i;
-        if (e < E) {
-          const float ss = warp_row_sumsq(w_router + size_t(e) * H, H);
-          if (lane == 0) wnorm[e] = norm_from_sumsq(ss);
+      const uint32_t ra = sb0 + s * kRtStageBytes + r * 128, rb = ra + kRtA;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t o = uint32_t(((c ^ (r & 7)) * 16));
+        const uint4 xv = lds128(ra + o), wv = lds128(rb + o);
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float x0 = __uint_as_float(xs[j] << 16), x1 = __uint_as_float(xs[j] & 0xFFFF0000u);
+          const float w0 = __uint_as_float(ws[j] << 16), w1 = __uint_as_float(ws[j] & 0xFFFF0000u);
+          ssx = fmaf(x0, x0, fmaf(x1, x1, ssx));
+          ssw = fmaf(w0, w0, fmaf(w1, w1, ssw));
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (fed) {
+      if (h == 0 && t0 + r < T) xnorm[t0 + r] = norm_from_sumsq(ssx);
+      if (tile == 0 && e0 + r < E) wnorm[e0 + r] = norm_from_sumsq(ssw);
+    }
     // One token row per thread: the chains' sum, in a fixed order, to global.
-    const int q = warp & 3;
-    const int t = t0 + q * 32 + lane;
+    const int t = t0 + r;
     if (mbar_wait(tfull, 0)) {
       tc_fence_after();
       const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16);
@@ -168,19 +187,29 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
         tmem_ld32(taddr + kRtNH + cc * 32, v1);
         tmem_ld32(taddr + 2 * kRtNH + cc * 32, v2);
         tmem_ld_wait();
-        if (t < T) {
-          float4* dst = reinterpret_cast<float4*>(logits + size_t(t) * Rpad + e0 + cc * 32);
+        // the row holds Rpad floats: columns past E (< 256 experts) are not stored
+        const int col0 = e0 + cc * 32;
+        if (t < T && col0 < E) {
+          float* dst = logits + size_t(t) * Rpad + col0;
+          if (col0 + 32 <= E) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float4 o;
-            o.x = (__uint_as_float(v0[i]) + __uint_as_float(v1[i])) + __uint_as_float(v2[i]);
-            o.y = (__uint_as_float(v0[i + 1]) + __uint_as_float(v1[i + 1])) +
-                  __uint_as_float(v2[i + 1]);
-            o.z = (__uint_as_float(v0[i + 2]) + __uint_as_float(v1[i + 2])) +
-                  __uint_as_float(v2[i + 2]);
-            o.w = (__uint_as_float(v0[i + 3]) + __uint_as_float(v1[i + 3])) +
-                  __uint_as_float(v2[i + 3]);
-            dst[i / 4] = o;
+            for (int i = 0; i < 32; i += 4) {
+              float4 o;
+              o.x = (__uint_as_float(v0[i]) + __uint_as_float(v1[i])) + __uint_as_float(v2[i]);
+              o.y = (__uint_as_float(v0[i + 1]) + __uint_as_float(v1[i + 1])) +
+                    __uint_as_float(v2[i + 1]);
+              o.z = (__uint_as_float(v0[i + 2]) + __uint_as_float(v1[i + 2])) +
+                    __uint_as_float(v2[i + 2]);
+              o.w = (__uint_as_float(v0[i + 3]) + __uint_as_float(v1[i + 3])) +
+                    __uint_as_float(v2[i + 3]);
+              reinterpret_cast<float4*>(dst)[i / 4] = o;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < E)
+                dst[i] = (__uint_as_float(v0[i]) + __uint_as_float(v1[i])) +
+                         __uint_as_float(v2[i]);
           }
         }
       }
@@ -202,11 +231,13 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   }
 }
 
-// Exact top-k over the router GEMM's logits: one CTA per 128-token tile
-// (16 warps, a token per warp at a time); writes the routing and the tile's
-// expert histogram.
-constexpr int kRtTopkThreads = 512;
-__global__ void __launch_bounds__(kRtTopkThreads, 1) route_topk_tc_kernel(
+// Exact top-k over the router GEMM's logits: a token per warp at a time, a
+// CTA per kRtTopkTokens tokens; each CTA adds its experts' counts into the
+// histogram of its 128-token tile (zeroed by the launcher).
+constexpr int kRtTopkThreads = 256;
+constexpr int kRtTopkTokens = 8;
+static_assert(kRtM % kRtTopkTokens == 0, "a CTA's tokens lie in one tile");
+__global__ void __launch_bounds__(kRtTopkThreads, 2) route_topk_tc_kernel(
     const float* __restrict__ logits, const float* __restrict__ xnorm,
     const float* __restrict__ wnorm, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w_router, int T, int H, int E, int K, int Rpad,
@@ -214,21 +245,31 @@ __global__ void __launch_bounds__(kRtTopkThreads, 1) route_topk_tc_kernel(
     float* __restrict__ shared_gate, int32_t* __restrict__ hist, ExactStats stats) {
   __shared__ int s_hist[kRtN];
   __shared__ float s_wn[kRtN];
+  __shared__ ExactCta<kRtTopkThreads / 32, kRtTopkTokens> xq;
   for (int e = threadIdx.x; e < kRtN; e += blockDim.x) {
     s_hist[e] = 0;
     s_wn[e] = e < E ? wnorm[e] : 0.f;
   }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5;
-  const int t0 = blockIdx.x * kRtM;
-  for (int i = warp; i < kRtM; i += kRtTopkThreads / 32) {
-    const int t = t0 + i;
-    if (t >= T) break;
-    warp_topk_token(logits + size_t(t) * Rpad, xnorm[t], s_wn, gamma, t, E, K, x, w_router, H,
-                    stats, topk_idx, topk_w, shared_gate, s_hist);
+  if (threadIdx.x == 0) {
+    xq.n_pend = 0;
+    xq.n_req = 0;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[size_t(blockIdx.x) * E + e] = s_hist[e];
+  const int warp = threadIdx.x >> 5;
+  const int t0 = blockIdx.x * kRtTopkTokens;
+  for (int i = warp; i < kRtTopkTokens; i += kRtTopkThreads / 32) {
+    const int t = t0 + i;
+    if (t >= T) break;
+    const float* row = logits + size_t(t) * Rpad;
+    warp_topk_stage(xq, [&](int e) { return row[e]; }, s_wn, xnorm[t], gamma, t, E, K, x,
+                    w_router, H, stats, topk_idx, topk_w, s_hist);
+    if ((threadIdx.x & 31) == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
+  }
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, s_hist);
+  __syncthreads();
+  int32_t* h = hist + size_t(t0 / kRtM) * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (s_hist[e]) atomicAdd(&h[e], s_hist[e]);
 }
 
 // ---------------------------------------------------------------------------
@@ -359,7 +400,7 @@ cudaError_t route_tc_init() {
                               kRtSmem);
 }
 
-float route_tc_gamma(const Dims& d) { return float(router_tc_depth(d.H)) * kAccStepErr; }
+float route_tc_gamma(const Dims& d) { return router_tc_gamma(d.H); }
 
 bool route_tc_supported(const Dims& d) {
   return d.E <= kRtN && d.K <= kRtMaxK && d.H % kRtK == 0;
@@ -412,8 +453,10 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
                           cudaMemcpyDeviceToDevice, st);
     if (err != cudaSuccess) return err;
   }
-  const float gamma = float(router_tc_depth(d.H)) * kAccStepErr;
-  route_topk_tc_kernel<<<nb, kRtTopkThreads, 0, st>>>(
+  const float gamma = router_tc_gamma(d.H);
+  err = cudaMemsetAsync(hist, 0, sizeof(int32_t) * size_t(nb) * d.E, st);
+  if (err != cudaSuccess) return err;
+  route_topk_tc_kernel<<<(d.T + kRtTopkTokens - 1) / kRtTopkTokens, kRtTopkThreads, 0, st>>>(
       logits, xnorm, wnorm, x, w_router, d.T, d.H, d.E, d.K, d.Rpad, gamma, topk_idx, topk_w,
       shared_gate, hist, ExactStats{status + 8, status + 9});
   return cudaGetLastError();

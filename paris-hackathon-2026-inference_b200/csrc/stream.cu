@@ -78,6 +78,7 @@ struct UnitRing {
   uint64_t full[kUnitSlots];
   uint64_t empty[kUnitSlots];
   int unit[kUnitSlots];
+  int4 info[kUnitSlots];  // optional per-unit facts the producer already loaded
 
   __device__ void init() {
     for (int i = 0; i < kUnitSlots; ++i) {
@@ -91,11 +92,12 @@ struct UnitRing {
     return q < n_units ? n_units - 1 - q : -1;
   }
   // Producer: hand unit `u` to the consumers in hand-off `ui`.
-  __device__ bool publish_unit(uint32_t ui, int u) {
+  __device__ bool publish_unit(uint32_t ui, int u, int4 inf = make_int4(0, 0, 0, 0)) {
     const int slot = ui % kUnitSlots;
     if (ui >= uint32_t(kUnitSlots) && !mbar_wait(&empty[slot], ((ui / kUnitSlots) & 1) ^ 1))
       return false;
     unit[slot] = u;
+    info[slot] = inf;
     mbar_arrive(&full[slot]);
     return true;
   }
@@ -104,13 +106,15 @@ struct UnitRing {
     return publish_unit(ui, *out_unit);
   }
   // Consumer warp: unit published in hand-off `ui`.
-  __device__ bool take(uint32_t ui, int lane, int* out_unit) {
+  __device__ bool take(uint32_t ui, int lane, int* out_unit, int4* out_info = nullptr) {
     const int slot = ui % kUnitSlots;
     if (!mbar_wait(&full[slot], (ui / kUnitSlots) & 1)) return false;
     const int u = unit[slot];
+    const int4 inf = info[slot];
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     *out_unit = u;
+    if (out_info) *out_info = inf;
     return true;
   }
 };
@@ -322,23 +326,30 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     int u_next = ur.ticket(queue, n_units);
     for (uint32_t ui = 0;; ++ui) {
       const int u = u_next;
-      if (!ur.publish_unit(ui, u)) {
+      // the unit's expert and rows go to the consumers with the unit, so they
+      // do not repeat these dependent global loads
+      int e = 0, p0 = 0, n = 0;
+      if (u >= 0) {
+        e = tb.active[u / UR];
+        p0 = tb.offsets[e];
+        n = tb.offsets[e + 1] - p0;
+      }
+      if (!ur.publish_unit(ui, u, make_int4(e, p0, n, 0))) {
         set_status(status, kStatusTimeoutEmpty);
         drain(full, it, kStages);
         return;
       }
       if (u < 0) break;
       u_next = ur.ticket(queue, n_units);
-      const int e = tb.active[u / UR], rbg = u % UR;
+      const int rbg = u % UR;
       const bool sh = (e == E);
       const int nkc = (sh ? Is : I) / (kKC * KCH);
-      const int p0 = tb.offsets[e];
-      const int n = tb.offsets[e + 1] - p0;
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
-      for (int sub = 0; sub < row_blocks; ++sub) {
-      const int rb = rbg * row_blocks + sub;
-      const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
+      // passes of up to 32 dispatched rows, each over the unit's row blocks
       for (int nb = 0; nb < n; nb += kActRows) {
+      for (int sub = 0; sub < row_blocks; ++sub) {
+        const int rb = rbg * row_blocks + sub;
+        const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
         // passes of at most 8 rows load an 8-row activation box (1 KiB/chunk)
         const bool small = n - nb <= 8;
         const CUtensorMap* mh = small ? &tm_h8 : &tm_h;
@@ -360,7 +371,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
           }
         }
       }
-      }  // sub
+      }  // nb
     }
     return;
   }
@@ -371,20 +382,32 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
   uint32_t it = 0;
   for (uint32_t ui = 0;; ++ui) {
     int u;
-    if (!ur.take(ui, lane, &u)) {
+    int4 inf;
+    if (!ur.take(ui, lane, &u, &inf)) {
       set_status(status, kStatusTimeoutFull);
       return;
     }
     if (u < 0) break;
-    const int e = tb.active[u / UR], rbg = u % UR;
+    const int e = inf.x, p0 = inf.y, n = inf.z, rbg = u % UR;
     const bool sh = (e == E);
     const int nkc = (sh ? Is : I) / (kKC * KCH);
-    const int p0 = tb.offsets[e];
-    const int n = tb.offsets[e + 1] - p0;
-    for (int sub = 0; sub < row_blocks; ++sub) {
-    const int rb = rbg * row_blocks + sub;
     for (int nb = 0; nb < n; nb += kActRows) {
-      const int ng = min(4, (n - nb + 7) / 8);
+    const int ng = min(4, (n - nb + 7) / 8);
+    // this lane's output rows of the pass (weight, destination), loaded once
+    // for all of the unit's row blocks, before the first stage wait
+    float wt[4][2];
+    int dsti[4][2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = nb + q * 8 + 2 * c + hh;
+        const bool ok = q < ng && i < n;
+        wt[q][hh] = ok ? tb.pair_w[p0 + i] : 0.f;
+        dsti[q][hh] = ok ? tb.pair_dst[p0 + i] : -1;
+      }
+    for (int sub = 0; sub < row_blocks; ++sub) {
+      const int rb = rbg * row_blocks + sub;
       float acc[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
         const int s = it % kStages;
@@ -417,14 +440,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q < ng) {
-          const int i = nb + q * 8 + 2 * c;
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            if (i + hh < n) {
-              const int p = p0 + i + hh;
-              const float wt = tb.pair_w[p];
-              const size_t off = size_t(tb.pair_dst[p]) * H;
-              const float v0 = acc[q][hh] * wt, v1 = acc[q][2 + hh] * wt;
+            if (dsti[q][hh] >= 0) {
+              const float wk = wt[q][hh];
+              const size_t off = size_t(dsti[q][hh]) * H;
+              const float v0 = acc[q][hh] * wk, v1 = acc[q][2 + hh] * wk;
               if (ep.world > 0) {
                 // every computed row goes to every rank (peer stores over NVLink)
                 for (int rr = 0; rr < ep.world; ++rr) {
@@ -442,7 +463,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
         }
       }
     }
-    }  // sub
+    }  // nb
   }
   if (ep.world > 0) {
     // All of this warp's peer stores are made visible system-wide before it

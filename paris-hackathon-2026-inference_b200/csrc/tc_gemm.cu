@@ -49,14 +49,8 @@ constexpr int kTcStageBytes = kWBytes + kRowBytes;  // 32 KiB
 constexpr int kEpiWarps = 16;  // four per TMEM lane quadrant, each owning 64 columns
 constexpr int kEpiWarpBytes = 32 * 16 * 2;  // per-warp gate_up staging tile (bf16 32 x 16)
 constexpr int kBarBytes = 256;            // mbarriers + TMEM slot
-// down with the fused combine: per column quarter, the list of tokens whose
-// every row segment of this CTA's 128 features is now stored (64 + 1 ints)
-constexpr int kFuseListInts = 68;
-constexpr int kFuseBytes = 4 * kFuseListInts * 4;
-constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps * kEpiWarpBytes +
-                        kFuseBytes;
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + kBarBytes + kEpiWarps * kEpiWarpBytes;
 constexpr int kTcThreads = 32 * (2 + kEpiWarps);
-constexpr int kCombineMaxKFused = 8;      // top-k sizes the fused down combine handles
 constexpr uint32_t kTmemCols = 512;       // two 256-column fp32 accumulators
 static_assert(kTcSmem <= 227 * 1024, "shared memory");
 // barrier area: 16 mbarriers (128 B), the TMEM slot at 128, four abort flags at 192
@@ -71,19 +65,9 @@ struct TileTables {
   const float* pair_w;
   RowsOut out;              // down: peer destinations (out.world > 0) of the rows
   int T, K;                 // for the token of a token-major row
+  int sh_lo;                // first token of the shared expert's rows
   int sh5;                  // gate_up: shared gate|up in one 5-D map (tm_b_sh0)
   int sh_swap;              // ... whose first half is the up rows (w_sh_up < w_sh_gate)
-  // down, fused combine (fuse != 0; every token has all K routed rows and
-  // its shared row on this GPU): cnt[t * (H/128) + c] counts the stored
-  // 128-feature segments c of token t's rows; the epilogue that stores the
-  // last of them sums the token's segments into y (see the down epilogue).
-  int fuse;
-  int* cnt;
-  const int32_t* topk_idx;
-  const float* topk_w;
-  const float* shared_gate;
-  const __nv_bfloat16* resid;  // decoder layer: y = bf16(resid + bf16(sum)); may be null
-  __nv_bfloat16* y;
 };
 
 __device__ __forceinline__ uint8_t* tc_align1024(uint8_t* p) {
@@ -96,94 +80,6 @@ __device__ __forceinline__ void tc_status(int* status, int code) { atomicCAS(sta
 // tile's descriptor one tile ahead).
 __device__ __forceinline__ int4 tile_at(const TileTables& tt, int t, int ntiles) {
   return t < ntiles ? tt.tiles[t] : make_int4(0, 0, 0, 0);
-}
-
-// Fused routing-weighted combine of the down GEMM (single GPU, every row of
-// every token computed here).  Called by the four warps of a column quarter
-// after they stored the segments [fq, fq + 128) of the tile's columns
-// cw .. cw + 63 (dispatched rows; ldst = their token-major rows, lane-indexed
-// per 32-column half, identical in the four warps).  Each stored segment
-// increments its token's counter for this 128-feature chunk; the store that
-// completes a token's K + 1 segments (counter reaches K + 1) makes this quarter
-// sum them: y[t, fq .. fq+127] = bf16(sum_k w_tk * row_k + g_t * row_shared)
-// in fp32, k = 0..K-1 then the shared row, exactly as combine_rows_tok_kernel
-// (bit-identical results).  The counter is reset for the next call.
-// Ordering: stores -> __threadfence -> atomicAdd; the last adder's
-// atomicAdd -> __threadfence -> L2 loads (ld.cg).
-__device__ __forceinline__ void down_fused_combine(const TileTables& tt, int H, int fq,
-                                                   int quarter, int q, int lane, int cw,
-                                                   int nrows, const int (&ldst)[2],
-                                                   const __nv_bfloat16* __restrict__ rows,
-                                                   int* s_list) {
-  const int bar_id = 1 + quarter;
-  const int tq = q * 32 + lane;  // 0..127 within the quarter
-  const int nch = H / 128, ch = fq / 128;
-  const int tk = tt.T * tt.K;
-  __threadfence();
-  if (tq == 0) s_list[64] = 0;
-  named_bar_sync(bar_id, 128);
-  if (q < 2) {
-    const int col = cw + tq;  // warp q < 2 holds this column's row in ldst[q]
-    const int dst = q == 0 ? ldst[0] : ldst[1];
-    if (col < nrows) {
-      const int t = dst < tk ? dst / tt.K : dst - tk;
-      int* c = tt.cnt + size_t(t) * nch + ch;
-      if (atomicAdd(c, 1) == tt.K) {  // this store completed the token's K + 1 segments
-        *c = 0;                       // ready for the next call
-        s_list[atomicAdd(&s_list[64], 1)] = t;
-      }
-    }
-  }
-  named_bar_sync(bar_id, 128);
-  const int n = s_list[64];
-  const int part = tq & 15;  // 16 threads x 8 features per token
-  for (int i = tq >> 4; i < n; i += 8) {
-    const int t = s_list[i];
-    __threadfence();
-    float w[kCombineMaxKFused + 1];
-    uint4 v[kCombineMaxKFused + 1];
-#pragma unroll
-    for (int k = 0; k < kCombineMaxKFused; ++k)
-      if (k < tt.K) w[k] = __ldcg(tt.topk_w + size_t(t) * tt.K + k);
-    w[kCombineMaxKFused] = __ldcg(tt.shared_gate + t);
-#pragma unroll
-    for (int k = 0; k <= kCombineMaxKFused; ++k) {
-      const size_t r = k < kCombineMaxKFused ? size_t(t) * tt.K + k : size_t(tk) + t;
-      if (k < tt.K || k == kCombineMaxKFused)
-        v[k] = __ldcg(reinterpret_cast<const uint4*>(rows + r * H + fq) + part);
-    }
-    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int k = 0; k <= kCombineMaxKFused; ++k) {
-      if (!(k < tt.K || k == kCombineMaxKFused)) continue;
-      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v[k]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(b2[j]);
-        s[2 * j] = fmaf(w[k], f.x, s[2 * j]);
-        s[2 * j + 1] = fmaf(w[k], f.y, s[2 * j + 1]);
-      }
-    }
-    if (tt.resid) {  // decoder layer: y = bf16(resid + bf16(sum))
-      const uint4 rv = __ldg(reinterpret_cast<const uint4*>(tt.resid + size_t(t) * H + fq) + part);
-      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(r2[j]);
-        s[2 * j] = f.x + bf16_round(s[2 * j]);
-        s[2 * j + 1] = f.y + bf16_round(s[2 * j + 1]);
-      }
-    }
-    uint4 o;
-    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * j], s[2 * j + 1]);
-      op[j] = *reinterpret_cast<uint32_t*>(&b2);
-    }
-    reinterpret_cast<uint4*>(tt.y + size_t(t) * H + fq)[part] = o;
-  }
-  (void)nch;
 }
 
 // One persistent kernel per GEMM, launched as CTA pairs (clusters of 2).  A
@@ -204,12 +100,16 @@ __device__ __forceinline__ void down_fused_combine(const TileTables& tt, int H, 
 // accumulator on the even CTA's barrier.
 // tm_b: routed weights (5-D for gate_up), tm_b_sh0/1: shared-expert weights
 // (16-row boxes for gate_up), tm_a / tm_a32: the dispatched rows (x_perm for
-// gate_up, h for down) in 128- and 32-row boxes.
+// gate_up, h for down) in 128- and 32-row boxes; tm_x / tm_x32: gate_up's
+// shared-expert rows, which are the tokens sh_lo.. in order, read from x
+// itself (x_perm holds no copy of them).
 template <int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b_sh0,
     const __grid_constant__ CUtensorMap tm_b_sh1, const __grid_constant__ CUtensorMap tm_a,
-    const __grid_constant__ CUtensorMap tm_a32, const __grid_constant__ TileTables tt, int H, int E, int I, int Is,
+    const __grid_constant__ CUtensorMap tm_a32, const __grid_constant__ CUtensorMap tm_x,
+    const __grid_constant__ CUtensorMap tm_x32, const __grid_constant__ TileTables tt, int H,
+    int E, int I, int Is,
     int ldh, __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ out_rows,
     int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
@@ -254,6 +154,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
     if (lane == 0) {
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_a);
+      if (MODE == kGateUp) prefetch_tmap(&tm_x);
       const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // even CTA's stage barriers
       uint32_t it = 0;
       bool ok = true;
@@ -298,12 +199,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
             else
               tma_load_2d_pair(st, &tm_b, kc * kBK, e * H + f0, fb);
           }
+          // gate_up's shared rows P + i are token sh_lo + i: straight from x
+          const bool from_x = MODE == kGateUp && sh;
+          const int ra = from_x ? r0 - tt.T * tt.K + tt.sh_lo : r0;
+          const CUtensorMap* ma = from_x ? &tm_x : &tm_a;
+          const CUtensorMap* ma32 = from_x ? &tm_x32 : &tm_a32;
           if (whole) {
-            tma_load_2d_pair(st + kWBytes, &tm_a, kc * kBK, r0, fb);
+            tma_load_2d_pair(st + kWBytes, ma, kc * kBK, ra, fb);
           } else {
             for (int j = 0; j < nchunks; ++j)
-              tma_load_2d_pair(st + kWBytes + j * kRowChunk * kBK * 2, &tm_a32, kc * kBK,
-                               r0 + j * kRowChunk, fb);
+              tma_load_2d_pair(st + kWBytes + j * kRowChunk * kBK * 2, ma32, kc * kBK,
+                               ra + j * kRowChunk, fb);
           }
         }
       }
@@ -476,17 +382,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_pair_kernel(
             }
           }
         }
-        if (tt.fuse) {
-          // The accumulator is read: release it before the combine work.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty0 + b * 8);
-          down_fused_combine(tt, H, fq, quarter, q, lane, cw, nrows, ldst, out_rows,
-                             reinterpret_cast<int*>(smem + kTcStages * kTcStageBytes +
-                                                    kBarBytes + kEpiWarps * kEpiWarpBytes) +
-                                 quarter * kFuseListInts);
-          continue;
-        }
       }
       tc_fence_before();
       __syncwarp();
@@ -516,7 +411,7 @@ constexpr int kGatherMaxH8 = 8;  // H <= 2048 for the unrolled row copy
 
 __global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(
     const __nv_bfloat16* __restrict__ x, const int4* __restrict__ m_tiles,
-    const int32_t* __restrict__ count, const int32_t* __restrict__ sorted_tok, int H,
+    const int32_t* __restrict__ count, const int32_t* __restrict__ sorted_tok, int H, int E,
     __nv_bfloat16* __restrict__ x_perm) {
   const int lane = threadIdx.x & 31;
   constexpr int kItems = kGatherRows / kGatherItemRows;
@@ -525,6 +420,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(
   for (int w = blockIdx.x * (kGatherThreads / 32) + (threadIdx.x >> 5); w < nw;
        w += gridDim.x * (kGatherThreads / 32)) {
     const int4 tl = m_tiles[w / kItems];
+    if (tl.x == E) continue;  // the shared expert's rows are read from x itself
     const int r_beg = (w % kItems) * kGatherItemRows;
     const int r_end = min(tl.z, r_beg + kGatherItemRows);
     for (int r = r_beg; r < r_end; r += 2) {
@@ -903,16 +799,6 @@ __global__ void __launch_bounds__(256) combine_rows_tok_kernel(
 namespace {
 int g_pairs = 74;  // co-resident CTA pairs of the GEMM kernels
 
-// PMOE_UNFUSED_COMBINE=1 runs the combine as its own kernel after the down
-// GEMM (for measuring the fusion; the results are bit-identical).
-bool fused_combine_disabled() {
-  static const bool off = [] {
-    const char* v = std::getenv("PMOE_UNFUSED_COMBINE");
-    return v && v[0] == '1';
-  }();
-  return off;
-}
-
 // Per-block cost constant of the row split, in rows: 512 (two full blocks'
 // rows) evens out the GEMM tile count per rank where few tiles per rank make
 // the last round of the persistent grid decide the time, and keeps rows even
@@ -989,7 +875,7 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
   };
   const uint64_t H = d.H, I = d.I, Is = d.Is, E = d.E, T = d.T;
   const uint64_t P = T * d.K, R = P + T, ldh = d.ldh;
-  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h, tm_h32, tm_xp, tm_xp32;
+  CUtensorMap tm_gu, tm_sg, tm_su, tm_dn, tm_sd, tm_h, tm_h32, tm_xp, tm_xp32, tm_x, tm_x32;
   // gate_up weights [E][2I][H] seen as (k, row in group, gate|up, group, expert):
   // one box = 4 groups of 16 gate rows, each followed by its 16 up rows.
   const uint64_t gu_dims[5] = {H, 16, 2, I / 16, E};
@@ -1003,14 +889,16 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
       !make_tmap_bf16_2d(&tm_h, ws.h, ldh, R, ldh * 2, kBK, kHalfTok) ||
       !make_tmap_bf16_2d(&tm_h32, ws.h, ldh, R, ldh * 2, kBK, kRowChunk) ||
       !make_tmap_bf16_2d(&tm_xp, ws.x_perm, H, R, H * 2, kBK, kHalfTok) ||
-      !make_tmap_bf16_2d(&tm_xp32, ws.x_perm, H, R, H * 2, kBK, kRowChunk))
+      !make_tmap_bf16_2d(&tm_xp32, ws.x_perm, H, R, H * 2, kBK, kRowChunk) ||
+      !make_tmap_bf16_2d(&tm_x, x, H, T, H * 2, kBK, kHalfTok) ||
+      !make_tmap_bf16_2d(&tm_x32, x, H, T, H * 2, kBK, kRowChunk))
     return cudaErrorInvalidValue;
   plan_tiles_kernel<<<1, kPlanThreads, 0, st>>>(ws.offsets, ws.active, ws.n_active, d.E, d.H,
                                                 d.I, d.Is, rank, world, split_c0(),
                                                 ws.gu_tiles,
                                                 ws.dn_tiles, ws.m_tiles, ws.tile_counts);
   gather_rows_kernel<<<2 * g_pairs * 16, kGatherThreads, 0, st>>>(
-      x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, ws.x_perm);
+      x, ws.m_tiles, ws.tile_counts + 2, ws.sorted_tok, d.H, d.E, ws.x_perm);
   cudaError_t err = mark(0);
   if (err != cudaSuccess) return err;
   int* status = ws.status + 1;
@@ -1034,36 +922,19 @@ cudaError_t launch_tc_experts(const Dims& d, const __nv_bfloat16* x,
     }
   }
   TileTables gu{ws.gu_tiles, ws.tile_counts, ws.pair_dst, ws.pair_w, RowsOut{}, d.T, d.K,
-                sh5, sh_swap};
+                d.sh_lo, sh5, sh_swap};
   TileTables dn{ws.dn_tiles, ws.tile_counts + 1, ws.pair_dst, ws.pair_w,
-                rows_out ? *rows_out : RowsOut{}, d.T, d.K, 0, 0};
-  // The routing-weighted combine runs inside the down GEMM's epilogue when
-  // this GPU computes every row of every token (no expert or row split).
-  const bool fuse = !rows_out && world == 1 && lo == 0 && hi == d.E && with_routed &&
-                    with_shared && d.sh_lo == 0 && d.sh_hi == d.T && d.K <= kCombineMaxKFused &&
-                    d.H % 128 == 0 && !fused_combine_disabled();
-  if (fuse) {
-    dn.fuse = 1;
-    dn.cnt = ws.comb_cnt;
-    dn.topk_idx = ws.topk_idx;
-    dn.topk_w = ws.topk_w;
-    dn.shared_gate = ws.shared_gate;
-    dn.resid = resid;
-    dn.y = y;
-    err = cudaMemsetAsync(ws.comb_cnt, 0, sizeof(int) * size_t(d.T) * (d.H / 128), st);
-    if (err != cudaSuccess) return err;
-  }
-  err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, gu, d.H, d.E, d.I, d.Is,
-                              d.ldh, ws.h, ws.rows_bf16, status);
+                rows_out ? *rows_out : RowsOut{}, d.T, d.K, d.sh_lo, 0, 0};
+  err = launch_pairs<kGateUp>(st, tm_gu, tm_sg, tm_su, tm_xp, tm_xp32, tm_x, tm_x32, gu, d.H, d.E,
+                              d.I, d.Is, d.ldh, ws.h, ws.rows_bf16, status);
   if (err != cudaSuccess) return err;
   err = mark(1);
   if (err != cudaSuccess) return err;
-  err = launch_pairs<kDown>(st, tm_dn, tm_sd, tm_sd, tm_h, tm_h32, dn, d.H, d.E, d.I, d.Is,
-                            d.ldh, ws.h, ws.rows_bf16, status);
+  err = launch_pairs<kDown>(st, tm_dn, tm_sd, tm_sd, tm_h, tm_h32, tm_h, tm_h32, dn, d.H, d.E,
+                            d.I, d.Is, d.ldh, ws.h, ws.rows_bf16, status);
   if (err != cudaSuccess) return err;
   err = mark(2);
   if (err != cudaSuccess) return err;
-  if (fuse) return cudaSuccess;                             // y is complete
   if (rows_out && rows_out->world > 0) return cudaSuccess;  // the token owners combine
   const long n8 = long(T) * d.H / 8;
   const int* pp = world > 1 ? ws.pair_pos : nullptr;

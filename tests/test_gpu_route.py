@@ -37,8 +37,10 @@ def check_route(x, wts, idx, w):
     oidx, ow = O.topk_route(logits, wts.shape.K)
     bad = np.nonzero(np.any(idx != oidx, axis=-1))[0]
     assert bad.size == 0, f"{bad.size} tokens differ, first {bad[:5]}: {idx[bad[:2]]} vs {oidx[bad[:2]]}"
-    close = np.all(np.isclose(w, ow, rtol=3e-6, atol=1e-7), axis=-1)
-    assert close.mean() >= 0.999, close.mean()
+    close = np.all(np.isclose(w, ow, rtol=1e-5, atol=1e-7), axis=-1)
+    # a weight uses the approximate logit's rounding where the bound did not call for
+    # an exact evaluation; that moves the rare row by one bf16 ulp of a logit
+    assert close.mean() >= 0.99, close.mean()
     np.testing.assert_allclose(w, ow, atol=0.05)
     return oidx
 
@@ -182,3 +184,50 @@ def test_route_all_tied_logits(T):
     idx, w, offs, stok, sslot, sg = ops.moe_route(x, wts.w_router, wts.w_sh_gvec, 8)
     assert (idx.cpu() == torch.arange(8, dtype=torch.int32)).all()
     assert torch.allclose(w.cpu(), torch.full((T, 8), 1 / 8))
+
+
+def _exact_logits_gpu(x, w):
+    from paris_moe_b200 import _lib
+    lib = _lib.load()
+    T, H = x.shape
+    E = w.shape[0]
+    xg, wg = x.cuda().contiguous(), w.cuda().contiguous()
+    out = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    bad = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.check("pmoe_exact_logits", lib.pmoe_exact_logits(
+        xg.data_ptr(), T, H, E, wg.data_ptr(), out.data_ptr(), bad.data_ptr(),
+        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), int(bad.item())
+
+
+def test_exact_logits_all_pairs_bit_exact():
+    """The GPU's exact evaluation on every (token, expert) pair equals the
+    oracle's exactly rounded logits bit for bit: the full decode batch, Zipf
+    rows, and rows that take the general (integer-field) path -- bf16
+    subnormals, exact zeros, huge and tiny entries, exact midpoints."""
+    from paris_moe_b200 import workload as W
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=11, zipf_s=1.1)
+    x = W.make_hidden(64, S, seed=11, zipf=True)
+    got, bad = _exact_logits_gpu(x, wts.w_router)
+    want = O.router_logits(bits(x), bits(wts.w_router))
+    diff = np.argwhere(got != want)
+    assert diff.size == 0, (diff[:5], got[tuple(diff[:5].T)], want[tuple(diff[:5].T)])
+    assert bad == 0
+    f = lambda v: torch.tensor(v, dtype=torch.float32).to(torch.bfloat16)
+    xs = torch.zeros((6, 256), dtype=torch.bfloat16)
+    ws = (torch.randn((40, 256), generator=torch.Generator().manual_seed(3)) * 0.02).bfloat16()
+    xs[0] = (torch.randn(256, generator=torch.Generator().manual_seed(4))).bfloat16()
+    xs[1] = (xs[0].float() * 2.0 ** -122).bfloat16()                          # subnormals
+    xs[2] = xs[0] * f(2.0 ** 60)                                               # huge
+    xs[3, :2] = f(1.0)
+    xs[3, 2] = f(2.0 ** -8)                                                    # midpoints
+    xs[4] = xs[0]
+    xs[4, 5] = f(2.0 ** -60)                                                   # wide spread
+    ws[0, :3] = f(1.0)
+    got, bad = _exact_logits_gpu(xs, ws)
+    want = O.router_logits(bits(xs), bits(ws))
+    diff = np.argwhere(got != want)
+    assert diff.size == 0, (diff[:5], got[tuple(diff[:5].T)], want[tuple(diff[:5].T)])
+    assert bad == 0
