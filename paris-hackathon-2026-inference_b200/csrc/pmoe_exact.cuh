@@ -657,7 +657,8 @@ struct ExactCta {
   int n_pend, n_req;
 };
 
-// Writes token t's routing from lane k's (expert, bf16 logit).
+// Writes token t's routing from lane k's (expert, bf16 logit); cnt: the
+// expert counts this token is added to.
 __device__ __forceinline__ void warp_write_route(int t, int K, int e, float v,
                                                  int32_t* __restrict__ topk_idx,
                                                  float* __restrict__ topk_w, int* cnt) {
@@ -673,12 +674,12 @@ __device__ __forceinline__ void warp_write_route(int t, int K, int e, float v,
 // Queue token t, which the fast check could not settle (gx = gamma * slack
 // * ||x_t||): its candidates' intervals and the exact evaluations they need;
 // a token that does not fit the queue is settled here by warp_select_intervals.
-template <int NW, int MAXPEND, typename LogitFn>
+template <int NW, int MAXPEND, typename LogitFn, typename CntFn>
 __device__ __forceinline__ void warp_topk_queue(
     ExactCta<NW, MAXPEND>& sm, LogitFn lg, const float* __restrict__ wn, float gx, int t, int E,
     int K, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_router,
     int H, ExactStats stats, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-    int* cnt) {
+    CntFn cnt_of) {
   const int lane = threadIdx.x & 31;
   int e;
   float v;
@@ -755,7 +756,7 @@ __device__ __forceinline__ void warp_topk_queue(
   rbase = __shfl_sync(0xffffffffu, rbase, 0);
   if (slot < 0) {
     warp_select_intervals(lg, wn, gx, E, K, x + size_t(t) * H, w_router, H, stats, e, v);
-    warp_write_route(t, K, e, v, topk_idx, topk_w, cnt);
+    warp_write_route(t, K, e, v, topk_idx, topk_w, cnt_of(t));
     return;
   }
   auto& P = sm.pend[slot];
@@ -791,33 +792,33 @@ __device__ __forceinline__ void warp_topk_queue(
 
 // Step A (one warp, token t): settle it, or queue it.  `sm.n_pend` and
 // `sm.n_req` must be zero (and visible) before the CTA's first call.
-template <int NW, int MAXPEND, typename LogitFn>
+template <int NW, int MAXPEND, typename LogitFn, typename CntFn>
 __device__ __forceinline__ void warp_topk_stage(
     ExactCta<NW, MAXPEND>& sm, LogitFn lg, const float* __restrict__ wn, float nx, float gamma,
     int t, int E, int K, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w_router, int H, ExactStats stats,
-    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int* cnt) {
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, CntFn cnt_of) {
   const float gx = gamma * kBoundSlack * nx;
   int e;
   float v;
   if (warp_fast_check(lg, wn, gx, E, K, e, v)) {
-    warp_write_route(t, K, e, v, topk_idx, topk_w, cnt);
+    warp_write_route(t, K, e, v, topk_idx, topk_w, cnt_of(t));
     return;
   }
-  warp_topk_queue(sm, lg, wn, gx, t, E, K, x, w_router, H, stats, topk_idx, topk_w, cnt);
+  warp_topk_queue(sm, lg, wn, gx, t, E, K, x, w_router, H, stats, topk_idx, topk_w, cnt_of);
 }
 
 // Step A for two tokens of one warp, their fast checks interleaved
 // (valid1 false: only t0).
-template <int NW, int MAXPEND, typename LogitFn2>
+template <int NW, int MAXPEND, typename LogitFn2, typename CntFn>
 __device__ __forceinline__ void warp_topk_stage2(
     ExactCta<NW, MAXPEND>& sm, LogitFn2 lg, const float* __restrict__ wn, float nx0, float nx1,
     float gamma, int t0, int t1, bool valid1, int E, int K, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w_router, int H, ExactStats stats,
-    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int* cnt) {
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, CntFn cnt_of) {
   if (!valid1) {
     warp_topk_stage(sm, [&](int ee) { return lg(0, ee); }, wn, nx0, gamma, t0, E, K, x, w_router,
-                    H, stats, topk_idx, topk_w, cnt);
+                    H, stats, topk_idx, topk_w, cnt_of);
     return;
   }
   const float gx[2] = {gamma * kBoundSlack * nx0, gamma * kBoundSlack * nx1};
@@ -829,21 +830,21 @@ __device__ __forceinline__ void warp_topk_stage2(
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     if (ok[i])
-      warp_write_route(ts[i], K, e[i], v[i], topk_idx, topk_w, cnt);
+      warp_write_route(ts[i], K, e[i], v[i], topk_idx, topk_w, cnt_of(ts[i]));
     else
       warp_topk_queue(sm, [&](int ee) { return lg(i, ee); }, wn, gx[i], ts[i], E, K, x, w_router,
-                      H, stats, topk_idx, topk_w, cnt);
+                      H, stats, topk_idx, topk_w, cnt_of);
   }
 }
 
 // Steps B and C, by every thread of the CTA (contains __syncthreads).
-template <int NW, int MAXPEND>
+template <int NW, int MAXPEND, typename CntFn>
 __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
                                                 const __nv_bfloat16* __restrict__ x,
                                                 const __nv_bfloat16* __restrict__ w_router,
                                                 int H, int K, ExactStats stats,
                                                 int32_t* __restrict__ topk_idx,
-                                                float* __restrict__ topk_w, int* cnt) {
+                                                float* __restrict__ topk_w, CntFn cnt_of) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __syncthreads();
   const int nreq = min(sm.n_req, kXMaxReq);
@@ -852,34 +853,53 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
   const int lg = 32 - __clz(H + 63);
   const int room = 127 - 16 - 2 - lg;
   if (nreq > 0) {
-    // B1: exponent ranges of the queued rows
-    for (int r = 0; r < nreq; ++r) {
-      auto& q = sm.req[r];
-      if (q.slot < 0) continue;
-      const uint2* xr = reinterpret_cast<const uint2*>(x + size_t(q.t) * H + warp * chunk);
-      const uint2* wr = reinterpret_cast<const uint2*>(w_router + size_t(q.e) * H + warp * chunk);
-      uint32_t xmx = 0u, xmn = 0x7FFF7FFFu, wmx = 0u, wmn = 0x7FFF7FFFu;
-      for (int u = lane; u < chunk / 4; u += 32) {
-        const uint2 xv = __ldg(xr + u), wv = __ldg(wr + u);
-        const uint32_t xs[2] = {xv.x, xv.y}, ws[2] = {wv.x, wv.y};
+    // B1: exponent ranges of the queued rows (the loads of every request of
+    // this warp's pass are issued before any is used: up to 4 at a time)
+    for (int r0 = 0; r0 < nreq; r0 += 4) {
+      uint2 xv[4], wv[4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const uint32_t ax = xs[j] & 0x7FFF7FFFu, aw = ws[j] & 0x7FFF7FFFu;
-          xmx = __vmaxu2(xmx, ax);
-          wmx = __vmaxu2(wmx, aw);
-          xmn = __vminu2(xmn, ax | (__vcmpeq2(ax, 0u) & 0x7FFF7FFFu));
-          wmn = __vminu2(wmn, aw | (__vcmpeq2(aw, 0u) & 0x7FFF7FFFu));
+      for (int j = 0; j < 4; ++j) {
+        const int r = r0 + j;
+        const bool live = r < nreq && sm.req[r].slot >= 0 && lane < chunk / 4;
+        xv[j] = wv[j] = make_uint2(0u, 0u);
+        if (live) {
+          const auto& q = sm.req[r];
+          xv[j] = __ldg(reinterpret_cast<const uint2*>(x + size_t(q.t) * H + warp * chunk) + lane);
+          wv[j] = __ldg(reinterpret_cast<const uint2*>(w_router + size_t(q.e) * H + warp * chunk) +
+                        lane);
         }
       }
-      const uint32_t a = __reduce_max_sync(0xffffffffu, max(xmx & 0xFFFFu, xmx >> 16));
-      const uint32_t b = __reduce_max_sync(0xffffffffu, max(wmx & 0xFFFFu, wmx >> 16));
-      const uint32_t c = __reduce_min_sync(0xffffffffu, min(xmn & 0xFFFFu, xmn >> 16));
-      const uint32_t d = __reduce_min_sync(0xffffffffu, min(wmn & 0xFFFFu, wmn >> 16));
-      if (lane == 0) {
-        atomicMax(&q.xmax, a);
-        atomicMax(&q.wmax, b);
-        atomicMin(&q.xmin, c);
-        atomicMin(&q.wmin, d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = r0 + j;
+        if (r >= nreq || sm.req[r].slot < 0) continue;
+        auto& q = sm.req[r];
+        uint32_t xmx = 0u, xmn = 0x7FFF7FFFu, wmx = 0u, wmn = 0x7FFF7FFFu;
+        for (int u = lane; u < chunk / 4; u += 32) {
+          const uint2 xa = u == lane ? xv[j] : __ldg(reinterpret_cast<const uint2*>(
+                                                   x + size_t(q.t) * H + warp * chunk) + u);
+          const uint2 wa = u == lane ? wv[j] : __ldg(reinterpret_cast<const uint2*>(
+                                                   w_router + size_t(q.e) * H + warp * chunk) + u);
+          const uint32_t xs[2] = {xa.x, xa.y}, ws[2] = {wa.x, wa.y};
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const uint32_t ax = xs[k] & 0x7FFF7FFFu, aw = ws[k] & 0x7FFF7FFFu;
+            xmx = __vmaxu2(xmx, ax);
+            wmx = __vmaxu2(wmx, aw);
+            xmn = __vminu2(xmn, ax | (__vcmpeq2(ax, 0u) & 0x7FFF7FFFu));
+            wmn = __vminu2(wmn, aw | (__vcmpeq2(aw, 0u) & 0x7FFF7FFFu));
+          }
+        }
+        const uint32_t a = __reduce_max_sync(0xffffffffu, max(xmx & 0xFFFFu, xmx >> 16));
+        const uint32_t b = __reduce_max_sync(0xffffffffu, max(wmx & 0xFFFFu, wmx >> 16));
+        const uint32_t c = __reduce_min_sync(0xffffffffu, min(xmn & 0xFFFFu, xmn >> 16));
+        const uint32_t d = __reduce_min_sync(0xffffffffu, min(wmn & 0xFFFFu, wmn >> 16));
+        if (lane == 0) {
+          atomicMax(&q.xmax, a);
+          atomicMax(&q.wmax, b);
+          atomicMin(&q.xmin, c);
+          atomicMin(&q.wmin, d);
+        }
       }
     }
     __syncthreads();
@@ -982,7 +1002,7 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
       }
       if (key == wmax) key = 0u;
     }
-    warp_write_route(P.t, K, e, v, topk_idx, topk_w, cnt);
+    warp_write_route(P.t, K, e, v, topk_idx, topk_w, cnt_of(P.t));
   }
 }
 

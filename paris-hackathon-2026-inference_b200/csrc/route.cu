@@ -419,13 +419,13 @@ __global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
     const float* r1 = s_lg + size_t(v1 ? tl1 : tl0) * Rpad;
     warp_topk_stage2(xq, [&](int i, int e) { return (i ? r1 : r0)[e]; }, s_wn, s_xn[tl0],
                      s_xn[v1 ? tl1 : tl0], gamma, t0 + tl0, t0 + tl1, v1, E, K, x, w_router, H,
-                     stats, topk_idx, topk_w, s_cnt);
+                     stats, topk_idx, topk_w, [&](int) { return s_cnt; });
     if (lane == 0) {
       shared_gate[t0 + tl0] = 1.0f / (1.0f + expf(-r0[E]));
       if (v1) shared_gate[t0 + tl1] = 1.0f / (1.0f + expf(-r1[E]));
     }
   }
-  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, s_cnt);
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, [&](int) { return s_cnt; });
   __threadfence();
   __syncthreads();
   // Level 2: the last group to finish builds the dispatch for all tokens.
@@ -501,10 +501,11 @@ __global__ void __launch_bounds__(256, 2) topk_kernel(
     const float gamma = accumulation_gamma(H / 16, 1);
     const float* row = logits + size_t(t) * Rpad;
     warp_topk_stage(xq, [&](int e) { return row[e]; }, wn, nx, gamma, t, E, K, x, w_router, H,
-                    stats, topk_idx, topk_w, counts);
+                    stats, topk_idx, topk_w, [&](int) { return counts; });
     if ((threadIdx.x & 31) == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
   }
-  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, counts);
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w,
+                  [&](int) { return counts; });
 }
 
 constexpr int kDispatchThreads = 1024;

@@ -257,15 +257,16 @@ __global__ void __launch_bounds__(kRtTopkThreads, 2) route_topk_tc_kernel(
   __syncthreads();
   const int warp = threadIdx.x >> 5;
   const int t0 = blockIdx.x * kRtTopkTokens;
+  auto cnt_of = [&](int) { return s_hist; };
   for (int i = warp; i < kRtTopkTokens; i += kRtTopkThreads / 32) {
     const int t = t0 + i;
     if (t >= T) break;
     const float* row = logits + size_t(t) * Rpad;
     warp_topk_stage(xq, [&](int e) { return row[e]; }, s_wn, xnorm[t], gamma, t, E, K, x,
-                    w_router, H, stats, topk_idx, topk_w, s_hist);
+                    w_router, H, stats, topk_idx, topk_w, cnt_of);
     if ((threadIdx.x & 31) == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
   }
-  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, s_hist);
+  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, cnt_of);
   __syncthreads();
   int32_t* h = hist + size_t(t0 / kRtM) * E;
   for (int e = threadIdx.x; e < E; e += blockDim.x)
