@@ -24,6 +24,7 @@
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
 #include "pmoe_tma.cuh"
+#include "pmoe_tc.cuh"
 
 namespace pmoe {
 
@@ -46,6 +47,11 @@ constexpr int kActChunkBytes = kActRows * kKC * 2;  // 4 KiB activation chunk
 constexpr int kRingBudget = 200 * 1024;
 constexpr int kUnitSlots = 4;
 constexpr int kDnRowBlocks = 8;  // down unit = 8 x 64 output rows (4: 99.9 us, 8: 98.4, 16: 117.8)
+// down: eight consumer warps, two per 16-row slice, each on half of a
+// stage's k-chunks (shorter dependent MMA chains), partial sums added
+// through shared memory
+constexpr int kDnConsumers = 8;
+constexpr int kDnThreads = 32 * (kDnConsumers + 1);
 
 template <int KCH>
 struct GuCfg {
@@ -80,10 +86,10 @@ struct UnitRing {
   int unit[kUnitSlots];
   int4 info[kUnitSlots];  // optional per-unit facts the producer already loaded
 
-  __device__ void init() {
+  __device__ void init(int consumers = kConsumers) {
     for (int i = 0; i < kUnitSlots; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumers);
+      mbar_init(&empty[i], consumers);
     }
   }
   // Next unit from the global queue, heaviest (last) first; -1 = done.
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
 // read as zero).  rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
 // ---------------------------------------------------------------------------
 template <int KCH>
-__global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
+__global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
     const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
     const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ CUtensorMap tm_h8,
     ExpertTables tb, int H, int E, int I, int Is,
@@ -300,13 +306,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
   uint64_t* empty = full + kStages;
   __shared__ UnitRing ur;
+  __shared__ float s_part[2][4][32][16];  // partial accumulators of the upper-k warps, by parity
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumers);
+      mbar_init(&empty[s], kDnConsumers);
     }
-    ur.init();
+    ur.init(kDnConsumers);
     mbar_fence_init();
   }
   __syncthreads();
@@ -376,10 +383,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     return;
   }
 
-  const int cw = warp - 1, g = lane >> 2, c = lane & 3;
-  const int r0 = cw * 16 + g, r1 = r0 + 8;
+  // consumer warp cw: rows slice rq (16 rows), k half kh of every stage
+  const int cw = warp - 1, rq = cw & 3, kh = cw >> 2, g = lane >> 2, c = lane & 3;
+  const int r0 = rq * 16 + g, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
-  uint32_t it = 0;
+  uint32_t it = 0, blk = 0;
   for (uint32_t ui = 0;; ++ui) {
     int u;
     int4 inf;
@@ -402,11 +410,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int i = nb + q * 8 + 2 * c + hh;
-        const bool ok = q < ng && i < n;
+        const bool ok = kh == 0 && q < ng && i < n;
         wt[q][hh] = ok ? tb.pair_w[p0 + i] : 0.f;
         dsti[q][hh] = ok ? tb.pair_dst[p0 + i] : -1;
       }
-    for (int sub = 0; sub < row_blocks; ++sub) {
+    for (int sub = 0; sub < row_blocks; ++sub, ++blk) {
       const int rb = rbg * row_blocks + sub;
       float acc[4][4] = {};
       for (int kc = 0; kc < nkc; ++kc, ++it) {
@@ -418,6 +426,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
         const uint32_t st0 = sbase + s * C::kStageBytes;
 #pragma unroll
         for (int j = 0; j < KCH; ++j) {
+          if (KCH > 1 && (2 * j) / KCH != kh) continue;  // the other warp's half
+          if (KCH == 1 && kh != 0) continue;
           const uint32_t tw = st0 + j * kBoxBytes;
           const uint32_t th = st0 + KCH * kBoxBytes + j * kActChunkBytes;
 #pragma unroll
@@ -436,6 +446,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
+      // the upper-k warp hands its partial sums to its partner through
+      // shared memory (two parities: the partner reads slot p before it
+      // arrives at the next row block's barrier)
+      float* slot = &s_part[blk & 1][rq][lane][0];
+      if (kh == 1) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) slot[q * 4 + i] = acc[q][i];
+      }
+      named_bar_sync(1 + rq, 64);
+      if (kh == 1) continue;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[q][i] += slot[q * 4 + i];
       const int orow = rb * kUnitRows + r0;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -472,7 +498,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) down_tma_kernel(
     __syncwarp();
     if (lane == 0) {
       const int prev = atomicAdd(ep.ticket, 1);
-      if (prev == int(gridDim.x) * kConsumers - 1) {
+      if (prev == int(gridDim.x) * kDnConsumers - 1) {
         __threadfence_system();
         *ep.ticket = 0;
         for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, epoch);
@@ -656,7 +682,7 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
   gate_up_tma_kernel<KCH><<<g_num_sms, kStreamThreads, GuCfg<KCH>::kSmem, st>>>(      \
       tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
 #define PMOE_DN(KCH)                                                                  \
-  down_tma_kernel<KCH><<<g_num_sms, kStreamThreads, DnCfg<KCH>::kSmem, st>>>(         \
+  down_tma_kernel<KCH><<<g_num_sms, kDnThreads, DnCfg<KCH>::kSmem, st>>>(             \
       tm_dn, tm_sd, tm_h, tm_h8, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep, rbk)
   if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
   if (mid_event) {
