@@ -450,8 +450,8 @@ int pmoe_route_slice(const uint16_t* x, int T, int H, int E, int K, int I, int I
   if (cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st) != cudaSuccess ||
       launch_router_tc(ds, bf(x) + size_t(t0) * H, bf(w_router), bf(w_sh_gvec),
                        topk_idx + size_t(t0) * K, topk_w + size_t(t0) * K, shared_gate + t0,
-                       ws.hist, ws.status, ws.logit_part, ws.xnorm, ws.wnorm, nullptr,
-                       st) != cudaSuccess)
+                       ws.hist, ws.status, ws.logit_part, ws.xnorm, ws.wnorm, ws.route_queue,
+                       nullptr, st) != cudaSuccess)
     return PMOE_ERR_CUDA;
   return PMOE_OK;
 }

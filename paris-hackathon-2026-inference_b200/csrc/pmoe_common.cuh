@@ -33,8 +33,8 @@ struct Workspace {
   float* diag;          // not carved: when set, the routing copies its fp32 logits [T][Rpad] here
   int32_t* status;      // [kStatusWords] [0] route ticket, [1] error code (kStatus*), [2]/[3]
                         //            stream queues, [4..7] decode group tickets, [8] exact logit
-                        //            evaluations, [9] of which outside the exactness condition;
-                        //            cleared per call
+                        //            evaluations, [9] of which outside the exactness condition,
+                        //            [10] entries of route_queue; cleared per call
   __nv_bfloat16* h;     // [T*K+T][ldh] SiLU(gate)*up, dispatched order
   __nv_bfloat16* xn;    // [T][H]     RMSNorm(x) (decoder-layer entry points)
   float* rows;          // [T*K+T][H] weighted expert outputs, token-major (streaming path)
@@ -47,6 +47,7 @@ struct Workspace {
   int4* m_tiles;        // (expert, row0, nrows, 0): one per 128-row block of a computed expert
   int32_t* tile_counts; // [8] tiles: [0] gate_up [1] down [2] M blocks; [4]/[5] the dispatched
                         //     rows [lo, hi) this call computes (row-split expert parallelism)
+  int32_t* route_queue; // [T]       tokens the prefill top-k's fast check left open
   int32_t* hist;        // [ceil(T/128)][E] per-tile expert histogram (prefill routing)
   int32_t* hist_base;   // [ceil(T/128)][E] first output slot per (tile, expert)
   size_t bytes;
@@ -165,6 +166,7 @@ inline Workspace carve(void* base, const Dims& d) {
   w.dn_tiles = (int4*)take(sizeof(int4) * mt_max * size_t(d.H / 128 + 1));
   w.m_tiles = (int4*)take(sizeof(int4) * mt_max);
   w.tile_counts = (int32_t*)take(sizeof(int32_t) * 8);
+  w.route_queue = (int32_t*)take(sizeof(int32_t) * size_t(d.T));
   const size_t ntile = (size_t(d.T) + 127) / 128;
   w.hist = (int32_t*)take(sizeof(int32_t) * ntile * d.E);
   w.hist_base = (int32_t*)take(sizeof(int32_t) * ntile * d.E);

@@ -50,12 +50,14 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
                             int with_routed, const Workspace& ws, cudaStream_t st);
 // The router GEMM + exact top-k alone, for d.T tokens starting at x, into the
 // given arrays (hist: per-128-token-tile expert counts; status: the status
-// words, error at [1], exact-evaluation counts at [8]/[9]; logits [d.T][Rpad],
-// xnorm [d.T], wnorm [E]: scratch; diag: optional copy of the fp32 logits).
+// words (zeroed by the caller), error at [1], exact-evaluation counts at
+// [8]/[9], queue length at [10]; logits [d.T][Rpad], xnorm [d.T], wnorm [E],
+// queue [d.T]: scratch; diag: optional copy of the fp32 logits).
 cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                              const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
                              float* shared_gate, int32_t* hist, int* status, float* logits,
-                             float* xnorm, float* wnorm, float* diag, cudaStream_t st);
+                             float* xnorm, float* wnorm, int32_t* queue, float* diag,
+                             cudaStream_t st);
 // Exactly rounded logits of all T x E pairs (one warp each); n_inexact (a
 // device counter) counts pairs outside the exactness condition.
 cudaError_t launch_exact_logits(const __nv_bfloat16* x, const __nv_bfloat16* w, int T, int H,

@@ -231,46 +231,73 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
   }
 }
 
-// Exact top-k over the router GEMM's logits: a token per warp at a time, a
-// CTA per kRtTopkTokens tokens; each CTA adds its experts' counts into the
-// histogram of its 128-token tile (zeroed by the launcher).
-constexpr int kRtTopkThreads = 256;
-constexpr int kRtTopkTokens = 8;
-static_assert(kRtM % kRtTopkTokens == 0, "a CTA's tokens lie in one tile");
-__global__ void __launch_bounds__(kRtTopkThreads, 2) route_topk_tc_kernel(
+// Exact top-k over the router GEMM's logits (pmoe_exact.cuh), in two kernels
+// so that the common case runs at high occupancy:
+//   route_fast_kernel   one token per warp: the fast check; a settled token
+//                       gets its routing and is counted in its 128-token
+//                       tile's histogram (zeroed by the launcher), an open one
+//                       is appended to a queue;
+//   route_fixup_kernel  the queued tokens, kRtFixTokens per CTA round: the
+//                       interval selection with the exact evaluations shared
+//                       by the CTA's warps.
+constexpr int kRtFastThreads = 256;
+constexpr int kRtFixThreads = 256;
+constexpr int kRtFixTokens = 8;
+
+__global__ void __launch_bounds__(kRtFastThreads) route_fast_kernel(
+    const float* __restrict__ logits, const float* __restrict__ xnorm,
+    const float* __restrict__ wnorm, int T, int E, int K, int Rpad, float gamma,
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
+    int32_t* __restrict__ hist, int32_t* __restrict__ queue, int* __restrict__ queue_count) {
+  __shared__ float s_wn[kRtN];
+  for (int e = threadIdx.x; e < kRtN; e += blockDim.x) s_wn[e] = e < E ? wnorm[e] : 0.f;
+  __syncthreads();
+  const int t = blockIdx.x * (kRtFastThreads / 32) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int lane = threadIdx.x & 31;
+  const float* row = logits + size_t(t) * Rpad;
+  if (lane == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
+  int e;
+  float v;
+  if (warp_fast_check([&](int ee) { return row[ee]; }, s_wn, gamma * kBoundSlack * xnorm[t], E,
+                      K, e, v))
+    warp_write_route(t, K, e, v, topk_idx, topk_w, hist + size_t(t / kRtM) * E);
+  else if (lane == 0)
+    queue[atomicAdd(queue_count, 1)] = t;
+}
+
+__global__ void __launch_bounds__(kRtFixThreads, 2) route_fixup_kernel(
     const float* __restrict__ logits, const float* __restrict__ xnorm,
     const float* __restrict__ wnorm, const __nv_bfloat16* __restrict__ x,
-    const __nv_bfloat16* __restrict__ w_router, int T, int H, int E, int K, int Rpad,
-    float gamma, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-    float* __restrict__ shared_gate, int32_t* __restrict__ hist, ExactStats stats) {
-  __shared__ int s_hist[kRtN];
+    const __nv_bfloat16* __restrict__ w_router, int H, int E, int K, int Rpad, float gamma,
+    const int32_t* __restrict__ queue, const int* __restrict__ queue_count,
+    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int32_t* __restrict__ hist,
+    ExactStats stats) {
+  constexpr int kWarps = kRtFixThreads / 32;
   __shared__ float s_wn[kRtN];
-  __shared__ ExactCta<kRtTopkThreads / 32, kRtTopkTokens> xq;
-  for (int e = threadIdx.x; e < kRtN; e += blockDim.x) {
-    s_hist[e] = 0;
-    s_wn[e] = e < E ? wnorm[e] : 0.f;
-  }
-  if (threadIdx.x == 0) {
-    xq.n_pend = 0;
-    xq.n_req = 0;
-  }
+  __shared__ ExactCta<kWarps, kRtFixTokens> xq;
+  __shared__ int s_n;
+  for (int e = threadIdx.x; e < kRtN; e += blockDim.x) s_wn[e] = e < E ? wnorm[e] : 0.f;
+  if (threadIdx.x == 0) s_n = *queue_count;
   __syncthreads();
-  const int warp = threadIdx.x >> 5;
-  const int t0 = blockIdx.x * kRtTopkTokens;
-  auto cnt_of = [&](int) { return s_hist; };
-  for (int i = warp; i < kRtTopkTokens; i += kRtTopkThreads / 32) {
-    const int t = t0 + i;
-    if (t >= T) break;
-    const float* row = logits + size_t(t) * Rpad;
-    warp_topk_stage(xq, [&](int e) { return row[e]; }, s_wn, xnorm[t], gamma, t, E, K, x,
-                    w_router, H, stats, topk_idx, topk_w, cnt_of);
-    if ((threadIdx.x & 31) == 0) shared_gate[t] = 1.0f / (1.0f + expf(-row[E]));
+  const int n = s_n, warp = threadIdx.x >> 5;
+  auto cnt_of = [&](int t) { return hist + size_t(t / kRtM) * E; };
+  for (int base = blockIdx.x * kRtFixTokens; base < n; base += gridDim.x * kRtFixTokens) {
+    if (threadIdx.x == 0) {
+      xq.n_pend = 0;
+      xq.n_req = 0;
+    }
+    __syncthreads();
+    for (int i = warp; i < kRtFixTokens; i += kWarps) {
+      if (base + i >= n) break;
+      const int t = queue[base + i];
+      const float* row = logits + size_t(t) * Rpad;
+      warp_topk_queue(xq, [&](int ee) { return row[ee]; }, s_wn, gamma * kBoundSlack * xnorm[t],
+                      t, E, K, x, w_router, H, stats, topk_idx, topk_w, cnt_of);
+    }
+    cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, cnt_of);
+    __syncthreads();
   }
-  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, cnt_of);
-  __syncthreads();
-  int32_t* h = hist + size_t(t0 / kRtM) * E;
-  for (int e = threadIdx.x; e < E; e += blockDim.x)
-    if (s_hist[e]) atomicAdd(&h[e], s_hist[e]);
 }
 
 // ---------------------------------------------------------------------------
@@ -425,7 +452,8 @@ __global__ void __launch_bounds__(256) route_hist_kernel(const int32_t* __restri
 cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                              const __nv_bfloat16* w_gvec, int32_t* topk_idx, float* topk_w,
                              float* shared_gate, int32_t* hist, int* status, float* logits,
-                             float* xnorm, float* wnorm, float* diag, cudaStream_t st) {
+                             float* xnorm, float* wnorm, int32_t* queue, float* diag,
+                             cudaStream_t st) {
   CUtensorMap tm_x, tm_w, tm_g;
   const uint64_t H = d.H;
   if (!make_tmap_bf16_2d(&tm_x, x, H, d.T, H * 2, kRtK, kRtM) ||
@@ -457,9 +485,16 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
   const float gamma = router_tc_gamma(d.H);
   err = cudaMemsetAsync(hist, 0, sizeof(int32_t) * size_t(nb) * d.E, st);
   if (err != cudaSuccess) return err;
-  route_topk_tc_kernel<<<(d.T + kRtTopkTokens - 1) / kRtTopkTokens, kRtTopkThreads, 0, st>>>(
-      logits, xnorm, wnorm, x, w_router, d.T, d.H, d.E, d.K, d.Rpad, gamma, topk_idx, topk_w,
-      shared_gate, hist, ExactStats{status + 8, status + 9});
+  int* queue_count = status + 10;  // zeroed with the status words
+  route_fast_kernel<<<(d.T + kRtFastThreads / 32 - 1) / (kRtFastThreads / 32), kRtFastThreads, 0,
+                      st>>>(logits, xnorm, wnorm, d.T, d.E, d.K, d.Rpad, gamma, topk_idx, topk_w,
+                            shared_gate, hist, queue, queue_count);
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  route_fixup_kernel<<<2 * sms, kRtFixThreads, 0, st>>>(
+      logits, xnorm, wnorm, x, w_router, d.H, d.E, d.K, d.Rpad, gamma, queue, queue_count,
+      topk_idx, topk_w, hist, ExactStats{status + 8, status + 9});
   return cudaGetLastError();
 }
 
@@ -484,7 +519,8 @@ cudaError_t launch_route_tc(const Dims& d, const __nv_bfloat16* x, const __nv_bf
   cudaError_t err = cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st);
   if (err != cudaSuccess) return err;
   err = launch_router_tc(d, x, w_router, w_gvec, ws.topk_idx, ws.topk_w, ws.shared_gate, ws.hist,
-                         ws.status, ws.logit_part, ws.xnorm, ws.wnorm, ws.diag, st);
+                         ws.status, ws.logit_part, ws.xnorm, ws.wnorm, ws.route_queue, ws.diag,
+                         st);
   if (err != cudaSuccess) return err;
   return launch_dispatch(d, lo, hi, with_shared, with_routed, ws, st);
 }
