@@ -38,7 +38,8 @@ enum {
   PMOE_ERR_UNSUPPORTED = -5,/* shape outside what the kernels implement */
   PMOE_ERR_PEER_TIMEOUT = -6,/* a bounded wait on a peer GPU ran out */
   PMOE_ERR_DEVICE = -7,     /* not an sm_100 device */
-  PMOE_ERR_NOALLOC_TOO_LARGE = -8 /* shape needs more scratch than the no-alloc entry has */
+  PMOE_ERR_NOALLOC_TOO_LARGE = -8, /* shape needs more scratch than the no-alloc entry has */
+  PMOE_ERR_COMM_CAPACITY = -9 /* batch larger than the communicator's exchange buffers */
 };
 
 /* Flags of pmoe_block_forward. */
@@ -266,6 +267,43 @@ int pmoe_block_forward_rows_fused(
     const uint16_t* w_sh_up, const uint16_t* w_sh_down, const uint16_t* w_sh_gvec, int rank,
     int world, void* const* bufs, int T_max, int epoch, int flags, uint16_t* y,
     void* workspace, size_t workspace_bytes, void* stream, void* const* events, int n_events);
+
+/* ---- communicator: the comm_handle of the paris_moe::moe_block operator -----
+ * An opaque handle holding one rank's view of the two NVLink exchanges above
+ * (peer pointers of the pmoe_block_forward_ep buffers and of the
+ * pmoe_block_forward_rows_fused buffers) plus the host epoch of the row
+ * exchange.  It owns no device memory: the caller allocates, IPC-maps and
+ * frees the buffers and registers them here (again after growing them; the
+ * row epoch restarts, the new buffers being zeroed).  Not thread-safe across
+ * ranks' host threads beyond its internal lock.  Replaces the process-group
+ * handle that engine/runtime/ep.py:97-143 hands to all_reduce (:140). */
+int pmoe_comm_create(int rank, int world, void** comm);
+int pmoe_comm_destroy(void* comm);
+/* bufs NULL: unregister.  t_max: the batch size the buffers were sized for. */
+int pmoe_comm_set_ep(void* comm, void* const* bufs, size_t buf_bytes, int t_max);
+int pmoe_comm_set_rows(void* comm, void* const* bufs, int t_max);
+/* Take the next row-exchange epoch (for pmoe_rows_partial / pmoe_rows_allreduce
+ * calls that share the row buffers with pmoe_block_forward_comm). */
+int pmoe_comm_next_rows_epoch(void* comm, int* epoch);
+/* rank, world, and the largest T each registered exchange takes (0: none). */
+int pmoe_comm_info(void* comm, int* rank, int* world, int* ep_tmax, int* rows_tmax);
+/* The full block output on every rank of the communicator (all ranks call with
+ * the same x, T and weights, in the same order).  Rank r computes the experts
+ * [r*E/world, (r+1)*E/world) (engine/runtime/ep.py:78-86) and the shared expert
+ * of tokens [r*T/world, (r+1)*T/world).  T <= the decode exchange's t_max:
+ * pmoe_block_forward_ep with the device-side epoch (CUDA-graph capturable);
+ * else, with PMOE_F_SHARED|PMOE_F_ROUTED and T <= the row exchange's t_max:
+ * pmoe_block_forward_rows_fused with the next host epoch (not capturable:
+ * the epoch is baked into the launch); else PMOE_ERR_COMM_CAPACITY.
+ * comm NULL or world 1: pmoe_block_forward over all experts.  events /
+ * n_events: as pmoe_block_forward_rows_fused (may be NULL / 0). */
+int pmoe_block_forward_comm(void* comm, const uint16_t* x, int T, int H, int E, int K, int I,
+                            int Is, const uint16_t* w_router, const uint16_t* w_gate_up,
+                            const uint16_t* w_down, const uint16_t* w_sh_gate,
+                            const uint16_t* w_sh_up, const uint16_t* w_sh_down,
+                            const uint16_t* w_sh_gvec, int flags, uint16_t* y, void* workspace,
+                            size_t workspace_bytes, void* stream, void* const* events,
+                            int n_events);
 
 /* One decoder layer of the MoE-only stack: y = x + block(RMSNorm(x)), with
  * RMSNorm(x) = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w_norm)) in fp32 and the

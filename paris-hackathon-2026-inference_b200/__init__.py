@@ -6,7 +6,9 @@ hyphens): ``load_package()`` in ``bench.py`` / ``tests/conftest.py`` /
 
 Public surface (mirrors the reference's engine/kernels API):
   fused_moe_forward, patch_qwen3_5_moe, unpatch_qwen3_5_moe   (moe.py)
-  torch.ops.paris_moe.moe_block / moe_route                    (ops.py)
+  torch.ops.paris_moe.moe_block / moe_route / moe_layer / rmsnorm
+      (C++ csrc/torch_ops.cpp -> libparis_moe_torch.so, loaded by ops.py)
+  EPGroup (NVLink expert parallelism; comm_handle of moe_block)  (ep.py)
   workload generators                                          (workload.py)
 """
 from __future__ import annotations

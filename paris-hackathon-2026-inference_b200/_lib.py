@@ -60,6 +60,15 @@ SIGNATURES = {
                                               _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P,
                                               _SZ, _P, ctypes.POINTER(_P), _I]),
     "pmoe_read_status": (_I, [_P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "pmoe_comm_create": (_I, [_I, _I, ctypes.POINTER(_P)]),
+    "pmoe_comm_destroy": (_I, [_P]),
+    "pmoe_comm_set_ep": (_I, [_P, ctypes.POINTER(_P), _SZ, _I]),
+    "pmoe_comm_set_rows": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "pmoe_comm_next_rows_epoch": (_I, [_P, ctypes.POINTER(_I)]),
+    "pmoe_comm_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I),
+                            ctypes.POINTER(_I)]),
+    "pmoe_block_forward_comm": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P,
+                                     _I, _P, _P, _SZ, _P, ctypes.POINTER(_P), _I]),
     "pmoe_ipc_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
     "pmoe_ipc_free": (_I, [_P]),
     "pmoe_ipc_handle": (_I, [_P, ctypes.c_char_p]),
@@ -68,6 +77,7 @@ SIGNATURES = {
 }
 
 PMOE_ERR_PEER_TIMEOUT = -6
+PMOE_ERR_COMM_CAPACITY = -9
 
 PMOE_F_SHARED = 1
 PMOE_F_ROUTED = 2

@@ -2,8 +2,10 @@
 
     python paris-hackathon-2026-inference_b200/build.py [--verbose-ptxas]
 
-The library has no torch dependency: it exports the C ABI of
-include/paris_moe.h and is loaded with ctypes.
+libparis_moe.so has no torch dependency: it exports the C ABI of
+include/paris_moe.h and is loaded with ctypes.  libparis_moe_torch.so
+(csrc/torch_ops.cpp, g++ against the installed torch's headers) registers the
+torch.ops.paris_moe operators over that ABI.
 """
 from __future__ import annotations
 
@@ -18,6 +20,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libparis_moe.so")
+OPS_LIB = os.path.join(PKG, "libparis_moe_torch.so")
+OPS_SRC = os.path.join(CSRC, "torch_ops.cpp")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -45,6 +49,35 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> str:
+    build_lib(force, verbose_ptxas)
+    build_ops(force)
+    return LIB
+
+
+def build_ops(force: bool = False) -> str:
+    """The torch operator library, linked against libparis_moe.so and torch."""
+    if (not force and os.path.exists(OPS_LIB) and
+            os.path.getmtime(OPS_LIB) > max(os.path.getmtime(f) for f in
+                                            [OPS_SRC, LIB, *headers()])):
+        return OPS_LIB
+    import torch
+    from torch.utils import cpp_extension
+    cuda_home = os.path.dirname(os.path.dirname(nvcc_path()))
+    inc = cpp_extension.include_paths() + [os.path.join(cuda_home, "include"),
+                                           os.path.join(ROOT, "include")]
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = OPS_LIB + ".tmp"
+    cmd = (["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}"] +
+           [f"-I{d}" for d in inc] + [OPS_SRC, "-o", tmp, f"-L{PKG}", "-lparis_moe",
+                                      f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch_cpu",
+                                      "-ltorch", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"])
+    subprocess.check_call(cmd)
+    os.replace(tmp, OPS_LIB)
+    return OPS_LIB
+
+
+def build_lib(force: bool = False, verbose_ptxas: bool = False) -> str:
     if not force and not needs_build():
         return LIB
     nvcc = nvcc_path()

@@ -65,6 +65,8 @@ const char* pmoe_status_string(int s) {
     case PMOE_ERR_DEVICE: return "device is not sm_100 (B200)";
     case PMOE_ERR_NOALLOC_TOO_LARGE:
       return "shape needs more scratch than pmoe_block_forward_noalloc's fixed array";
+    case PMOE_ERR_COMM_CAPACITY:
+      return "batch larger than the communicator's exchange buffers (grow them first)";
     default: return "unknown status";
   }
 }

@@ -22,7 +22,11 @@ are summed.  Two ways to sum:
   full output and no collective kernel runs;
   Prefill-sized batches use the row split: the down GEMM stores each row at
   the rank owning its token over NVLink, that rank combines its token slice
-  and pushes it to every rank (``pmoe_block_forward_rows_fused``);
+  and pushes it to every rank (``pmoe_block_forward_rows_fused``).  Both
+  exchanges are registered with a native communicator (``pmoe_comm_create``),
+  which picks the path by T and keeps the row exchange's epoch; its handle is
+  the ``comm_handle`` of ``torch.ops.paris_moe.moe_block``, the call the
+  patched HF module makes (``EPGroup.op_forward``);
 * ``nccl`` (the comparator): each rank returns its partial (its experts plus
   its share of the shared expert's tokens) and ``torch.distributed.all_reduce``
   sums them, as ep.py:140 does; ``a2a``: token dispatch with all_to_all_single.
@@ -136,6 +140,8 @@ class EPGroup:
             self.peer_ptrs = ptrs
             self.peer_arr = (ctypes.c_void_p * self.world)(*ptrs)
             self.t_max = t_max
+            _lib.check("pmoe_comm_set_ep", self.lib.pmoe_comm_set_ep(
+                self.comm, self.peer_arr, self.buf_bytes, min(t_max, FUSED_MAX_T)))
             torch.cuda.synchronize()
             dist.barrier(group)
 
@@ -152,7 +158,12 @@ class EPGroup:
         self.owns_buffers = True
         self.rx_local = None    # row-split exchange buffers (prefill), allocated on first use
         self.rx_tmax = 0
-        self.rx_epoch = 0
+        # the native communicator (pmoe_comm_create): the exchange buffers'
+        # peer pointers and the row exchange's epoch; the comm_handle of
+        # torch.ops.paris_moe.moe_block
+        c = ctypes.c_void_p()
+        _lib.check("pmoe_comm_create", self.lib.pmoe_comm_create(rank, world, ctypes.byref(c)))
+        self.comm = c.value
         # prefill exchange: "rows" (the down GEMM stores rows at their token
         # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
         # outputs summed by pmoe_rows_allreduce)
@@ -182,11 +193,15 @@ class EPGroup:
             g.peer_ptrs = list(peer_bufs)
             g.local_buf = g.peer_ptrs[rank]
             g.peer_arr = (ctypes.c_void_p * world)(*g.peer_ptrs)
+            _lib.check("pmoe_comm_set_ep", g.lib.pmoe_comm_set_ep(
+                g.comm, g.peer_arr, g.buf_bytes, min(t_max, FUSED_MAX_T)))
         if rows_bufs is not None:
             g.rx_ptrs = list(rows_bufs)
             g.rx_local = g.rx_ptrs[rank]
             g.rx_tmax = rows_t_max
             g.rx_arr = (ctypes.c_void_p * world)(*g.rx_ptrs)
+            _lib.check("pmoe_comm_set_rows", g.lib.pmoe_comm_set_rows(g.comm, g.rx_arr,
+                                                                      rows_t_max))
         return g
 
     # ---- peer-loss detection ---------------------------------------------------
@@ -249,19 +264,18 @@ class EPGroup:
         st = torch.cuda.current_stream(x.device).cuda_stream
         wp = [t.data_ptr() for t in w]
         slo, shi = token_range(T, self.rank, self.world)
-        if self.uses_exchange(T):
-            # each rank computes its experts and its share of the shared
-            # expert's tokens; every computed row is exchanged.  Epoch 0: the
-            # device-side counter, so the call can be captured in a CUDA graph.
-            s = self.lib.pmoe_block_forward_ep(
-                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.lo, self.hi, slo, shi, flags,
-                self.peer_arr, self.buf_bytes, self.rank, self.world, 0, y.data_ptr(),
-                ws.data_ptr(), nbytes, st)
-            _lib.check("pmoe_block_forward_ep", s)
-            self._status_enqueue(st)
-            return y
         if self.mode == "fused" and self.world > 1:
-            y = self._forward_rows(x, wp, I, Is, flags, y, ws, nbytes, st, events)
+            if not self.uses_exchange(T):
+                if self.prefill == "partial" or (flags & 3) != 3:
+                    return self._forward_rows_partial(x, wp, I, Is, flags, y, ws, nbytes, st)
+                self._rows_buffers(T)
+            # the communicator picks the exchange: T <= t_max the decode one
+            # (device-side epoch, so the call can be captured in a CUDA graph),
+            # else the row-split one with its next host epoch
+            ev, nev = (events, 5) if events is not None else (None, 0)
+            _lib.check("pmoe_block_forward_comm", self.lib.pmoe_block_forward_comm(
+                self.comm, x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, flags, y.data_ptr(),
+                ws.data_ptr(), nbytes, st, ev, nev))
             self._status_enqueue(st)
             return y
         if self.mode == "a2a" and self.world > 1:
@@ -274,36 +288,56 @@ class EPGroup:
             dist.all_reduce(y, group=self.group)
         return y
 
-    def _forward_rows(self, x, wp, I, Is, flags, y, ws, nbytes, st, events=None):
-        """Prefill-sized batches: every rank routes all tokens (the same kernel,
-        identical results; routing a slice per rank and all-gathering it was
-        slower: the tensor-core router is latency-bound per 128-token CTA),
-        computes its row-balanced share of the dispatched rows.  prefill "rows":
-        the down GEMM stores each row at the rank owning its token, which
-        combines its token slice locally and all ranks gather the slices
-        (pmoe_block_forward_rows_fused; y bit-identical to one GPU).  prefill
-        "partial": each rank's partial output (pmoe_block_forward_rows) goes to
-        its exchange buffer and pmoe_rows_allreduce sums the partials
-        (deterministic, fp32) into y."""
+    def reserve(self, T: int) -> None:
+        """Make the exchanges take batches of T tokens (collective: every rank
+        calls it with the same T).  Needed before torch.ops.paris_moe.moe_block
+        is called with this group's comm_handle at a T above t_max, since the
+        operator cannot allocate the IPC-mapped row buffers itself."""
+        if self.mode == "fused" and self.world > 1 and not self.uses_exchange(T):
+            self._rows_buffers(T)
+
+    @property
+    def comm_handle(self) -> int:
+        """The pmoe_comm_create handle, for torch.ops.paris_moe.moe_block(...,
+        ep_rank=rank, ep_size=world, comm_handle=...)."""
+        return int(self.comm or 0)
+
+    def op_forward(self, x: torch.Tensor, weights, flags: int = 3) -> torch.Tensor:
+        """forward() through the registered operator, as the patched HF module
+        calls it: torch.ops.paris_moe.moe_block with this group's comm_handle
+        (mode "fused"; the other modes are comparators and use forward())."""
+        if self.mode != "fused" or self.world == 1:
+            return self.forward(x, weights, flags)
+        from . import ops
+        self._status_check(block=False)
+        self.reserve(x.shape[0])
+        y = ops.moe_block(x, *weights, self.K, 0, -1, flags, ep_rank=self.rank,
+                          ep_size=self.world, comm_handle=self.comm_handle)
+        self._status_enqueue(torch.cuda.current_stream(x.device).cuda_stream)
+        return y
+
+    def _forward_rows_partial(self, x, wp, I, Is, flags, y, ws, nbytes, st):
+        """Prefill "partial" (the comparator of the fused row exchange): every
+        rank routes all tokens (identically), computes its row-balanced share of
+        the dispatched rows into its partial output in its exchange buffer
+        (pmoe_block_forward_rows), and pmoe_rows_allreduce sums the partials
+        (deterministic, fp32) into y.  The epoch comes from the communicator,
+        which shares the row buffers with the fused path."""
         T, H = x.shape
         self._rows_buffers(T)
-        self.rx_epoch += 1
-        if self.prefill == "rows" and (flags & 3) == 3:
-            ev, nev = (events, 5) if events is not None else (None, 0)
-            _lib.check("pmoe_block_forward_rows_fused", self.lib.pmoe_block_forward_rows_fused(
-                x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, self.rank, self.world,
-                self.rx_arr, self.rx_tmax, self.rx_epoch, flags, y.data_ptr(), ws.data_ptr(),
-                nbytes, st, ev, nev))
-            return y
+        ep = ctypes.c_int(0)
+        _lib.check("pmoe_comm_next_rows_epoch",
+                   self.lib.pmoe_comm_next_rows_epoch(self.comm, ctypes.byref(ep)))
         part = ctypes.c_void_p()
         _lib.check("pmoe_rows_partial", self.lib.pmoe_rows_partial(
-            self.rx_local, self.rx_tmax, H, self.rx_epoch, ctypes.byref(part)))
+            self.rx_local, self.rx_tmax, H, ep.value, ctypes.byref(part)))
         _lib.check("pmoe_block_forward_rows", self.lib.pmoe_block_forward_rows(
             x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, None, None, None, 0, self.E,
             self.rank, self.world, flags, part.value, ws.data_ptr(), nbytes, st))
         _lib.check("pmoe_rows_allreduce", self.lib.pmoe_rows_allreduce(
-            self.rx_arr, self.rx_tmax, T, H, self.rank, self.world, self.rx_epoch, y.data_ptr(),
+            self.rx_arr, self.rx_tmax, T, H, self.rank, self.world, ep.value, y.data_ptr(),
             st))
+        self._status_enqueue(st)
         return y
 
     def _forward_a2a(self, x, w, I, Is, y):
@@ -368,7 +402,7 @@ class EPGroup:
                    self.lib.pmoe_rows_fused_buffer_bytes(T, self.H, self.K, ctypes.byref(nb)))
         ptr = ctypes.c_void_p()
         _lib.check("pmoe_ipc_alloc", self.lib.pmoe_ipc_alloc(nb.value, ctypes.byref(ptr)))
-        self.rx_local, self.rx_tmax, self.rx_epoch = ptr.value, T, 0
+        self.rx_local, self.rx_tmax = ptr.value, T
         h = ctypes.create_string_buffer(64)
         _lib.check("pmoe_ipc_handle", self.lib.pmoe_ipc_handle(self.rx_local, h))
         ptrs = []
@@ -381,6 +415,7 @@ class EPGroup:
             ptrs.append(p.value)
         self.rx_ptrs = ptrs
         self.rx_arr = (ctypes.c_void_p * self.world)(*ptrs)
+        _lib.check("pmoe_comm_set_rows", self.lib.pmoe_comm_set_rows(self.comm, self.rx_arr, T))
         torch.cuda.synchronize()
         dist.barrier(self.group)
 
@@ -389,6 +424,7 @@ class EPGroup:
             return
         torch.cuda.synchronize()
         dist.barrier(self.group)
+        _lib.check("pmoe_comm_set_rows", self.lib.pmoe_comm_set_rows(self.comm, None, 0))
         for r, p in enumerate(self.rx_ptrs):
             if r != self.rank:
                 self.lib.pmoe_ipc_close(p)
@@ -442,6 +478,9 @@ class EPGroup:
                     if r != self.rank:
                         self.lib.pmoe_ipc_close(p)
                 self.lib.pmoe_ipc_free(self.local_buf)
+        if self.comm:
+            self.lib.pmoe_comm_destroy(self.comm)
+            self.comm = None
         self.peer_ptrs = None
         self.local_buf = None
         self.rx_local = None
@@ -465,6 +504,6 @@ def patch_moe_for_ep(model, rank: int, world_size: int, mode: str = "fused") -> 
                 group = EPGroup(m.gate.weight.shape[0], m.gate.weight.shape[1],
                                 int(m.gate.top_k), mode=mode)
             m._pmoe_expert_range = (group.lo, group.hi)
-            m._pmoe_post = (lambda blk, x, g=group: g.forward(x, block_weights(blk)))
+            m._pmoe_post = (lambda blk, x, g=group: g.op_forward(x, block_weights(blk)))
             count += 1
     return count

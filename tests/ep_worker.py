@@ -48,6 +48,36 @@ def main():
             ok &= good
             print(f"rank{rank} {name} T={T} exchange={g.uses_exchange(T)} rel_l2={r:.2e} "
                   f"max_abs={m:.2e} {'ok' if good else 'FAIL'}", flush=True)
+            if name == "fused":
+                # the registered operator with the group's comm_handle (the call
+                # the patched HF module makes) gives the same bits
+                yo = fused.op_forward(x, tensors).float().cpu().numpy()
+                same = bool((yo == y).all())
+                ok &= same
+                print(f"rank{rank} op(comm_handle) T={T} same bits as EPGroup.forward "
+                      f"{'ok' if same else 'FAIL'}", flush=True)
+    # the operator with comm_handle captured in a CUDA graph at a decode
+    # bucket replays to the eager result (device-side epoch)
+    x = W.make_hidden(32, S, seed=77, device=dev)
+    eager = fused.op_forward(x, tensors)
+    xs = x.clone()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        fused.op_forward(xs, tensors)              # warm-up on the capture stream
+    torch.cuda.synchronize()
+    dist.barrier()
+    with torch.cuda.graph(g, stream=side):
+        yg = fused.op_forward(xs, tensors)
+    good = True
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        good &= torch.equal(yg, eager)
+    ok &= good
+    print(f"rank{rank} op(comm_handle) T=32 CUDA graph replays bit-identical "
+          f"{'ok' if good else 'FAIL'}", flush=True)
     # MoE-only stack (3 layers, decode T=64): across ranks over the exchange
     # equals the single-GPU layers bit for bit, eagerly and as a CUDA graph.
     from paris_moe_b200 import stack

@@ -109,3 +109,63 @@ def test_rows_fused_rejects_bad_args_before_touching_gpu(lib):
     assert call(flags=2) == -1          # the slice combine needs routed and shared rows
     assert call() == -1                 # null x / weights / y / workspace
     assert call(T=0) == 0               # empty batch: no-op
+
+
+def test_communicator_host_logic(lib):
+    """pmoe_comm_*: registration, the row exchange's epoch (restarted when
+    buffers are re-registered), and the capacity refusal, which
+    pmoe_block_forward_comm returns before touching any pointer."""
+    P = ctypes.c_void_p
+    c = P()
+    assert lib.pmoe_comm_create(0, 9, ctypes.byref(c)) == -1        # more than 8 ranks
+    assert lib.pmoe_comm_create(2, 2, ctypes.byref(c)) == -1
+    assert lib.pmoe_comm_create(1, 2, ctypes.byref(c)) == 0
+    r, w, et, rt = (ctypes.c_int() for _ in range(4))
+    assert lib.pmoe_comm_info(c, *(ctypes.byref(v) for v in (r, w, et, rt))) == 0
+    assert (r.value, w.value, et.value, rt.value) == (1, 2, 0, 0)
+    bufs = (P * 2)(0x10000, 0x20000)
+    assert lib.pmoe_comm_set_ep(c, (P * 2)(0x10000, 0x20008), 4096, 64) == -1  # misaligned
+    assert lib.pmoe_comm_set_ep(c, bufs, 4096, 64) == 0
+    assert lib.pmoe_comm_set_rows(c, bufs, 1000) == 0
+    assert lib.pmoe_comm_info(c, *(ctypes.byref(v) for v in (r, w, et, rt))) == 0
+    assert (et.value, rt.value) == (64, 1000)
+    e = ctypes.c_int()
+    for want in (1, 2, 3):
+        assert lib.pmoe_comm_next_rows_epoch(c, ctypes.byref(e)) == 0 and e.value == want
+    assert lib.pmoe_comm_set_rows(c, bufs, 1000) == 0                 # fresh buffers
+    assert lib.pmoe_comm_next_rows_epoch(c, ctypes.byref(e)) == 0 and e.value == 1
+    ws = [None] * 7
+    assert lib.pmoe_block_forward_comm(c, None, 1001, 2048, 256, 8, 512, 512, *ws, 3, None,
+                                       None, 0, None, None, 0) == -9
+    # shared or routed alone cannot use the row exchange
+    assert lib.pmoe_block_forward_comm(c, None, 100, 2048, 256, 8, 512, 512, *ws, 1, None,
+                                       None, 0, None, None, 0) == -9
+    assert b"exchange buffers" in lib.pmoe_status_string(-9)
+    assert lib.pmoe_comm_destroy(c) == 0
+    assert lib.pmoe_comm_destroy(None) == -1
+
+
+def test_torch_ops_registered_with_the_boundary_schema():
+    """torch.ops.paris_moe.* come from the C++ library, with the ep_rank /
+    ep_size / comm_handle keyword arguments; Meta kernels give the shapes;
+    CPU tensors raise instead of computing."""
+    import torch
+    from paris_moe_b200 import ops
+    sch = torch.ops.paris_moe.moe_block.default._schema
+    kw = [a.name for a in sch.arguments if a.kwarg_only]
+    assert kw == ["ep_rank", "ep_size", "comm_handle"]
+    assert os.path.basename(ops.OPS_LIB_PATH) == "libparis_moe_torch.so"
+    H, E, I, Is, T = 64, 8, 32, 32, 5
+    m = dict(device="meta", dtype=torch.bfloat16)
+    x = torch.empty(T, H, **m)
+    w = (torch.empty(E, H, **m), torch.empty(E, 2 * I, H, **m), torch.empty(E, H, I, **m),
+         torch.empty(Is, H, **m), torch.empty(Is, H, **m), torch.empty(H, Is, **m),
+         torch.empty(1, H, **m))
+    assert ops.moe_block(x, *w, 2, ep_rank=1, ep_size=2).shape == (T, H)
+    outs = ops.moe_route(x, w[0], w[6], 2)
+    assert [tuple(o.shape) for o in outs] == [(T, 2), (T, 2), (E + 1,), (2 * T,), (2 * T,), (T,)]
+    assert [o.dtype for o in outs] == [torch.int32, torch.float32, torch.int32, torch.int32,
+                                       torch.int32, torch.float32]
+    c = torch.zeros(T, H, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ops.rmsnorm(c, torch.zeros(H, dtype=torch.bfloat16), 1e-6)

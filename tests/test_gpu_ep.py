@@ -262,3 +262,85 @@ def test_rows_fused_single_rank_matches_block(T):
     status = ctypes.c_int(-1)
     assert lib.pmoe_rows_status(buf.data_ptr(), ctypes.byref(status)) == 0
     assert status.value == 0
+
+
+def test_op_ep_partials_match_c_abi():
+    """torch.ops.paris_moe.moe_block(..., ep_rank=r, ep_size=4) without a
+    communicator is rank r's partial (its experts, its shared-expert tokens):
+    the same bits as pmoe_block_forward_ep with those ranges, and the four
+    partials sum to the whole block."""
+    from oracle import moe_oracle as O
+    from paris_moe_b200 import _lib, ops, workload as W
+    from paris_moe_b200.ep import expert_range, token_range
+    lib = _lib.load()
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=5, device="cuda")
+    T = 48
+    x = W.make_hidden(T, S, seed=8, device="cuda")
+    full = ops.moe_block(x, *wts.tensors(), S.K).float()
+    n = _lib.workspace_size(T, S.H, S.E, S.K, S.I, S.Is)
+    acc = torch.zeros_like(full)
+    for r in range(4):
+        got = ops.moe_block(x, *wts.tensors(), S.K, ep_rank=r, ep_size=4)
+        ws = torch.empty(n, dtype=torch.uint8, device="cuda")
+        want = torch.empty_like(x)
+        lo, hi = expert_range(S.E, r, 4)
+        slo, shi = token_range(T, r, 4)
+        assert lib.pmoe_block_forward_ep(
+            x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *[t.data_ptr() for t in wts.tensors()],
+            lo, hi, slo, shi, 3, None, 0, r, 4, 0, want.data_ptr(), ws.data_ptr(), n,
+            torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        acc += got.float()
+    assert O.rel_l2(acc.cpu().numpy(), full.cpu().numpy()) < 5e-3
+
+
+def test_op_comm_handle_world1_is_the_block():
+    """A one-rank communicator: the operator with comm_handle is the block."""
+    from paris_moe_b200 import ops, workload as W
+    from paris_moe_b200.ep import EPGroup
+    S = W.MoEShape()
+    wts = W.make_weights(S, seed=3, device="cuda")
+    g = EPGroup.emulated(S.E, S.H, S.K, 0, 1)
+    for T in (16, 300):
+        x = W.make_hidden(T, S, seed=T, device="cuda")
+        y = ops.moe_block(x, *wts.tensors(), S.K, ep_rank=0, ep_size=1,
+                          comm_handle=g.comm_handle)
+        assert torch.equal(y, ops.moe_block(x, *wts.tensors(), S.K))
+    g.close()
+
+
+def test_op_comm_handle_missing_peer_raises():
+    """The operator over a communicator whose rank 1 never runs (decode
+    exchange, then the row exchange): the bounded waits give up, and the
+    group raises PMOE_ERR_PEER_TIMEOUT through the patched module's path
+    (EPGroup.op_forward); a batch above the registered buffers is refused by
+    the communicator with PMOE_ERR_COMM_CAPACITY."""
+    from paris_moe_b200 import _lib, ops, workload as W
+    from paris_moe_b200.ep import EPGroup
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=128, Is=128)
+    wts = W.make_weights(S, seed=2, device="cuda")
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_ep_buffer_bytes(64, S.H, S.K, ctypes.byref(nb)) == 0
+    ep_bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    assert lib.pmoe_rows_fused_buffer_bytes(200, S.H, S.K, ctypes.byref(nb)) == 0
+    rx_bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    for T in (8, 200):
+        g = EPGroup.emulated(S.E, S.H, S.K, 0, 2, peer_bufs=[b.data_ptr() for b in ep_bufs],
+                             rows_bufs=[b.data_ptr() for b in rx_bufs], rows_t_max=200)
+        x = W.make_hidden(T, S, seed=T, device="cuda")
+        t0 = time.time()
+        g.op_forward(x, wts.tensors())
+        with pytest.raises(_lib.PmoeError) as ei:
+            g.check()
+        assert ei.value.status == _lib.PMOE_ERR_PEER_TIMEOUT
+        assert time.time() - t0 < 60
+        with pytest.raises(RuntimeError, match="status -9"):
+            ops.moe_block(W.make_hidden(201, S, seed=1, device="cuda"), *wts.tensors(), S.K,
+                          ep_rank=0, ep_size=2, comm_handle=g.comm_handle)
+        with pytest.raises(_lib.PmoeError):
+            g.close()
+        for b in ep_bufs + rx_bufs:
+            b.zero_()
