@@ -226,6 +226,10 @@ class EPGroup:
         ev = self._st_event
         if ev is None:
             return
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            # no event query while a graph is being captured: the sticky word
+            # is read at the next call outside the capture
+            return
         if block:
             ev.synchronize()
         elif not ev.query():

@@ -344,3 +344,34 @@ def test_op_comm_handle_missing_peer_raises():
             g.close()
         for b in ep_bufs + rx_bufs:
             b.zero_()
+
+
+def test_capture_after_an_exchange_call_skips_the_status_poll():
+    """An exchange call records a status event; capturing the next call in a
+    CUDA graph must not query it (CUDA forbids event queries during capture).
+    Rank 1 of the emulated group never runs, so the eager call times out and
+    the sticky word is raised at check() after the capture.  The graph is
+    not replayed."""
+    from paris_moe_b200 import _lib, workload as W
+    from paris_moe_b200.ep import EPGroup
+    lib = _lib.load()
+    S = W.MoEShape(H=256, E=16, K=4, I=64, Is=64)
+    wts = W.make_weights(S, seed=1, device="cuda")
+    x = W.make_hidden(8, S, seed=1, device="cuda")
+    nb = ctypes.c_size_t(0)
+    assert lib.pmoe_ep_buffer_bytes(64, S.H, S.K, ctypes.byref(nb)) == 0
+    bufs = [torch.zeros(nb.value, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    g = EPGroup.emulated(S.E, S.H, S.K, 0, 2, peer_bufs=[b.data_ptr() for b in bufs])
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        g.op_forward(x, wts.tensors())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        g.op_forward(x, wts.tensors())
+    with pytest.raises(_lib.PmoeError) as ei:
+        g.check()
+    assert ei.value.status == _lib.PMOE_ERR_PEER_TIMEOUT
+    del graph
+    with pytest.raises(_lib.PmoeError):
+        g.close()
