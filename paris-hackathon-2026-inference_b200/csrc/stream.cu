@@ -13,6 +13,11 @@
 //   * warps 1..4: consumers.  Each owns 16 weight rows of the tile, reads
 //     its mma.sync A and B fragments from shared memory with 128-bit loads,
 //     and releases the stage.
+// That is gate_up (96-97 % of the HBM copy rate).  The down projection, whose
+// per-stage work left the mma.sync consumers the limit, runs on the tcgen05
+// tensor cores instead (down_tc_kernel: single-thread MMA issue from the
+// staged tiles, accumulators in TMEM); down_tma_kernel is kept for shapes it
+// does not take.
 // Every weight byte is loaded from HBM exactly once per call.
 //
 // Reference arithmetic: the per-expert body of Qwen3_5MoeExperts.forward
@@ -61,7 +66,8 @@ struct GuCfg {
 };
 template <int KCH>
 struct DnCfg {
-  static constexpr int kStageBytes = KCH * (kBoxBytes + kActChunkBytes);
+  static constexpr int kActBytes = kActChunkBytes;
+  static constexpr int kStageBytes = KCH * (kBoxBytes + kActBytes);
   static constexpr int kStages = kRingBudget / kStageBytes > 16 ? 16 : kRingBudget / kStageBytes;
   static constexpr int kSmem = kStages * kStageBytes + 2 * kStages * 8 + 1024;
 };
@@ -299,6 +305,8 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
     float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep,
     int row_blocks) {
   using C = DnCfg<KCH>;
+  constexpr int AR = kActRows;
+  constexpr int kGroups = AR / 8;
   const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -353,14 +361,14 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
       const int nkc = (sh ? Is : I) / (kKC * KCH);
       const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
       // passes of up to 32 dispatched rows, each over the unit's row blocks
-      for (int nb = 0; nb < n; nb += kActRows) {
+      for (int nb = 0; nb < n; nb += AR) {
       for (int sub = 0; sub < row_blocks; ++sub) {
         const int rb = rbg * row_blocks + sub;
         const int row = sh ? rb * kUnitRows : e * H + rb * kUnitRows;
         // passes of at most 8 rows load an 8-row activation box (1 KiB/chunk)
         const bool small = n - nb <= 8;
         const CUtensorMap* mh = small ? &tm_h8 : &tm_h;
-        const uint32_t hbytes = small ? 8 * kKC * 2 : kActChunkBytes;
+        const uint32_t hbytes = small ? 8 * kKC * 2 : C::kActBytes;
         for (int kc = 0; kc < nkc; ++kc, ++it) {
           const int s = it % kStages;
           if (it >= uint32_t(kStages) && !mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1)) {
@@ -374,7 +382,7 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
           for (int j = 0; j < KCH; ++j) {
             const int k = (kc * KCH + j) * kKC;
             tma_load_2d_hint(dst + j * kBoxBytes, m, k, row, &full[s], pol);
-            tma_load_2d(dst + KCH * kBoxBytes + j * kActChunkBytes, mh, k, p0 + nb, &full[s]);
+            tma_load_2d(dst + KCH * kBoxBytes + j * C::kActBytes, mh, k, p0 + nb, &full[s]);
           }
         }
       }
@@ -385,7 +393,12 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
 
   // consumer warp cw: rows slice rq (16 rows), k half kh of every stage
   const int cw = warp - 1, rq = cw & 3, kh = cw >> 2, g = lane >> 2, c = lane & 3;
-  const int r0 = rq * 16 + g, r1 = r0 + 8;
+  // Fragment row / token g of the MMA is weight row (and token) gp = pi(g),
+  // pi = 0,4,1,5,2,6,3,7: the two rows a quarter-warp reads then differ in
+  // bit 2, so their four 16-byte chunks land in opposite halves of the
+  // 128-byte swizzle pattern (no bank conflict; adjacent rows collide).
+  const int gp = (g >> 1) | ((g & 1) << 2);
+  const int r0 = rq * 16 + gp, r1 = r0 + 8;
   const uint32_t sbase = smem_u32(smem);
   uint32_t it = 0, blk = 0;
   for (uint32_t ui = 0;; ++ui) {
@@ -399,17 +412,17 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
     const int e = inf.x, p0 = inf.y, n = inf.z, rbg = u % UR;
     const bool sh = (e == E);
     const int nkc = (sh ? Is : I) / (kKC * KCH);
-    for (int nb = 0; nb < n; nb += kActRows) {
-    const int ng = min(4, (n - nb + 7) / 8);
+    for (int nb = 0; nb < n; nb += AR) {
+    const int ng = min(kGroups, (n - nb + 7) / 8);
     // this lane's output rows of the pass (weight, destination), loaded once
     // for all of the unit's row blocks, before the first stage wait
     float wt[4][2];
     int dsti[4][2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < kGroups; ++q)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int i = nb + q * 8 + 2 * c + hh;
+        const int i = nb + q * 8 + c + 4 * hh;  // token of accumulator column 2c + hh
         const bool ok = kh == 0 && q < ng && i < n;
         wt[q][hh] = ok ? tb.pair_w[p0 + i] : 0.f;
         dsti[q][hh] = ok ? tb.pair_dst[p0 + i] : -1;
@@ -429,15 +442,15 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
           if (KCH > 1 && (2 * j) / KCH != kh) continue;  // the other warp's half
           if (KCH == 1 && kh != 0) continue;
           const uint32_t tw = st0 + j * kBoxBytes;
-          const uint32_t th = st0 + KCH * kBoxBytes + j * kActChunkBytes;
+          const uint32_t th = st0 + KCH * kBoxBytes + j * C::kActBytes;
 #pragma unroll
           for (int ks = 0; ks < 2; ++ks) {
             const int ch = ks * 4 + c;
             const uint4 a0 = lds128(tw + swz128(r0, ch)), a1 = lds128(tw + swz128(r1, ch));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < kGroups; ++q) {
               if (q < ng) {
-                const uint4 hv = lds128(th + swz128(q * 8 + g, ch));
+                const uint4 hv = lds128(th + swz128(q * 8 + gp, ch));
                 mma_k32(acc[q], a0, a1, hv);
               }
             }
@@ -452,19 +465,19 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
       float* slot = &s_part[blk & 1][rq][lane][0];
       if (kh == 1) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < kGroups; ++q)
 #pragma unroll
           for (int i = 0; i < 4; ++i) slot[q * 4 + i] = acc[q][i];
       }
       named_bar_sync(1 + rq, 64);
       if (kh == 1) continue;
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int q = 0; q < kGroups; ++q)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[q][i] += slot[q * 4 + i];
       const int orow = rb * kUnitRows + r0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < kGroups; ++q) {
         if (q < ng) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
@@ -504,6 +517,263 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
         for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, epoch);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// down + routing weight on the tcgen05 tensor cores (the decode default).
+// Unit = (expert, row_blocks x 128 output rows of down_proj).  A stage holds
+// one 128-row x 64-k weight box and the same k of the pass's 16 dispatched
+// rows of h (128-byte swizzle; rows past the end of h read as zero), so one
+// stage is four M128 x N16 x K16 MMAs issued by a single thread; the fp32
+// accumulator of a row block (128 TMEM lanes x 16 columns) is double
+// buffered.  Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// warps 2-5 epilogue (TMEM lane quadrant warp % 4): each lane owns one
+// output row, so every store of a token's 32 rows is one 128-byte segment.
+// The mma.sync version (down_tma_kernel) was bound by the legacy MMA
+// instruction rate, not by HBM.
+// rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
+// ---------------------------------------------------------------------------
+constexpr int kDtRows = 128;                          // weight rows per MMA (TMEM lanes)
+constexpr int kDtTok = 16;                            // dispatched rows per pass (MMA N)
+constexpr int kDtWBytes = kDtRows * kKC * 2;          // 16 KiB weight box
+constexpr int kDtHBytes = kDtTok * kKC * 2;           // 2 KiB activation box
+constexpr int kDtStageBytes = kDtWBytes + kDtHBytes;  // 18 KiB, a multiple of 1 KiB
+constexpr int kDtStages = 12;                         // 216 KiB ring
+constexpr int kDtEpiWarps = 4;
+constexpr int kDtThreads = 32 * (2 + kDtEpiWarps);
+constexpr int kDtBarBytes = 256;
+constexpr int kDtSmem = kDtStages * kDtStageBytes + kDtBarBytes + 1024;
+constexpr uint32_t kDtTmemCols = 32;                  // two 16-column accumulators
+static_assert(kDtStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
+static_assert((2 * kDtStages + 5) * 8 + 4 <= kDtBarBytes, "barrier area");
+static_assert(kDtSmem <= 227 * 1024, "shared memory");
+
+__global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_dn, const __grid_constant__ CUtensorMap tm_sd,
+    const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
+    float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep,
+    int row_blocks) {
+  const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDtStages * kDtStageBytes);
+  uint64_t* empty = full + kDtStages;
+  uint64_t* tfull = empty + kDtStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  __shared__ UnitRing ur;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kDtEpiWarps);
+    }
+    mbar_init(done, 1);
+    ur.init(1 + kDtEpiWarps);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kDtTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int UR = H / (kDtRows * row_blocks);
+  const int n_units = tb.n_active[0] * UR;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tm_dn);
+      prefetch_tmap(&tm_sd);
+      prefetch_tmap(&tm_h);
+      const uint64_t pol = l2_policy_evict_first();
+      uint32_t it = 0;
+      bool ok = true;
+      int u_next = ur.ticket(queue, n_units);
+      for (uint32_t ui = 0; ok; ++ui) {
+        const int u = u_next;
+        int e = 0, p0 = 0, n = 0;
+        if (u >= 0) {
+          e = tb.active[u / UR];
+          p0 = tb.offsets[e];
+          n = tb.offsets[e + 1] - p0;
+        }
+        if (!ur.publish_unit(ui, u, make_int4(e, p0, n, 0))) {
+          set_status(status, kStatusTimeoutEmpty);
+          break;
+        }
+        if (u < 0) break;
+        u_next = ur.ticket(queue, n_units);
+        const bool sh = (e == E);
+        const int nkc = (sh ? Is : I) / kKC;
+        const CUtensorMap* m = sh ? &tm_sd : &tm_dn;
+        // a unit read in several passes keeps its weights in L2 for the next
+        const bool reread = n > kDtTok;
+        for (int nb = 0; nb < n && ok; nb += kDtTok) {
+          for (int sub = 0; sub < row_blocks && ok; ++sub) {
+            const int rb = (u % UR) * row_blocks + sub;
+            const int row = sh ? rb * kDtRows : e * H + rb * kDtRows;
+            for (int kc = 0; kc < nkc; ++kc, ++it) {
+              const int s = it % kDtStages;
+              if (it >= uint32_t(kDtStages) &&
+                  !mbar_wait(&empty[s], ((it / kDtStages) & 1) ^ 1)) {
+                set_status(status, kStatusTimeoutEmpty);
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&full[s], kDtStageBytes);
+              uint8_t* dst = smem + s * kDtStageBytes;
+              if (reread)
+                tma_load_2d(dst, m, kc * kKC, row, &full[s]);
+              else
+                tma_load_2d_hint(dst, m, kc * kKC, row, &full[s], pol);
+              tma_load_2d(dst + kDtWBytes, &tm_h, kc * kKC, p0 + nb, &full[s]);
+            }
+          }
+        }
+      }
+      if (!ok) drain(full, it, kDtStages);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = idesc_bf16_f32(kDtRows, kDtTok);
+    const uint32_t sbase = smem_u32(smem);
+    uint32_t it = 0, acc = 0;
+    bool ok = true;
+    for (uint32_t ui = 0; ok; ++ui) {
+      int u;
+      int4 inf;
+      if (!ur.take(ui, lane, &u, &inf)) {
+        set_status(status, kStatusTimeoutFull);
+        break;
+      }
+      if (u < 0) break;
+      const int n = inf.z;
+      const int nkc = (inf.x == E ? Is : I) / kKC;
+      for (int nb = 0; nb < n && ok; nb += kDtTok) {
+        for (int sub = 0; sub < row_blocks && ok; ++sub, ++acc) {
+          const uint32_t b = acc & 1, use = acc >> 1;
+          if (acc >= 2 && !mbar_wait(&tempty[b], (use - 1) & 1)) {
+            set_status(status, kStatusTimeoutTmem);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + b * kDtTok;
+          for (int kc = 0; kc < nkc; ++kc, ++it) {
+            const int s = it % kDtStages;
+            if (!mbar_wait(&full[s], (it / kDtStages) & 1)) {
+              set_status(status, kStatusTimeoutFull);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+              const uint32_t st = sbase + s * kDtStageBytes;
+              const uint64_t wd = sdesc_k_sw128(st), hd = sdesc_k_sw128(st + kDtWBytes);
+#pragma unroll
+              for (int kk = 0; kk < kKC / 16; ++kk)
+                umma_bf16(d, wd + uint64_t(kk * 2), hd + uint64_t(kk * 2), idesc,
+                          (kc | kk) != 0 ? 1u : 0u);
+              umma_commit(&empty[s]);
+            }
+            __syncwarp();
+          }
+          if (!ok) break;
+          if (lane == 0) umma_commit(&tfull[b]);
+          __syncwarp();
+        }
+      }
+    }
+    // every MMA has completed before the TMEM is freed
+    if (lane == 0) umma_commit(done);
+    __syncwarp();
+    mbar_wait(done, 0);
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    uint32_t acc = 0;
+    bool ok = true;
+    for (uint32_t ui = 0; ok; ++ui) {
+      int u;
+      int4 inf;
+      if (!ur.take(ui, lane, &u, &inf)) {
+        set_status(status, kStatusTimeoutFull);
+        ok = false;
+        break;
+      }
+      if (u < 0) break;
+      const int p0 = inf.y, n = inf.z;
+      for (int nb = 0; nb < n && ok; nb += kDtTok) {
+        // lane t < 16: destination row and weight of the pass's token t
+        const int nt = min(kDtTok, n - nb);
+        int my_dst = -1;
+        float my_w = 0.f;
+        if (lane < nt) {
+          my_dst = tb.pair_dst[p0 + nb + lane];
+          my_w = tb.pair_w[p0 + nb + lane];
+        }
+        for (int sub = 0; sub < row_blocks; ++sub, ++acc) {
+          const uint32_t b = acc & 1, use = acc >> 1;
+          if (!mbar_wait(&tfull[b], use & 1)) {
+            set_status(status, kStatusTimeoutTmem);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t v[kDtTok];
+          tmem_ld16(tmem_base + (uint32_t(q * 32) << 16) + b * kDtTok, v);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[b]);
+          const int row = ((u % UR) * row_blocks + sub) * kDtRows + q * 32 + lane;
+#pragma unroll
+          for (int t = 0; t < kDtTok; ++t) {
+            if (t < nt) {
+              const int dst = __shfl_sync(0xffffffffu, my_dst, t);
+              const float val = __uint_as_float(v[t]) * __shfl_sync(0xffffffffu, my_w, t);
+              const size_t off = size_t(dst) * H + row;
+              if (ep.world > 0) {
+                // every computed row goes to every rank (peer stores over NVLink)
+                for (int rr = 0; rr < ep.world; ++rr) ep_rows(ep, rr, epoch)[off] = val;
+              } else {
+                rows[off] = val;
+              }
+            }
+          }
+        }
+      }
+    }
+    if (ok && ep.world > 0) {
+      // All of this warp's peer stores are made visible system-wide before it
+      // takes a ticket; the last epilogue warp of the grid releases the flags.
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0) {
+        const int prev = atomicAdd(ep.ticket, 1);
+        if (prev == int(gridDim.x) * kDtEpiWarps - 1) {
+          __threadfence_system();
+          *ep.ticket = 0;
+          for (int rr = 0; rr < ep.world; ++rr) st_release_sys(ep.flags[rr] + ep.rank, epoch);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kDtTmemCols);
   }
 }
 
@@ -610,7 +880,8 @@ namespace {
 int g_num_sms = 148;
 int g_kch_gu = 4;  // k-chunks per gate_up stage (512 B per weight row)
 int g_dn_row_blocks = kDnRowBlocks;
-int g_kch_dn = 8;  // k-chunks per down stage (two 96 KiB stages: measured 101 vs 106 us at 4)
+int g_kch_dn = 8;
+bool g_down_sync = false;  // force the mma.sync down kernel (comparison)  // k-chunks per down stage (two 96 KiB stages: measured 101 vs 106 us at 4)
 
 template <int KCH>
 cudaError_t set_attrs() {
@@ -641,6 +912,7 @@ cudaError_t stream_init(int num_sms) {
   g_num_sms = num_sms;
   g_kch_gu = env_kch("PMOE_STREAM_KCH_GU", g_kch_gu);
   g_kch_dn = env_kch("PMOE_STREAM_KCH_DN", g_kch_dn);
+  if (const char* v = std::getenv("PMOE_DOWN_SYNC")) g_down_sync = std::atoi(v) != 0;
   if (const char* v = std::getenv("PMOE_DN_ROWBLOCKS")) {
     const int r = std::atoi(v);
     if (r == 1 || r == 2 || r == 4 || r == 8 || r == 16) g_dn_row_blocks = r;
@@ -648,9 +920,12 @@ cudaError_t stream_init(int num_sms) {
   cudaError_t e = set_attrs<1>();
   if (e == cudaSuccess) e = set_attrs<2>();
   if (e == cudaSuccess) e = set_attrs<4>();
-  if (e == cudaSuccess)  // down only: 8 k-chunks (two 96 KiB stages) per stage
+  if (e == cudaSuccess)  // down only: 8 k-chunks per stage
     e = cudaFuncSetAttribute(down_tma_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              DnCfg<8>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kDtSmem);
   return e;
 }
 
@@ -689,8 +964,23 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (e != cudaSuccess) return e;
   }
-  if (kd == 8) PMOE_DN(8); else if (kd == 4) PMOE_DN(4); else if (kd == 2) PMOE_DN(2);
-  else PMOE_DN(1);
+  // tcgen05 down: 128-row weight boxes, 16-row activation boxes
+  const bool down_tc = !g_down_sync && d.H % kDtRows == 0 && d.I % kKC == 0 && d.Is % kKC == 0;
+  if (down_tc) {
+    CUtensorMap tm_dn128, tm_sd128, tm_h16;
+    if (!make_tmap_bf16_2d(&tm_dn128, w_down, I, E * H, I * 2, kKC, kDtRows) ||
+        !make_tmap_bf16_2d(&tm_sd128, w_sh_down, Is, H, Is * 2, kKC, kDtRows) ||
+        !make_tmap_bf16_2d(&tm_h16, ws.h, ldh, R, ldh * 2, kKC, kDtTok))
+      return cudaErrorInvalidValue;
+    int rbt = 4;  // 128-row blocks per unit, dividing H / 128
+    while (rbt > 1 && (d.H / kDtRows) % rbt != 0) rbt >>= 1;
+    down_tc_kernel<<<g_num_sms, kDtThreads, kDtSmem, st>>>(
+        tm_dn128, tm_sd128, tm_h16, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep,
+        rbt);
+  } else {
+    if (kd == 8) PMOE_DN(8); else if (kd == 4) PMOE_DN(4); else if (kd == 2) PMOE_DN(2);
+    else PMOE_DN(1);
+  }
 #undef PMOE_GU
 #undef PMOE_DN
   return cudaGetLastError();
