@@ -852,7 +852,26 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
   const int chunk = H / NW;  // elements per warp (a multiple of 16)
   const int lg = 32 - __clz(H + 63);
   const int room = 127 - 16 - 2 - lg;
-  if (nreq > 0) {
+  if (nreq > NW / 4) {
+    // Many evaluations: one warp per evaluation (warp_exact_dot, the same
+    // exactly rounded value), so their row loads are independent instead of
+    // one dependent round trip per evaluation in every warp.
+    for (int r = warp; r < nreq; r += NW) {
+      const auto& q = sm.req[r];
+      if (q.slot < 0) continue;
+      bool ok;
+      const float rv = warp_exact_dot(x + size_t(q.t) * H, w_router + size_t(q.e) * H, H, ok);
+      if (lane == 0) {
+        auto& P = sm.pend[q.slot];
+        P.klo[q.ci] = P.khi[q.ci] = logit_key(rv, q.e);
+        P.val[q.ci] = rv;
+        atomicAdd(stats.n_exact, 1);
+        if (!ok) atomicAdd(stats.n_inexact, 1);
+      }
+    }
+    __syncthreads();
+  } else if (nreq > 0) {
+    // Few evaluations (decode): each is split over the warps.
     // B1: exponent ranges of the queued rows (the loads of every request of
     // this warp's pass are issued before any is used: up to 4 at a time)
     for (int r0 = 0; r0 < nreq; r0 += 4) {

@@ -242,7 +242,10 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
 //                       by the CTA's warps.
 constexpr int kRtFastThreads = 256;
 constexpr int kRtFixThreads = 256;
-constexpr int kRtFixTokens = 8;
+// 4 queued tokens per CTA (fix-up of the Zipf T = 8192 case: 8 per CTA 39-43
+// us, 4: 31-35, 2: 41-42, 1: 56-58 -- fewer tokens per CTA spread the exact
+// evaluations over more SMs until the extra CTA rounds cost more)
+constexpr int kRtFixTokens = 4;
 
 __global__ void __launch_bounds__(kRtFastThreads) route_fast_kernel(
     const float* __restrict__ logits, const float* __restrict__ xnorm,
@@ -492,7 +495,7 @@ cudaError_t launch_router_tc(const Dims& d, const __nv_bfloat16* x, const __nv_b
   int sms = 148, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  route_fixup_kernel<<<2 * sms, kRtFixThreads, 0, st>>>(
+  route_fixup_kernel<<<4 * sms, kRtFixThreads, 0, st>>>(
       logits, xnorm, wnorm, x, w_router, d.H, d.E, d.K, d.Rpad, gamma, queue, queue_count,
       topk_idx, topk_w, hist, ExactStats{status + 8, status + 9});
   return cudaGetLastError();
