@@ -76,17 +76,67 @@ def measured_peaks():
 # ------------------------------------------------------------------ clocks --
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    """SM clocks and clock-event (throttle) reasons of this rank's GPU during
+    a region, read through NVML -- the counters nvidia-smi reports -- by a
+    thread every ~2 ms, plus one reading at each edge of the region, so even
+    a region of a few milliseconds has samples.  Falls back to nvidia-smi
+    (-lms 20) when NVML is unavailable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.f = None
+        self.nvml = None
+        self.handle = None
+        self.samples = []      # (sm MHz, max sm MHz, set of reasons)
+        self.stop = None
+        self.thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:  # the CUDA device's own GPU (CUDA and NVML orderings can differ)
+            uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _read(self):
+        N, h = self.nvml, self.handle
+        try:
+            sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+            smax = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            bits = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+        except Exception:
+            return
+        flags = {"hw_slowdown": N.nvmlClocksEventReasonHwSlowdown,
+                 "hw_thermal_slowdown": N.nvmlClocksEventReasonHwThermalSlowdown,
+                 "sw_thermal_slowdown": N.nvmlClocksEventReasonSwThermalSlowdown,
+                 "sw_power_cap": N.nvmlClocksEventReasonSwPowerCap}
+        self.samples.append((float(sm), float(smax), {n for n, b in flags.items() if bits & b}))
 
     def __enter__(self):
+        import threading
+        try:
+            self.nvml, self.handle = self._nvml_handle()
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self._read()
+            self.stop = threading.Event()
+
+            def loop():
+                while not self.stop.wait(0.002):
+                    self._read()
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.f = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
@@ -99,6 +149,11 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self.thread is not None:
+            self._read()
+            self.stop.set()
+            self.thread.join(timeout=5)
+            return
         if self.proc is not None:
             time.sleep(0.05)
             self.proc.terminate()
@@ -108,11 +163,17 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.thread is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+            reasons = set().union(*(r for _, _, r in self.samples))
+            return {"sm_mhz": statistics.median(x for x, _, _ in self.samples),
+                    "sm_max_mhz": max(x for _, x, _ in self.samples),
+                    "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
         if self.proc is None or self.f is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
         self.f.seek(0)
         sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -122,13 +183,13 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.NAMES, parts[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -254,11 +315,16 @@ class Runner:
         torch.cuda.synchronize()
         with ClockSampler(c.local) as clk:
             t0.record(c.st)
+            h0 = time.perf_counter()
             for _ in range(steps):
                 self.step()
+            # host time to enqueue the steps: near the device time means the
+            # loop is launch-bound, not GPU-bound
+            host = (time.perf_counter() - h0) * 1e3 / steps
             t1.record(c.st)
             torch.cuda.synchronize()
         c.barrier()
+        self.host_ms = c.max_over_ranks(host)
         return c.max_over_ranks(t0.elapsed_time(t1)) / steps, clk.summary()
 
     def phases(self, n):
@@ -357,11 +423,14 @@ def comparators(c, x, tensors, T, steps, warmup):
     out = {}
     runs = [("nccl", "nccl_all_reduce"), ("a2a", "all_to_all")]
     if T > ep.FUSED_MAX_T:
-        runs.append(("fused", "nvlink_partial_sum"))   # the earlier prefill exchange
+        # the prefill exchange EPGroup does not default to at this world size
+        runs.append(("fused", "nvlink_partial_sum" if c.world < 8 else "nvlink_rows_to_owner"))
     for mode, label in runs:
         g = ep.EPGroup(c.S.E, c.S.H, c.S.K, mode=mode)
         if label == "nvlink_partial_sum":
             g.prefill = "partial"
+        elif label == "nvlink_rows_to_owner":
+            g.prefill = "rows"
         y = torch.empty_like(x)
         for _ in range(warmup):
             g.forward(x, tensors, out=y)
@@ -513,7 +582,7 @@ def main():
         + (a.T * S.K + a.T) * S.I * 2
     line = {
         "metric": metric, "value": a.T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "host_ms_per_step": dec.host_ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init bf16 weights N(0,0.02), hidden N(0,1), seed 0)",
         "config": config, "e2e": e2e,
@@ -559,7 +628,7 @@ def main():
         flops = W.block_flops(S, a.prefill_T)
         pl = {"metric": f"MoE layer tokens/s (prefill T={a.prefill_T}, Zipf s={a.zipf})",
               "value": a.prefill_T / (pms * 1e-3), "unit": "tokens/s", "steps": psteps,
-              "ms_per_step": pms, "algorithmic_flops": flops,
+              "ms_per_step": pms, "host_ms_per_step": pre.host_ms, "algorithmic_flops": flops,
               "layer_tflops": flops / (pms * 1e-3) / 1e12,
               "layer_frac": flops / (pms * 1e-3) / 1e12 / peaks["bf16_tflops"],
               # router_tc, scan, scatter, plan, row copy, gate_up, down, combine per step;

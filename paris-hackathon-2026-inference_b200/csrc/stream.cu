@@ -526,10 +526,11 @@ __global__ void __launch_bounds__(kDnThreads, 1) down_tma_kernel(
 // one 128-row x 64-k weight box and the same k of the pass's 16 dispatched
 // rows of h (128-byte swizzle; rows past the end of h read as zero), so one
 // stage is four M128 x N16 x K16 MMAs issued by a single thread; the fp32
-// accumulator of a row block (128 TMEM lanes x 16 columns) is double
-// buffered.  Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
-// warps 2-5 epilogue (TMEM lane quadrant warp % 4): each lane owns one
-// output row, so every store of a token's 32 rows is one 128-byte segment.
+// accumulator of a row block (128 TMEM lanes x 16 columns) has four TMEM
+// buffers, so remote stores in the epilogue do not hold up the MMAs.  Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// warps 2-9 epilogue (TMEM lane quadrant warp % 4, token columns 0-7 or 8-15
+// by warp / 6): each lane owns one output row, so every store of a token's 32
+// rows is one 128-byte segment.
 // The mma.sync version (down_tma_kernel) was bound by the legacy MMA
 // instruction rate, not by HBM.
 // rows[pair_dst[p], r] = pair_w[p] * (h[p] . Wd_r).
@@ -540,13 +541,14 @@ constexpr int kDtWBytes = kDtRows * kKC * 2;          // 16 KiB weight box
 constexpr int kDtHBytes = kDtTok * kKC * 2;           // 2 KiB activation box
 constexpr int kDtStageBytes = kDtWBytes + kDtHBytes;  // 18 KiB, a multiple of 1 KiB
 constexpr int kDtStages = 12;                         // 216 KiB ring
-constexpr int kDtEpiWarps = 4;
+constexpr int kDtEpiWarps = 8;   // two per TMEM lane quadrant, each on half the tokens
+constexpr int kDtAcc = 4;        // accumulators in flight (TMEM, 16 columns each)
 constexpr int kDtThreads = 32 * (2 + kDtEpiWarps);
-constexpr int kDtBarBytes = 256;
+constexpr int kDtBarBytes = 512;
 constexpr int kDtSmem = kDtStages * kDtStageBytes + kDtBarBytes + 1024;
-constexpr uint32_t kDtTmemCols = 32;                  // two 16-column accumulators
+constexpr uint32_t kDtTmemCols = kDtAcc * kDtTok;    // 64 columns
 static_assert(kDtStageBytes % 1024 == 0, "stages keep the 1 KiB swizzle alignment");
-static_assert((2 * kDtStages + 5) * 8 + 4 <= kDtBarBytes, "barrier area");
+static_assert((2 * kDtStages + 2 * kDtAcc + 1) * 8 + 4 <= kDtBarBytes, "barrier area");
 static_assert(kDtSmem <= 227 * 1024, "shared memory");
 
 __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
@@ -560,8 +562,8 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDtStages * kDtStageBytes);
   uint64_t* empty = full + kDtStages;
   uint64_t* tfull = empty + kDtStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* done = tempty + 2;
+  uint64_t* tempty = tfull + kDtAcc;
+  uint64_t* done = tempty + kDtAcc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   __shared__ UnitRing ur;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kDtAcc; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kDtEpiWarps);
     }
@@ -661,8 +663,8 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
       const int nkc = (inf.x == E ? Is : I) / kKC;
       for (int nb = 0; nb < n && ok; nb += kDtTok) {
         for (int sub = 0; sub < row_blocks && ok; ++sub, ++acc) {
-          const uint32_t b = acc & 1, use = acc >> 1;
-          if (acc >= 2 && !mbar_wait(&tempty[b], (use - 1) & 1)) {
+          const uint32_t b = acc % kDtAcc, use = acc / kDtAcc;
+          if (acc >= uint32_t(kDtAcc) && !mbar_wait(&tempty[b], (use - 1) & 1)) {
             set_status(status, kStatusTimeoutTmem);
             ok = false;
             break;
@@ -700,7 +702,8 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
     mbar_wait(done, 0);
   } else {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    const int q = warp & 3;            // TMEM lanes 32q .. 32q+31
+    const int th = (warp - 2) >> 2;    // token columns th*8 .. th*8+7
     uint32_t acc = 0;
     bool ok = true;
     for (uint32_t ui = 0; ok; ++ui) {
@@ -723,25 +726,26 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
           my_w = tb.pair_w[p0 + nb + lane];
         }
         for (int sub = 0; sub < row_blocks; ++sub, ++acc) {
-          const uint32_t b = acc & 1, use = acc >> 1;
+          const uint32_t b = acc % kDtAcc, use = acc / kDtAcc;
           if (!mbar_wait(&tfull[b], use & 1)) {
             set_status(status, kStatusTimeoutTmem);
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t v[kDtTok];
-          tmem_ld16(tmem_base + (uint32_t(q * 32) << 16) + b * kDtTok, v);
+          uint32_t v[8];
+          tmem_ld8(tmem_base + (uint32_t(q * 32) << 16) + b * kDtTok + th * 8, v);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[b]);
           const int row = ((u % UR) * row_blocks + sub) * kDtRows + q * 32 + lane;
 #pragma unroll
-          for (int t = 0; t < kDtTok; ++t) {
+          for (int i = 0; i < 8; ++i) {
+            const int t = th * 8 + i;
             if (t < nt) {
               const int dst = __shfl_sync(0xffffffffu, my_dst, t);
-              const float val = __uint_as_float(v[t]) * __shfl_sync(0xffffffffu, my_w, t);
+              const float val = __uint_as_float(v[i]) * __shfl_sync(0xffffffffu, my_w, t);
               const size_t off = size_t(dst) * H + row;
               if (ep.world > 0) {
                 // every computed row goes to every rank (peer stores over NVLink)

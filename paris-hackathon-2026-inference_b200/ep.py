@@ -166,8 +166,12 @@ class EPGroup:
         self.comm = c.value
         # prefill exchange: "rows" (the down GEMM stores rows at their token
         # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
-        # outputs summed by pmoe_rows_allreduce)
-        self.prefill = "rows"
+        # outputs summed by pmoe_rows_allreduce).  Measured (tokens/s, T=8192
+        # Zipf): 2 ranks rows 14.7M / partial 13.9M, 4 ranks 17.4M / 17.1M,
+        # 8 ranks 5.9M / 18.6M -- back-to-back row-exchange calls stalled at 8
+        # ranks (a synchronised call took 0.39 ms, a pipelined one 1.39 ms), so
+        # from 8 ranks on the partial-sum exchange is the default.
+        self.prefill = "rows" if world < 8 else "partial"
         # sticky status words of this rank's exchange buffers ([0] decode, [1]
         # row split), copied here asynchronously after every exchange call
         self._st_host = torch.zeros(2, dtype=torch.int32,
@@ -310,7 +314,8 @@ class EPGroup:
         """forward() through the registered operator, as the patched HF module
         calls it: torch.ops.paris_moe.moe_block with this group's comm_handle
         (mode "fused"; the other modes are comparators and use forward())."""
-        if self.mode != "fused" or self.world == 1:
+        if self.mode != "fused" or self.world == 1 or (
+                self.prefill == "partial" and not self.uses_exchange(x.shape[0])):
             return self.forward(x, weights, flags)
         from . import ops
         self._status_check(block=False)

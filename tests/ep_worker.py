@@ -27,6 +27,7 @@ def main():
     wts = W.make_weights(S, seed=5, device=dev)
     tensors = wts.tensors()
     fused = ep.EPGroup(S.E, S.H, S.K, mode="fused")
+    fused.prefill = "rows"   # the bit-exact row exchange (the default below 8 ranks)
     nccl = ep.EPGroup(S.E, S.H, S.K, mode="nccl")
     a2a = ep.EPGroup(S.E, S.H, S.K, mode="a2a")
     partial = ep.EPGroup(S.E, S.H, S.K, mode="fused")

@@ -50,3 +50,14 @@ def test_a2a_plan_sends_each_token_once_per_owning_rank():
     send, counts = a2a_plan(idx, E, world)
     assert counts.tolist() == [3, 2, 1, 2]
     assert send.tolist() == [0, 2, 3, 0, 2, 2, 1, 2]
+
+
+def test_prefill_exchange_default_by_world_size():
+    """The row exchange below 8 ranks, the partial-sum exchange from 8 on (the
+    measured faster one at each size); a communicator exists either way."""
+    from paris_moe_b200.ep import EPGroup
+    for world, want in ((2, "rows"), (4, "rows"), (8, "partial")):
+        g = EPGroup.emulated(256, 2048, 8, 0, world)
+        assert g.prefill == want
+        assert g.comm_handle != 0
+        g.close()
