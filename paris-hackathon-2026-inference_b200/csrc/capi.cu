@@ -252,16 +252,20 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   // The block reads xin; a decoder layer normalises x first and adds it back
   // in the combine (in place, y == x, is allowed: each combine thread reads
   // its residual chunk before writing the same chunk).
+  // Prefill-sized batches route on the tensor cores.
+  const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
   const __nv_bfloat16* xin = bf(x);
   const __nv_bfloat16* resid = nullptr;
+  // The decode routing kernel normalises x itself (writing xn, bit-identical
+  // to the standalone RMSNorm kernel); other paths run that kernel first.
+  const bool norm_in_route = layer && !rs && !route_tc && route_fuses_norm(d);
   if (layer) {
-    if (launch_rmsnorm(bf(x), bf(layer->w_norm), layer->eps, T, H, ws.xn, st) != cudaSuccess)
+    if (!norm_in_route &&
+        launch_rmsnorm(bf(x), bf(layer->w_norm), layer->eps, T, H, ws.xn, st) != cudaSuccess)
       return PMOE_ERR_CUDA;
     xin = ws.xn;
     resid = bf(x);
   }
-  // Prefill-sized batches route on the tensor cores.
-  const bool route_tc = use_tc && T > kFusedRouteMaxT && route_tc_supported(d);
   const cudaError_t rerr =
       rs && rs->topk_idx
           ? launch_dispatch_given(d, rs->topk_idx, rs->topk_w, rs->shared_gate, expert_lo,
@@ -270,8 +274,11 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                              with_shared, with_routed, ws, st)
       : route_tc ? launch_route_tc(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
                                    with_shared, with_routed, ws, st)
-                 : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi,
-                                with_shared, with_routed, ws, st, epoch_bump);
+      : norm_in_route
+          ? launch_route(d, bf(x), bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi, with_shared,
+                         with_routed, ws, st, epoch_bump, bf(layer->w_norm), layer->eps, ws.xn)
+          : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi, with_shared,
+                         with_routed, ws, st, epoch_bump);
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down

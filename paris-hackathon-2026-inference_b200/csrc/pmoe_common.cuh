@@ -218,6 +218,63 @@ __device__ __forceinline__ void mma_k32(float (&d)[4], const uint4& wa, const ui
 // overflows to +inf and the quotient is 0, the limit).
 __device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
+// Qwen3_5MoeRMSNorm (modeling_qwen3_5_moe.py:795-812) in pieces, for kernels
+// that normalise rows as they load them.  rms_row_scale is rsqrt(mean(x^2) +
+// eps) of one row computed by one warp in exactly the order of
+// rmsnorm_kernel's 256 threads: thread i (warp v = i / 32) sums its 16-byte
+// pieces i, i + 256, ... with fmaf, each warp's sum is lane 0's result of the
+// xor-shuffle tree, and the eight warp sums are added in order -- so the
+// value, and every output below, equals the standalone kernel's bit for bit.
+// H % 8 == 0.
+__device__ __forceinline__ float rms_row_scale(const __nv_bfloat16* __restrict__ row, int H,
+                                               float eps) {
+  const int lane = threadIdx.x & 31, n8 = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(row);
+  // the first piece of each of the eight warps, all loads in flight at once
+  // (a missing piece adds fmaf(0, 0, s) = s: exact)
+  uint4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = k * 32 + lane;
+    v[k] = i < n8 ? __ldg(xr + i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float ss = 0.f;
+    uint4 p = v[k];
+    for (int i = k * 32 + lane;; i += 256) {
+      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b[j]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+      if (i + 256 >= n8) break;  // rows longer than 2048: the thread's next piece
+      p = __ldg(xr + i + 256);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    tot += __shfl_sync(0xffffffffu, ss, 0);
+  }
+  return rsqrtf(tot / float(H) + eps);
+}
+// bf16(x * r * (1 + w)) of eight elements (the standalone kernel's expression).
+__device__ __forceinline__ uint4 rms_apply8(const uint4& xv, const uint4& wv, float r) {
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&xv);
+  const __nv_bfloat162* c = reinterpret_cast<const __nv_bfloat162*>(&wv);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(b[j]), g = __bfloat1622float2(c[j]);
+    __nv_bfloat162 r2 = __floats2bfloat162_rn(f.x * r * (1.f + g.x), f.y * r * (1.f + g.y));
+    op[j] = *reinterpret_cast<uint32_t*>(&r2);
+  }
+  return o;
+}
+
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }

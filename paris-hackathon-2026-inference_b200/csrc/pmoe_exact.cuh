@@ -34,6 +34,9 @@
 //     a row outside it is counted in a statistics word.  (FP64 is avoided:
 //     on this part double-precision throughput is a small fraction of the
 //     integer rate.)
+// The token rows are read through L2 (ld.global.cg), not the read-only
+// path: the decode routing kernel evaluates rows of the RMSNorm output that
+// other CTAs of the same launch wrote.
 #pragma once
 #include "pmoe_common.cuh"
 
@@ -216,7 +219,7 @@ static __device__ __noinline__ void exact_sums_general(const __nv_bfloat16* __re
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int i = lane * 8; i < n; i += 256) {
-    uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + i));
+    uint4 xv = __ldcg(reinterpret_cast<const uint4*>(x + i));
     uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + i));
 #pragma unroll 1
     for (int j = 0; j < 4; ++j) {
@@ -257,7 +260,7 @@ static __device__ __noinline__ float warp_exact_dot(const __nv_bfloat16* __restr
 #pragma unroll
     for (int i = 0; i < kChunk; ++i) {
       const int o = c0 + (i * 32 + lane) * 8;
-      xv[i] = o < n ? __ldg(reinterpret_cast<const uint4*>(x + o)) : make_uint4(0u, 0u, 0u, 0u);
+      xv[i] = o < n ? __ldcg(reinterpret_cast<const uint4*>(x + o)) : make_uint4(0u, 0u, 0u, 0u);
       wv[i] = o < n ? __ldg(reinterpret_cast<const uint4*>(w + o)) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
@@ -883,7 +886,7 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
         xv[j] = wv[j] = make_uint2(0u, 0u);
         if (live) {
           const auto& q = sm.req[r];
-          xv[j] = __ldg(reinterpret_cast<const uint2*>(x + size_t(q.t) * H + warp * chunk) + lane);
+          xv[j] = __ldcg(reinterpret_cast<const uint2*>(x + size_t(q.t) * H + warp * chunk) + lane);
           wv[j] = __ldg(reinterpret_cast<const uint2*>(w_router + size_t(q.e) * H + warp * chunk) +
                         lane);
         }
@@ -895,7 +898,7 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
         auto& q = sm.req[r];
         uint32_t xmx = 0u, xmn = 0x7FFF7FFFu, wmx = 0u, wmn = 0x7FFF7FFFu;
         for (int u = lane; u < chunk / 4; u += 32) {
-          const uint2 xa = u == lane ? xv[j] : __ldg(reinterpret_cast<const uint2*>(
+          const uint2 xa = u == lane ? xv[j] : __ldcg(reinterpret_cast<const uint2*>(
                                                    x + size_t(q.t) * H + warp * chunk) + u);
           const uint2 wa = u == lane ? wv[j] : __ldg(reinterpret_cast<const uint2*>(
                                                    w_router + size_t(q.e) * H + warp * chunk) + u);
@@ -940,7 +943,7 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
           const int eb = kmin + 141, W = 62 - 16 - lg;
           long long acc[2][3] = {{0ll, 0ll, 0ll}, {0ll, 0ll, 0ll}};
           for (int u = lane; u < chunk / 4; u += 32) {
-            const uint2 xv = __ldg(xr + u), wv = __ldg(wr + u);
+            const uint2 xv = __ldcg(xr + u), wv = __ldg(wr + u);
             exact_word_fast(xv.x, wv.x, eb, W, acc);
             exact_word_fast(xv.y, wv.y, eb, W, acc);
           }
@@ -952,7 +955,7 @@ __device__ __forceinline__ void cta_topk_finish(ExactCta<NW, MAXPEND>& sm,
           if (kmax + 2 - kb > room) kb = kmax + 2 - room;
           U128 pos{0ull, 0ull}, neg{0ull, 0ull};
           for (int u = lane; u < chunk / 4; u += 32) {
-            const uint2 xv = __ldg(xr + u), wv = __ldg(wr + u);
+            const uint2 xv = __ldcg(xr + u), wv = __ldg(wr + u);
             exact_add_general(xv.x & 0xFFFFu, wv.x & 0xFFFFu, kb, pos, neg);
             exact_add_general(xv.x >> 16, wv.x >> 16, kb, pos, neg);
             exact_add_general(xv.y & 0xFFFFu, wv.y & 0xFFFFu, kb, pos, neg);

@@ -13,7 +13,12 @@ cudaError_t stream_init(int num_sms);
 cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                          const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                          int with_routed, const Workspace& ws, cudaStream_t st,
-                         int* epoch_bump = nullptr);
+                         int* epoch_bump = nullptr, const __nv_bfloat16* w_norm = nullptr,
+                         float eps = 0.f, __nv_bfloat16* xn = nullptr);
+// The decode routing kernel can fuse a decoder layer's RMSNorm (w_norm, eps:
+// x is normalised as it is read and written to xn, bit-identical to
+// launch_rmsnorm) when this holds for d.
+bool route_fuses_norm(const Dims& d);
 bool route_bumps_epoch(const Dims& d);
 // Accumulation-bound factor gamma of the exact top-k for the routing path
 // that launch_route / launch_route_tc take for d (pmoe_exact.cuh).

@@ -42,7 +42,10 @@ __device__ __forceinline__ void router_tile(const __nv_bfloat16* __restrict__ x,
                                            const __nv_bfloat16* __restrict__ w_router,
                                            const __nv_bfloat16* __restrict__ w_gvec, int T,
                                            int H, int E, int rg, int tt, int k_begin, int k_len,
-                                           float (&acc)[4][4], float (&wss)[2], float (&xss)[4]) {
+                                           float (&acc)[4][4], float (&wss)[2], float (&xss)[4],
+                                           const __nv_bfloat16* __restrict__ w_norm = nullptr,
+                                           const float* s_rs = nullptr,
+                                           __nv_bfloat16* __restrict__ xn_out = nullptr) {
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int r0 = rg * 16 + g, r1 = r0 + 8;
   auto row_ptr = [&](int r) -> const __nv_bfloat16* {
@@ -73,10 +76,17 @@ __device__ __forceinline__ void router_tile(const __nv_bfloat16* __restrict__ x,
     const uint4 wb = wb_p ? ldg_stream(wb_p + kk) : zero;
     wss[0] += sumsq8(wa);
     wss[1] += sumsq8(wb);
+    // decoder layer: x is normalised on the way in (s_rs: the group's row
+    // scales), and xn_out, when given, receives the normalised rows
+    const uint4 wn = w_norm ? ldg_keep(w_norm + kk) : zero;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       if (tt * 32 + q * 8 < T) {  // warp-uniform
-        const uint4 xv = xp[q] ? ldg_keep(xp[q] + kk) : zero;
+        uint4 xv = xp[q] ? ldg_keep(xp[q] + kk) : zero;
+        if (w_norm && xp[q]) {
+          xv = rms_apply8(xv, wn, s_rs[q * 8 + g]);
+          if (xn_out) *reinterpret_cast<uint4*>(xn_out + (xp[q] - x) + kk) = xv;
+        }
         mma_k32(acc[q], wa, wb, xv);
         xss[q] += sumsq8(xv);
       }
@@ -272,8 +282,10 @@ __global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
     int lo, int hi, int with_shared, int with_routed, float* __restrict__ logit_part,
     float* __restrict__ xn_part, float* __restrict__ wn_part, float* __restrict__ diag,
     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, float* __restrict__ shared_gate,
-    DispatchOut o, int32_t* __restrict__ sync, int* __restrict__ epoch_bump) {
+    DispatchOut o, int32_t* __restrict__ sync, int* __restrict__ epoch_bump,
+    const __nv_bfloat16* __restrict__ w_norm, float eps, __nv_bfloat16* __restrict__ xn) {
   __shared__ float s_part[kFusedRouteWarps][32][17];
+  __shared__ float s_rs[32];
   __shared__ float s_wss[kFusedRouteWarps][16], s_xss[kFusedRouteWarps][32];
   __shared__ float s_wn[256], s_xn[32];
   __shared__ int s_cnt[256], s_off[256], s_cur[256], s_wsum[32], s_tot[2], s_last;
@@ -293,9 +305,25 @@ __global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
   const int Hk = H / KS, kb = kg * Hk;
   const int slice = (Hk / kFusedRouteWarps + 31) / 32 * 32;
   const int k_off = min(Hk, warp * slice);
+  // Decoder layer (w_norm given): the RMSNorm of the group's tokens is fused
+  // here -- every CTA computes the row scales (the standalone kernel's
+  // arithmetic), normalises its x tiles as it loads them, and the CTAs of
+  // router row group 0 write their k range of xn for the expert kernels and
+  // for the exact evaluations below (which read it through L2 after the
+  // group's counter); the exact top-k then works on xn.
+  if (w_norm) {
+    for (int tl = warp; tl < 32; tl += kFusedRouteWarps) {
+      const int t = tt * 32 + tl;
+      const float r = t < T ? rms_row_scale(x + size_t(t) * H, H, eps) : 0.f;
+      if (lane == 0) s_rs[tl] = r;
+    }
+    __syncthreads();
+  }
   float acc[4][4], wss[2], xss[4];
   router_tile(x, w_router, w_gvec, T, H, E, rg, tt, kb + k_off, min(slice, Hk - k_off), acc, wss,
-              xss);
+              xss, w_norm, s_rs, (w_norm && rg == 0) ? xn : nullptr);
+  // from here on the token rows are the normalised ones
+  const __nv_bfloat16* xr = w_norm ? xn : x;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     s_part[warp][q * 8 + 2 * c][g] = acc[q][0];
@@ -418,14 +446,14 @@ __global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
     const float* r0 = s_lg + size_t(tl0) * Rpad;
     const float* r1 = s_lg + size_t(v1 ? tl1 : tl0) * Rpad;
     warp_topk_stage2(xq, [&](int i, int e) { return (i ? r1 : r0)[e]; }, s_wn, s_xn[tl0],
-                     s_xn[v1 ? tl1 : tl0], gamma, t0 + tl0, t0 + tl1, v1, E, K, x, w_router, H,
+                     s_xn[v1 ? tl1 : tl0], gamma, t0 + tl0, t0 + tl1, v1, E, K, xr, w_router, H,
                      stats, topk_idx, topk_w, [&](int) { return s_cnt; });
     if (lane == 0) {
       shared_gate[t0 + tl0] = 1.0f / (1.0f + expf(-r0[E]));
       if (v1) shared_gate[t0 + tl1] = 1.0f / (1.0f + expf(-r1[E]));
     }
   }
-  cta_topk_finish(xq, x, w_router, H, K, stats, topk_idx, topk_w, [&](int) { return s_cnt; });
+  cta_topk_finish(xq, xr, w_router, H, K, stats, topk_idx, topk_w, [&](int) { return s_cnt; });
   __threadfence();
   __syncthreads();
   // Level 2: the last group to finish builds the dispatch for all tokens.
@@ -531,7 +559,8 @@ size_t dispatch_smem_bytes(int E) {
 cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloat16* w_router,
                          const __nv_bfloat16* w_gvec, int lo, int hi, int with_shared,
                          int with_routed, const Workspace& ws, cudaStream_t st,
-                         int* epoch_bump) {
+                         int* epoch_bump, const __nv_bfloat16* w_norm, float eps,
+                         __nv_bfloat16* xn) {
   DispatchOut o{ws.offsets, ws.active, ws.n_active, ws.sorted_tok, ws.sorted_slot, ws.pair_dst,
                 ws.pair_w, d.sh_lo, d.sh_hi};
   const int RG = d.Rpad / 16, TT = (d.T + 31) / 32;
@@ -542,7 +571,7 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
                          fused_route_smem_bytes(d.T, d.E, d.K, d.Rpad), st>>>(
         x, w_router, w_gvec, d.T, d.H, d.E, d.K, d.Rpad, d.KS, lo, hi, with_shared,
         with_routed, ws.logit_part, ws.xnorm, ws.wnorm, ws.diag, ws.topk_idx, ws.topk_w,
-        ws.shared_gate, o, ws.status, epoch_bump);
+        ws.shared_gate, o, ws.status, epoch_bump, w_norm, eps, xn);
     return cudaGetLastError();
   }
   const long items = long(RG) * TT;
@@ -563,6 +592,7 @@ cudaError_t launch_route(const Dims& d, const __nv_bfloat16* x, const __nv_bfloa
 }
 
 bool route_bumps_epoch(const Dims& d) { return d.T <= kFusedRouteMaxT; }
+bool route_fuses_norm(const Dims& d) { return d.T <= kFusedRouteMaxT && d.H % 8 == 0; }
 
 float route_gamma(const Dims& d) {
   if (d.T <= kFusedRouteMaxT) {

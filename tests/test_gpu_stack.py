@@ -76,6 +76,24 @@ def test_layer_matches_oracle(three_layers, T):
     assert_close(y, _layer_ref(h, gn[0], gb[0], blocks[0]), f"layer T={T}")
 
 
+@pytest.mark.parametrize("T", [1, 17, 64, 200])
+def test_layer_fused_norm_equals_composition(three_layers, T):
+    """At decode sizes the layer's routing kernel normalises x as it reads it
+    (and writes xn for the expert kernels) instead of running the RMSNorm
+    kernel first; the layer must still equal, bit for bit, the standalone
+    RMSNorm, then the block on its output, then bf16(x + bf16(block)).
+    T = 200 (tensor-core path, separate RMSNorm kernel) checks the same
+    composition."""
+    from paris_moe_b200 import ops, workload as W
+    norms, blocks, gn, gb = three_layers
+    h = W.make_hidden(T, W.MoEShape(), seed=T + 1).cuda()
+    y = ops.moe_layer(h, gn[1], EPS, *gb[1].tensors(), gb[1].shape.K, 3)
+    xn = ops.rmsnorm(h, gn[1], EPS)
+    blk = ops.moe_block(xn, *gb[1].tensors(), gb[1].shape.K, 0, -1, 3)
+    ref = (h.float() + blk.float()).to(torch.bfloat16)
+    assert torch.equal(y, ref)
+
+
 def test_stack_equals_layers_and_graph(three_layers):
     from paris_moe_b200 import ops, stack, workload as W
     norms, blocks, gn, gb = three_layers
