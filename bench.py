@@ -17,7 +17,11 @@ from HBM; no L2 flush is needed) and hidden states are synthetic N(0,1).
 * ``value``: tokens/s with inputs resident in HBM, device-timed with CUDA
   events over exactly K steps between barriers; for N>1 the max over ranks.
 * ``e2e``: the same metric through the public op with pinned host buffers:
-  every step copies x host->device and y device->host inside the timed region.
+  every step copies x host->device and y device->host inside the timed region,
+  pipelined as a serving loop would (the next step's upload and the previous
+  step's download on their own streams while a step computes).
+* ``host_ms_per_step``: host time to enqueue a step (launch-bound if near
+  ``ms_per_step``).
 * ``roofline``: the dominant kernel (decode: the gate_up + SiLU*mul weight
   stream, HBM-bound; prefill: the gate_up grouped GEMM, tensor-bound),
   algorithmic bytes or FLOPs per launch / its event-timed average duration,
@@ -33,7 +37,8 @@ ranges by rank (engine/runtime/ep.py:78-86), the weighted expert rows cross
 NVLink from the down-projection epilogue (no collective kernel).  Prefill:
 every rank routes all tokens, computes a cost-balanced run of the dispatched
 rows, and its down GEMM stores each row at the rank owning the row's token
-over NVLink; each rank combines its token slice and pushes it to every rank.
+over NVLink; each rank combines its token slice and pushes it to every rank
+(from 8 ranks on: per-rank partials summed over NVLink, pmoe_rows_allreduce).
 ``comparators`` (decode and prefill) times the same call with the
 reference's NCCL all_reduce exchange and with a token-dispatch
 all_to_all_single exchange.
@@ -343,36 +348,66 @@ class Runner:
         return [v / n for v in acc]
 
     def e2e(self, steps):
-        """Public op with pinned host buffers, copies inside the timed region."""
+        """The public op end to end: every step copies its input from pinned host
+        memory to the GPU, runs the op and copies the result back to pinned host
+        memory, all inside the timed region.  The steps are pipelined the way a
+        serving loop runs them: three slots, the upload of step i+1 and the
+        download of step i-1 on their own streams (the two copy engines) while
+        step i computes, ordered by events."""
         import torch
         c = self.ctx
-        x_host = self.x.cpu().pin_memory()
-        y_host = torch.empty((self.T, c.S.H), dtype=torch.bfloat16).pin_memory()
-        xd = torch.empty_like(self.x)
+        nslot = 3
+        x_host = [self.x.cpu().pin_memory() for _ in range(nslot)]
+        y_host = [torch.empty((self.T, c.S.H), dtype=torch.bfloat16).pin_memory()
+                  for _ in range(nslot)]
+        xd = [torch.empty_like(self.x) for _ in range(nslot)]
+        # three non-default streams (the legacy default stream would serialise them)
+        s_up, s_comp, s_down = (torch.cuda.Stream(c.dev) for _ in range(3))
+        up_done = [torch.cuda.Event() for _ in range(nslot)]
+        comp_done = [torch.cuda.Event() for _ in range(nslot)]
+        down_done = [torch.cuda.Event() for _ in range(nslot)]
+        # each slot keeps its step's output alive until the slot's next step
+        # (Tensor.record_stream instead cost ~0.3 ms of host time per step)
+        keep = [None] * nslot
         from paris_moe_b200 import ops
 
-        def one():
-            xd.copy_(x_host, non_blocking=True)
-            if c.world > 1:
-                out = c.group.forward(xd, self.tensors)
-            else:
-                out = ops.moe_block(xd, *self.tensors, c.S.K, 0, c.S.E, 3)
-            y_host.copy_(out, non_blocking=True)
+        def one(i):
+            k = i % nslot
+            with torch.cuda.stream(s_up):       # slot k's input is free once step i-3 computed
+                if i >= nslot:
+                    s_up.wait_event(comp_done[k])
+                xd[k].copy_(x_host[k], non_blocking=True)
+                up_done[k].record(s_up)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(up_done[k])
+                if i >= nslot:                  # step i-3's output has left the GPU, so
+                    s_comp.wait_event(down_done[k])  # its memory, freed below, is reusable
+                if c.world > 1:
+                    out = c.group.forward(xd[k], self.tensors)
+                else:
+                    out = ops.moe_block(xd[k], *self.tensors, c.S.K, 0, c.S.E, 3)
+                comp_done[k].record(s_comp)
+            with torch.cuda.stream(s_down):
+                s_down.wait_event(comp_done[k])
+                y_host[k].copy_(out, non_blocking=True)
+                down_done[k].record(s_down)
+            keep[k] = out
 
-        for _ in range(3):
-            one()
+        for i in range(3):
+            one(i)
         torch.cuda.synchronize()
         c.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(c.st)
-        for _ in range(steps):
-            one()
-        e1.record(c.st)
+        e0.record(s_up)
+        for i in range(steps):
+            one(i)
+        e1.record(s_down)
         torch.cuda.synchronize()
         ms = c.max_over_ranks(e0.elapsed_time(e1)) / steps
         return {"value": self.T / (ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": self.T * c.S.H * 2,
-                "d2h_bytes_per_step": self.T * c.S.H * 2, "ms_per_step": ms}
+                "d2h_bytes_per_step": self.T * c.S.H * 2, "ms_per_step": ms,
+                "pipeline": "3 slots; upload, op and download on separate streams"}
 
 
 class Ctx:
