@@ -137,6 +137,15 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before its predecessor finishes; pdl_wait() blocks
+// until the predecessor grids have completed and their memory is visible
+// (a no-op without the attribute), pdl_trigger() lets this kernel's
+// dependents launch (their CTAs take SMs as this grid's CTAs retire).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -15,6 +15,7 @@
 //  * larger T: router GEMM tiles -> warp-per-token top-k -> one-CTA dispatch.
 #include "pmoe_common.cuh"
 #include "pmoe_kernels.cuh"
+#include "pmoe_tma.cuh"
 #include "pmoe_exact.cuh"
 
 namespace pmoe {
@@ -297,6 +298,7 @@ __global__ void __launch_bounds__(kFusedRouteThreads, 1) route_fused_kernel(
   int* s_wcnt = reinterpret_cast<int*>(s_sg + T);             // [warps][E]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const int RG = Rpad / 16, TT = (T + 31) / 32;
+  pdl_trigger();  // the gate_up kernel's CTAs may start their set-up as SMs free up
   if (epoch_bump && blockIdx.x == 0 && threadIdx.x == 0) *epoch_bump += 1;
   const int kg = blockIdx.x % KS, rest = blockIdx.x / KS;
   const int rg = rest % RG, tt = rest / RG;

@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
   __shared__ int s_tok[kActRows];
   __shared__ UnitRing ur;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) gate_up_tma_kernel(
     mbar_fence_init();
   }
   __syncthreads();
+  pdl_wait();  // the routing tables
   const int UJ = (I > Is ? I : Is) / kUnitRows;
   const int n_units = tb.n_active[0] * UJ;
   const int nkc = H / (kKC * KCH);
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
     const __grid_constant__ CUtensorMap tm_h, ExpertTables tb, int H, int E, int I, int Is,
     float* __restrict__ rows, int* __restrict__ status, int* __restrict__ queue, EpPeers ep,
     int row_blocks) {
-  const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDtStages * kDtStageBytes);
@@ -587,6 +589,8 @@ __global__ void __launch_bounds__(kDtThreads, 1) down_tc_kernel(
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // h and the routing tables of the kernels before
+  const int epoch = ep.world > 0 ? ep_epoch(ep) : 0;
   const uint32_t tmem_base = *tmem_slot;
   const int UR = H / (kDtRows * row_blocks);
   const int n_units = tb.n_active[0] * UR;
@@ -797,6 +801,7 @@ __global__ void __launch_bounds__(256) combine_kernel(
     const int* __restrict__ wait_flags, int world, const int* __restrict__ epoch_dev,
     int epoch_host, int* __restrict__ status, int* __restrict__ sticky,
     const __nv_bfloat16* __restrict__ resid, __nv_bfloat16* __restrict__ y) {
+  pdl_wait();  // the expert rows
   const int epoch = epoch_dev ? *epoch_dev : epoch_host;
   if (world > 0) rows += size_t(epoch & 1) * par_stride;
   if (world > 0) {
@@ -881,6 +886,28 @@ __global__ void __launch_bounds__(256) combine_kernel(
 }
 
 namespace {
+// Programmatic dependent launch of the decode chain (PMOE_PDL=0: plain launches).
+const bool g_pdl = [] {
+  const char* v = std::getenv("PMOE_PDL");
+  return !(v && std::atoi(v) == 0);
+}();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dep(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int g_num_sms = 148;
 int g_kch_gu = 4;  // k-chunks per gate_up stage (512 B per weight row)
 int g_dn_row_blocks = kDnRowBlocks;
@@ -957,13 +984,14 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
     return cudaErrorInvalidValue;
   ExpertTables tb{ws.active, ws.n_active, ws.offsets, ws.sorted_tok, ws.pair_dst, ws.pair_w};
   int* status = ws.status + 1;
-#define PMOE_GU(KCH)                                                                  \
-  gate_up_tma_kernel<KCH><<<g_num_sms, kStreamThreads, GuCfg<KCH>::kSmem, st>>>(      \
-      tm_gu, tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
+#define PMOE_GU(KCH)                                                                        \
+  launch_dep(gate_up_tma_kernel<KCH>, g_num_sms, kStreamThreads, GuCfg<KCH>::kSmem, st, tm_gu, \
+             tm_sg, tm_su, tm_x, tb, d.H, d.E, d.I, d.Is, d.ldh, ws.h, status, ws.status + 2)
 #define PMOE_DN(KCH)                                                                  \
   down_tma_kernel<KCH><<<g_num_sms, kDnThreads, DnCfg<KCH>::kSmem, st>>>(             \
       tm_dn, tm_sd, tm_h, tm_h8, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep, rbk)
-  if (kg == 4) PMOE_GU(4); else if (kg == 2) PMOE_GU(2); else PMOE_GU(1);
+  const cudaError_t eg = kg == 4 ? PMOE_GU(4) : kg == 2 ? PMOE_GU(2) : PMOE_GU(1);
+  if (eg != cudaSuccess) return eg;
   if (mid_event) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(mid_event), st);
     if (e != cudaSuccess) return e;
@@ -978,9 +1006,10 @@ cudaError_t launch_stream_experts(const Dims& d, const __nv_bfloat16* x,
       return cudaErrorInvalidValue;
     int rbt = 4;  // 128-row blocks per unit, dividing H / 128
     while (rbt > 1 && (d.H / kDtRows) % rbt != 0) rbt >>= 1;
-    down_tc_kernel<<<g_num_sms, kDtThreads, kDtSmem, st>>>(
-        tm_dn128, tm_sd128, tm_h16, tb, d.H, d.E, d.I, d.Is, rows, status, ws.status + 3, ep,
-        rbt);
+    const cudaError_t e = launch_dep(down_tc_kernel, g_num_sms, kDtThreads, kDtSmem, st, tm_dn128,
+                                     tm_sd128, tm_h16, tb, d.H, d.E, d.I, d.Is, rows, status,
+                                     ws.status + 3, ep, rbt);
+    if (e != cudaSuccess) return e;
   } else {
     if (kd == 8) PMOE_DN(8); else if (kd == 4) PMOE_DN(4); else if (kd == 2) PMOE_DN(2);
     else PMOE_DN(1);
@@ -997,10 +1026,11 @@ cudaError_t launch_combine(const Dims& d, const Workspace& ws, int lo, int hi, i
   if (n == 0) return cudaSuccess;
   const float* rows = ep.world > 0 ? ep.rows[ep.rank] : ws.rows;
   const int* flags = ep.world > 0 ? ep.flags[ep.rank] : nullptr;
-  combine_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(
-      rows, ep.par_stride, ws.topk_idx, d.T, d.H, d.K, lo, hi, with_shared, with_routed, d.sh_lo,
-      d.sh_hi, flags, ep.world, ep.epoch_dev, ep.epoch, ws.status + 1, ep.sticky, resid, y);
-  return cudaGetLastError();
+  return launch_dep(combine_kernel, unsigned((n + 255) / 256), 256u, size_t(0), st, rows,
+                    ep.par_stride, static_cast<const int32_t*>(ws.topk_idx), d.T, d.H, d.K, lo,
+                    hi, with_shared, with_routed, d.sh_lo, d.sh_hi, flags, ep.world,
+                    static_cast<const int*>(ep.epoch_dev), ep.epoch, ws.status + 1, ep.sticky,
+                    resid, y);
 }
 
 // One thread: the device epoch counter of an exchange buffer, bumped at the
