@@ -460,12 +460,15 @@ def comparators(c, x, tensors, T, steps, warmup):
     if T > ep.FUSED_MAX_T:
         # the prefill exchange EPGroup does not default to at this world size
         runs.append(("fused", "nvlink_partial_sum" if c.world < 8 else "nvlink_rows_to_owner"))
+        runs.append(("fused", "nvlink_rows_route_slices"))  # routing by token slice
     for mode, label in runs:
         g = ep.EPGroup(c.S.E, c.S.H, c.S.K, mode=mode)
         if label == "nvlink_partial_sum":
             g.prefill = "partial"
         elif label == "nvlink_rows_to_owner":
             g.prefill = "rows"
+        elif label == "nvlink_rows_route_slices":
+            g.prefill = "slice"
         y = torch.empty_like(x)
         for _ in range(warmup):
             g.forward(x, tensors, out=y)

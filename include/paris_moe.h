@@ -47,7 +47,11 @@ enum {
   PMOE_F_SHARED = 1,        /* add sigmoid(x.w_sh_gvec) * shared_expert(x) */
   PMOE_F_ROUTED = 2,        /* add the routed experts in [expert_lo, expert_hi) */
   PMOE_F_FORCE_STREAM = 4,  /* weight-streaming kernels at any T (testing) */
-  PMOE_F_FORCE_TC = 8       /* tcgen05 grouped GEMMs at any T (testing) */
+  PMOE_F_FORCE_TC = 8,      /* tcgen05 grouped GEMMs at any T (testing) */
+  PMOE_F_ROUTE_SLICE = 16   /* pmoe_block_forward_rows_fused only: each rank routes its
+                               token slice [r*T/N, (r+1)*T/N) and the routing slices are
+                               exchanged over NVLink (peer stores) instead of every rank
+                               routing all T tokens; same output bits */
 };
 
 /* Human-readable name of a status code. */
@@ -261,6 +265,10 @@ int pmoe_rows_status_async(const void* own_buf, int* dst, void* stream);
  * events: as pmoe_block_forward_profiled ([4] after the gather; may be NULL).
  * Waits are bounded (status 4 via pmoe_rows_status). */
 int pmoe_rows_fused_buffer_bytes(int T_max, int H, int K, size_t* bytes);
+/* (flags may add PMOE_F_ROUTE_SLICE: routing by token slice, the token-dispatch
+ * form of the exchange -- the routing of engine/runtime/ep.py's replicated
+ * tokens is split by token owner, and only the routing crosses NVLink, since
+ * every rank holds the tokens themselves.) */
 int pmoe_block_forward_rows_fused(
     const uint16_t* x, int T, int H, int E, int K, int I, int Is, const uint16_t* w_router,
     const uint16_t* w_gate_up, const uint16_t* w_down, const uint16_t* w_sh_gate,

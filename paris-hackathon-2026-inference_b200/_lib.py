@@ -83,6 +83,7 @@ PMOE_F_SHARED = 1
 PMOE_F_ROUTED = 2
 PMOE_F_FORCE_STREAM = 4
 PMOE_F_FORCE_TC = 8
+PMOE_F_ROUTE_SLICE = 16
 
 _lock = threading.Lock()
 _lib = None

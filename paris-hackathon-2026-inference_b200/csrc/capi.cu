@@ -177,6 +177,9 @@ struct RowSplit {
   // owner's buffer and the call ends with the full y on every rank.
   void* const* bufs = nullptr;
   int T_max = 0, epoch = 0;
+  // With bufs: route only this rank's token slice and exchange the routing
+  // (PMOE_F_ROUTE_SLICE) instead of routing every token on every rank.
+  bool route_slice = false;
 };
 
 // Shared implementation of the forward entry points.  `ep` (world > 0)
@@ -196,8 +199,10 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
   if (s != PMOE_OK) return s;
   if (expert_lo < 0 || expert_hi > E || expert_lo > expert_hi) return PMOE_ERR_ARG;
   if (sh_lo < 0 || sh_hi > T || sh_lo > sh_hi) return PMOE_ERR_ARG;
-  if (flags & ~(PMOE_F_SHARED | PMOE_F_ROUTED | PMOE_F_FORCE_STREAM | PMOE_F_FORCE_TC))
+  if (flags & ~(PMOE_F_SHARED | PMOE_F_ROUTED | PMOE_F_FORCE_STREAM | PMOE_F_FORCE_TC |
+                PMOE_F_ROUTE_SLICE))
     return PMOE_ERR_ARG;
+  if ((flags & PMOE_F_ROUTE_SLICE) && !(rs && rs->bufs)) return PMOE_ERR_ARG;
   if (T == 0) return PMOE_OK;
   const void* ptrs[] = {x, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up, w_sh_down, w_sh_gvec,
                         y, workspace};
@@ -266,7 +271,34 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
     xin = ws.xn;
     resid = bf(x);
   }
-  const cudaError_t rerr =
+  cudaError_t rerr = cudaSuccess;
+  if (rs && rs->bufs && rs->route_slice) {
+    // This rank's token slice on the tensor-core router (the exact top-k
+    // makes each token's routing independent of the batch it is routed in),
+    // the slices exchanged by peer stores, then the dispatch of all T tokens.
+    const int t0 = int(long(rs->rank) * T / rs->world);
+    const int t1 = int(long(rs->rank + 1) * T / rs->world);
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int32_t* ai = nullptr;
+    const float *aw = nullptr, *asg = nullptr;
+    rerr = cudaMemsetAsync(ws.status, 0, kStatusWords * sizeof(int32_t), st);
+    if (rerr == cudaSuccess && t1 > t0)
+      rerr = launch_router_tc(make_dims(t1 - t0, H, E, K, I, Is), xin + size_t(t0) * H,
+                              bf(w_router), bf(w_sh_gvec), ws.topk_idx + size_t(t0) * K,
+                              ws.topk_w + size_t(t0) * K, ws.shared_gate + t0, ws.hist,
+                              ws.status, ws.logit_part, ws.xnorm, ws.wnorm, ws.route_queue,
+                              nullptr, st);
+    if (rerr == cudaSuccess)
+      rerr = launch_route_exchange(rs->bufs, rs->T_max, rs->world, rs->rank, rs->epoch, T, H, K,
+                                   ws.topk_idx, ws.topk_w, ws.shared_gate, sms, st, &ai, &aw,
+                                   &asg);
+    if (rerr == cudaSuccess)
+      rerr = launch_dispatch_given(d, ai, aw, asg, expert_lo, expert_hi, with_shared,
+                                   with_routed, ws, st);
+  } else {
+  rerr =
       rs && rs->topk_idx
           ? launch_dispatch_given(d, rs->topk_idx, rs->topk_w, rs->shared_gate, expert_lo,
                                   expert_hi, with_shared, with_routed, ws, st)
@@ -279,6 +311,7 @@ static int forward_impl(const uint16_t* x, int T, int H, int E, int K, int I, in
                          with_routed, ws, st, epoch_bump, bf(layer->w_norm), layer->eps, ws.xn)
           : launch_route(d, xin, bf(w_router), bf(w_sh_gvec), expert_lo, expert_hi, with_shared,
                          with_routed, ws, st, epoch_bump);
+  }
   if (rerr != cudaSuccess) return PMOE_ERR_CUDA;
   if (use_tc) {
     void* ev[3] = {nullptr, nullptr, nullptr};  // before gate_up, after gate_up, after down
@@ -516,6 +549,7 @@ int pmoe_block_forward_rows_fused(
   rs.bufs = bufs;
   rs.T_max = T_max;
   rs.epoch = epoch;
+  rs.route_slice = (flags & PMOE_F_ROUTE_SLICE) != 0;
   return forward_impl(x, T, H, E, K, I, Is, w_router, w_gate_up, w_down, w_sh_gate, w_sh_up,
                       w_sh_down, w_sh_gvec, 0, E, 0, T, flags, y, workspace, workspace_bytes,
                       stream, events, n_events, none, nullptr, &rs);

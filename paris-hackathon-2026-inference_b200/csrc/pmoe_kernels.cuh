@@ -91,6 +91,16 @@ cudaError_t launch_rows_allreduce(void* const* bufs, int T_max, int world, int r
 // combines its slice locally; then the gather (rows_exchange.cu).
 size_t rx_fused_buffer_bytes(int T_max, int H, int K);
 size_t rx_fused_rows_offset(int T_max, int H, int K, int epoch);
+size_t rx_fused_route_offset(int T_max, int H, int K, int epoch);
+// Routing slices of the fused row exchange: this rank's slice [r*T/N,
+// (r+1)*T/N) of topk_idx / topk_w / shared_gate goes to every rank's routing
+// region (peer stores), flags R are raised and awaited (bounded); *all_* then
+// point at the complete routing in this rank's own buffer.
+cudaError_t launch_route_exchange(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                  int T, int H, int K, const int32_t* topk_idx,
+                                  const float* topk_w, const float* shared_gate, int num_sms,
+                                  cudaStream_t st, const int32_t** all_idx, const float** all_w,
+                                  const float** all_sg);
 cudaError_t launch_rows_fused_tail(void* const* bufs, int T_max, int world, int rank, int epoch,
                                    int T, int H, int E, int K, const int32_t* topk_idx,
                                    const float* topk_w, const float* shared_gate,

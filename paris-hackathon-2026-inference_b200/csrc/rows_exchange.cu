@@ -5,6 +5,8 @@
 //   [0, 256)     flags A: flagsA[q] = epoch when rank q's partial is complete
 //   [256, 512)   flags B: flagsB[q] = epoch when rank q's token slice is reduced
 //   [512, 520)   ticket (CTA completion counter), status word
+//   [768, 800)   flags R: flagsR[q] = epoch when rank q's routing slice is
+//                delivered (fused exchange with routing slices)
 //   [1024, ...)  two parity regions of T_max x H bf16
 // Per call (epoch e > 0, parity e & 1), after this rank wrote its partial into
 // its own region:
@@ -27,7 +29,8 @@
 namespace pmoe {
 
 constexpr size_t kRxHeader = 1024;
-constexpr int kRxFlagsA = 0, kRxFlagsB = 256, kRxTicket = 512, kRxStatus = 516;
+constexpr int kRxFlagsA = 0, kRxFlagsB = 256, kRxTicket = 512, kRxStatus = 516, kRxFlagsR = 768;
+static_assert(kRxFlagsR + 4 * kMaxRanks <= 1024, "header");
 constexpr int kRxThreads = 256;
 
 struct RxPeers {
@@ -226,8 +229,75 @@ static size_t rx_rows_region(int T_max, int H, int K) {
   return (size_t(T_max) * (K + 1) * H * 2 + 255) / 256 * 256;
 }
 
+// Routing region (fused exchange with routing slices), per parity after the
+// rows regions: topk_idx [T_max][K] i32, topk_w [T_max][K] f32,
+// shared_gate [T_max] f32.
+static size_t rx_route_region(int T_max, int K) {
+  return (size_t(T_max) * (2 * K + 1) * 4 + 255) / 256 * 256;
+}
+
 size_t rx_fused_buffer_bytes(int T_max, int H, int K) {
-  return rx_buffer_bytes(T_max, H) + 2 * rx_rows_region(T_max, H, K);
+  return rx_buffer_bytes(T_max, H) + 2 * rx_rows_region(T_max, H, K) +
+         2 * rx_route_region(T_max, K);
+}
+
+size_t rx_fused_route_offset(int T_max, int H, int K, int epoch) {
+  return rx_buffer_bytes(T_max, H) + 2 * rx_rows_region(T_max, H, K) +
+         size_t(epoch & 1) * rx_route_region(T_max, K);
+}
+
+// This rank's routing slice [t0, t1) into the routing region (parity of the
+// epoch) of every rank, peer stores; made visible system-wide before the
+// flag that follows on the stream.
+__global__ void __launch_bounds__(kRxThreads) rx_route_push_kernel(
+    RxPeers p, size_t route_off, int T_max, int K, int t0, int t1,
+    const int32_t* __restrict__ idx, const float* __restrict__ w,
+    const float* __restrict__ sg) {
+  if (__ldcg(rx_flags(p, p.rank, kRxStatus)) != 0) return;
+  const long nk = long(t1 - t0) * K, n = nk + (t1 - t0);
+  for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += long(gridDim.x) * blockDim.x) {
+    const bool gate = i >= nk;           // the shared-expert gates follow the K-wide arrays
+    const long j = gate ? (i - nk) : i;  // element of the slice
+    for (int q = 0; q < p.world; ++q) {
+      char* r = p.base[q] + route_off;
+      if (gate) {
+        reinterpret_cast<float*>(r + size_t(T_max) * 2 * K * 4)[t0 + j] = sg[t0 + j];
+      } else {
+        const size_t o = size_t(t0) * K + j;
+        reinterpret_cast<int32_t*>(r)[o] = idx[o];
+        reinterpret_cast<float*>(r + size_t(T_max) * K * 4)[o] = w[o];
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+cudaError_t launch_route_exchange(void* const* bufs, int T_max, int world, int rank, int epoch,
+                                  int T, int H, int K, const int32_t* topk_idx,
+                                  const float* topk_w, const float* shared_gate, int num_sms,
+                                  cudaStream_t st, const int32_t** all_idx, const float** all_w,
+                                  const float** all_sg) {
+  RxPeers p{};
+  for (int q = 0; q < world; ++q) p.base[q] = static_cast<char*>(bufs[q]);
+  p.world = world;
+  p.rank = rank;
+  p.epoch = epoch;
+  p.region = (size_t(T_max) * H * 2 + 255) / 256 * 256;
+  const size_t off = rx_fused_route_offset(T_max, H, K, epoch);
+  const int t0 = int(long(rank) * T / world), t1 = int(long(rank + 1) * T / world);
+  const long n = long(t1 - t0) * (K + 1);
+  const unsigned blocks =
+      unsigned(std::max<long>(1, std::min<long>((n + kRxThreads - 1) / kRxThreads, num_sms)));
+  rx_route_push_kernel<<<blocks, kRxThreads, 0, st>>>(p, off, T_max, K, t0, t1, topk_idx,
+                                                      topk_w, shared_gate);
+  rx_publish_kernel<<<1, 1, 0, st>>>(p, kRxFlagsR);
+  rx_wait_kernel<<<1, 1, 0, st>>>(p, kRxFlagsR);
+  const char* own = static_cast<const char*>(bufs[rank]) + off;
+  *all_idx = reinterpret_cast<const int32_t*>(own);
+  *all_w = reinterpret_cast<const float*>(own + size_t(T_max) * K * 4);
+  *all_sg = reinterpret_cast<const float*>(own + size_t(T_max) * 2 * K * 4);
+  return cudaGetLastError();
 }
 
 size_t rx_fused_rows_offset(int T_max, int H, int K, int epoch) {

@@ -165,8 +165,10 @@ class EPGroup:
         _lib.check("pmoe_comm_create", self.lib.pmoe_comm_create(rank, world, ctypes.byref(c)))
         self.comm = c.value
         # prefill exchange: "rows" (the down GEMM stores rows at their token
-        # owner, pmoe_block_forward_rows_fused) or "partial" (per-rank partial
-        # outputs summed by pmoe_rows_allreduce).  Measured (tokens/s, T=8192
+        # owner, pmoe_block_forward_rows_fused), "slice" (the same with each
+        # rank routing only its token slice and the routing exchanged over
+        # NVLink: token-dispatch routing, PMOE_F_ROUTE_SLICE) or "partial"
+        # (per-rank partial outputs summed by pmoe_rows_allreduce).  Measured (tokens/s, T=8192
         # Zipf): 2 ranks rows 14.7M / partial 13.9M, 4 ranks 17.4M / 17.1M,
         # 8 ranks 5.9M / 18.6M -- back-to-back row-exchange calls stalled at 8
         # ranks (a synchronised call took 0.39 ms, a pipelined one 1.39 ms), so
@@ -281,8 +283,11 @@ class EPGroup:
             # (device-side epoch, so the call can be captured in a CUDA graph),
             # else the row-split one with its next host epoch
             ev, nev = (events, 5) if events is not None else (None, 0)
+            fl = flags
+            if self.prefill == "slice" and not self.uses_exchange(T):
+                fl |= _lib.PMOE_F_ROUTE_SLICE
             _lib.check("pmoe_block_forward_comm", self.lib.pmoe_block_forward_comm(
-                self.comm, x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, flags, y.data_ptr(),
+                self.comm, x.data_ptr(), T, H, self.E, self.K, I, Is, *wp, fl, y.data_ptr(),
                 ws.data_ptr(), nbytes, st, ev, nev))
             self._status_enqueue(st)
             return y

@@ -32,17 +32,20 @@ def main():
     a2a = ep.EPGroup(S.E, S.H, S.K, mode="a2a")
     partial = ep.EPGroup(S.E, S.H, S.K, mode="fused")
     partial.prefill = "partial"
+    sliced = ep.EPGroup(S.E, S.H, S.K, mode="fused")
+    sliced.prefill = "slice"   # routing by token slice, exchanged over NVLink
     ok = True
     for T in (1, 5, 64, 64, 64, 200, 1024, 1024, 200):
         x = W.make_hidden(T, S, seed=100 + T, device=dev)
         ref = ops.moe_block(x, *tensors, S.K, 0, S.E, 3).float().cpu().numpy()
-        for name, g in (("fused", fused), ("partial", partial), ("nccl", nccl), ("a2a", a2a)):
-            if name == "partial" and g.uses_exchange(T):
+        for name, g in (("fused", fused), ("slice", sliced), ("partial", partial), ("nccl", nccl),
+                        ("a2a", a2a)):
+            if name in ("partial", "slice") and g.uses_exchange(T):
                 continue
             y = g.forward(x, tensors).float().cpu().numpy()
             r, m = O.rel_l2(y, ref), O.max_abs(y, ref)
             good = r <= 5e-3 and m <= 3e-2
-            if name == "fused" and not g.uses_exchange(T):
+            if name in ("fused", "slice") and not g.uses_exchange(T):
                 # rows stored at their token owner, combined in the one-GPU
                 # order: the same bits as the single-GPU op
                 good &= bool((y == ref).all())
@@ -102,6 +105,7 @@ def main():
           f"{'ok' if good else 'FAIL'}", flush=True)
     fused.close()
     partial.close()
+    sliced.close()
     dist.barrier()
     print(f"rank{rank} EP_{'OK' if ok else 'FAIL'}", flush=True)
     dist.destroy_process_group()

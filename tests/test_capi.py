@@ -87,7 +87,8 @@ def test_rows_fused_buffer_layout(lib):
     assert lib.pmoe_rows_buffer_bytes(T, H, ctypes.byref(a)) == 0
     assert lib.pmoe_rows_fused_buffer_bytes(T, H, K, ctypes.byref(b)) == 0
     assert a.value == 1024 + 2 * r256(T * H * 2)
-    assert b.value == a.value + 2 * r256(T * (K + 1) * H * 2)
+    # + two parity regions of rows, + two of routing slices (idx, w: K each; the gate)
+    assert b.value == a.value + 2 * r256(T * (K + 1) * H * 2) + 2 * r256(T * (2 * K + 1) * 4)
     assert lib.pmoe_rows_fused_buffer_bytes(T, H, 0, ctypes.byref(b)) == -1
     assert lib.pmoe_rows_fused_buffer_bytes(T, 2047, K, ctypes.byref(b)) == -1
     assert lib.pmoe_rows_fused_buffer_bytes(0, H, K, ctypes.byref(b)) == -1
@@ -169,3 +170,11 @@ def test_torch_ops_registered_with_the_boundary_schema():
     c = torch.zeros(T, H, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         ops.rmsnorm(c, torch.zeros(H, dtype=torch.bfloat16), 1e-6)
+
+
+def test_route_slice_flag_only_with_the_row_exchange(lib):
+    """PMOE_F_ROUTE_SLICE is refused (before any pointer or device use) by the
+    entry points without the fused row exchange."""
+    ws = [None] * 7
+    assert lib.pmoe_block_forward(None, 64, 2048, 256, 8, 512, 512, *ws, 0, 256, 3 | 16,
+                                  None, None, 0, None) == -1

@@ -233,12 +233,13 @@ def test_rows_fused_missing_peer_raises_through_epgroup():
         g.close()
 
 
-@pytest.mark.parametrize("T", [200, 1000])
-def test_rows_fused_single_rank_matches_block(T):
+@pytest.mark.parametrize("T,slices", [(200, False), (1000, False), (200, True), (1000, True)])
+def test_rows_fused_single_rank_matches_block(T, slices):
     """The fused row exchange with world = 1 runs all of its kernels on one GPU
     (down-GEMM stores to the owner's buffer, both flag rounds, the slice
-    combine's push, the final copy): y equals pmoe_block_forward bit for bit,
-    for two calls (both buffer parities)."""
+    combine's push, the final copy; with routing slices also the routing push,
+    its flag round and the dispatch from the exchanged routing): y equals
+    pmoe_block_forward bit for bit, for two calls (both buffer parities)."""
     from paris_moe_b200 import _lib, ops, workload as W
     lib = _lib.load()
     S = W.MoEShape()
@@ -256,7 +257,8 @@ def test_rows_fused_single_rank_matches_block(T):
         y = torch.empty_like(x)
         assert lib.pmoe_block_forward_rows_fused(
             x.data_ptr(), T, S.H, S.E, S.K, S.I, S.Is, *[t.data_ptr() for t in wts.tensors()],
-            0, 1, arr, T, epoch, 3, y.data_ptr(), ws.data_ptr(), n, st, None, 0) == 0
+            0, 1, arr, T, epoch, 3 | (_lib.PMOE_F_ROUTE_SLICE if slices else 0), y.data_ptr(),
+            ws.data_ptr(), n, st, None, 0) == 0
         torch.cuda.synchronize()
         assert torch.equal(y, ref)
     status = ctypes.c_int(-1)
